@@ -1,0 +1,533 @@
+"""Benchmark of the B200 small-q paged attention path (one JSON line on rank 0).
+
+Workload (one "step" = one operator call over one batch): BASELINE config 2,
+B=4 sequences x q_len=4 draft tokens x kv_len=8192, fp16, 32 query / 8 KV
+heads, head_dim 128, page 16, random pages from a pool of 1.5x the needed
+pages.  With N GPUs every rank runs its own batch of 4 (batch sharding,
+weak scaling: global batch 4N, no collective on the hot path).
+
+Reported:
+* ``value``      effective HBM TB/s of the whole job = algorithmic bytes of all
+                 ranks' calls / max-over-ranks device time of K steps, inputs
+                 resident in HBM, the K calls replayed from one CUDA graph, each
+                 step on the next of 4 input replicas (805 MB > the 126 MB L2,
+                 so K/V always come from HBM);
+* ``e2e``        the same metric through the public Python API with the step's
+                 query, page table and lengths copied from pinned host memory
+                 and the output copied back every step (the KV cache is the
+                 serving state and stays resident);
+* ``roofline``   the split-KV kernel alone: algorithmic bytes / its mean
+                 CUDA-event duration, against the measured HBM copy bandwidth;
+* ``cpu_baseline`` the CPU oracle (numpy restatement of the upstream reference)
+                 on the host cores, on a bounded sample of the same workload.
+
+``--impl reference`` times the upstream algorithm on the CPU (the oracle port:
+the upstream reference is a Python/torch CPU function that does not travel to
+the GPU box) on the same workload; rank 0 only.
+
+``--matrix PATH`` instead writes one JSONL row per case of the 36-case matrix
+and the five named configurations (µs/call p50, TB/s, fraction of peak).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "us/call and HBM TB/s (% of peak) over the 36-case matrix; 1/2/4/8 B200"
+FALLBACK_HBM_GBS = 6650.0
+WORKLOAD = "cfg2"
+REPLICAS = 4
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def _traffic(workload: str):
+    """DRAM bytes per split-KV launch from the committed ncu summary, if any."""
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    return json.loads(p.read_text()).get(workload)
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML in a background thread."""
+
+    REASONS = {
+        "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4, "hw_slowdown": 0x8,
+        "sync_boost": 0x10, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+        "hw_power_brake_slowdown": 0x80, "display_clock_setting": 0x100,
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.002):
+        self.samples, self.reasons = [], 0
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self.period = period_s
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            uuid = None
+            try:
+                import torch
+
+                uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            except Exception:
+                pass
+            handle = None
+            if uuid:
+                for i in range(pynvml.nvmlDeviceGetCount()):
+                    h = pynvml.nvmlDeviceGetHandleByIndex(i)
+                    u = pynvml.nvmlDeviceGetUUID(h)
+                    u = u.decode() if isinstance(u, bytes) else u
+                    if u.replace("GPU-", "") == uuid.replace("GPU-", ""):
+                        handle = h
+                        break
+            self._h = handle or pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nv = None
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self._nv is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread:
+            self._thread.join()
+
+    def summary(self):
+        names = sorted(k for k, v in self.REASONS.items() if self.reasons & v)
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": names, "samples": len(self.samples),
+                "source": "nvml" if self._nv else "unavailable"}
+
+
+# ------------------------------------------------------------------ helpers
+def _dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def _init_pg(world, backend):
+    import datetime
+
+    import torch.distributed as dist
+
+    if world > 1 and not dist.is_initialized():
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+    return dist if world > 1 else None
+
+
+def _max_over_ranks(x: float, dist, device) -> float:
+    if dist is None:
+        return x
+    import torch
+
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _case_bytes(c):
+    from small_q_attention_b200.workloads import algorithmic_bytes
+
+    q = c["query"]
+    return algorithmic_bytes(q.shape[0], q.shape[1], c["lens"], q.shape[2], c["num_kv_heads"])
+
+
+def _cpu_cores():
+    try:
+        from threadpoolctl import threadpool_info
+
+        return max((i.get("num_threads") or 1) for i in threadpool_info()) if threadpool_info() else os.cpu_count()
+    except Exception:
+        return os.cpu_count()
+
+
+def _cpu_model():
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return "unknown"
+
+
+def time_oracle(c, budget_s: float, max_calls: int = 50):
+    """Time whole oracle calls on the host until ~budget_s has passed."""
+    from oracle import paged_mtp_attention_reference
+
+    host = {k: (v.cpu() if hasattr(v, "cpu") else v) for k, v in c.items()}
+    args = (host["query"], host["key_cache"], host["value_cache"], host["block_tables"], host["seq_lens"],
+            host["page_size"], host["num_kv_heads"])
+    paged_mtp_attention_reference(*args)  # warm the BLAS pool
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while len(times) < max_calls and (not times or time.perf_counter() < t_end):
+        t0 = time.perf_counter()
+        paged_mtp_attention_reference(*args)
+        times.append(time.perf_counter() - t0)
+    return times
+
+
+# ------------------------------------------------------------------ arms
+def run_ours(args):
+    import torch
+
+    import small_q_attention_b200 as sqa
+    from small_q_attention_b200 import _native
+    from small_q_attention_b200.attention import _fill_args
+    from small_q_attention_b200.workloads import CONFIGS, make_config
+
+    world, rank, local = _dist()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    dist = _init_pg(world, "nccl")
+    lib = _native.library()
+    peak_gbs, peak_src = _peaks()
+
+    # --- inputs: REPLICAS independent copies of this rank's batch
+    reps = [make_config(WORKLOAD, seed=1000 * rank + r, device=device) for r in range(REPLICAS)]
+    bytes_per_call = _case_bytes(reps[0])
+    cfg = CONFIGS[WORKLOAD]
+    outs = [torch.empty_like(r["query"]) for r in reps]
+    ws_bytes = sqa.workspace_bytes(reps[0]["query"], reps[0]["key_cache"], reps[0]["value_cache"],
+                                   reps[0]["block_tables"], reps[0]["seq_lens"], 16, cfg["kv_len"])
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=device)
+    cargs = []
+    for r, o in zip(reps, outs):
+        a = _fill_args(r["query"], r["key_cache"], r["value_cache"], r["block_tables"], r["seq_lens"], None,
+                       cfg["kv_len"], 0, 0)
+        a.out = o.data_ptr()
+        cargs.append(a)
+    import ctypes
+
+    def call(i, stream, ev0=None, ev1=None):
+        a = cargs[i % REPLICAS]
+        if ev0 is None:
+            code = lib.sqa_forward(ctypes.byref(a), ctypes.c_void_p(ws.data_ptr()), ctypes.c_size_t(ws_bytes),
+                                   ctypes.c_void_p(stream))
+        else:
+            code = lib.sqa_forward_timed(ctypes.byref(a), ctypes.c_void_p(ws.data_ptr()),
+                                         ctypes.c_size_t(ws_bytes), ctypes.c_void_p(stream),
+                                         ctypes.c_void_p(ev0), ctypes.c_void_p(ev1))
+        _native.check(code, "sqa_forward")
+
+    stream = torch.cuda.Stream(device)
+    sh = stream.cuda_stream
+    K, W = args.steps, args.warmup
+
+    # --- warm-up (eager), then capture exactly K steps in one graph
+    with torch.cuda.stream(stream):
+        for i in range(W):
+            call(i, sh)
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(K):
+            call(i, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    for _ in range(max(1, W // K + 1)):  # warm the graph itself
+        graph.replay()
+    torch.cuda.synchronize()
+
+    # --- timed region: K steps, barrier + synchronize on both sides
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+        start.record(stream)
+        with torch.cuda.stream(stream):
+            graph.replay()
+        end.record(stream)
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+    t_ms = _max_over_ranks(start.elapsed_time(end), dist, device)
+    value_tbs = world * K * bytes_per_call / (t_ms * 1e-3) / 1e12
+    del graph
+
+    # --- roofline: the split-KV kernel alone, one event pair per launch
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    for e0, e1 in evs:  # create the underlying CUDA events
+        e0.record(stream)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for i, (e0, e1) in enumerate(evs):
+            call(i, sh, e0.cuda_event, e1.cuda_event)
+    torch.cuda.synchronize()
+    kern_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs)
+    achieved_gbs = bytes_per_call / (kern_ms * 1e-3) / 1e9
+
+    # --- e2e through the public API with host buffers
+    host_in = [{k: r[k].cpu().pin_memory() for k in ("query", "block_tables", "seq_lens")} for r in reps]
+    dev_in = [{k: torch.empty_like(r[k]) for k in ("query", "block_tables", "seq_lens")} for r in reps]
+    host_out = [torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in outs]
+    h2d = sum(t.numel() * t.element_size() for t in host_in[0].values())
+    d2h = host_out[0].numel() * host_out[0].element_size()
+
+    def e2e_step(i):
+        j = i % REPLICAS
+        for k in ("query", "block_tables", "seq_lens"):
+            dev_in[j][k].copy_(host_in[j][k], non_blocking=True)
+        o = sqa.small_q_attention(dev_in[j]["query"], reps[j]["key_cache"], reps[j]["value_cache"],
+                                  dev_in[j]["block_tables"], dev_in[j]["seq_lens"], 16, cfg["kv_len"],
+                                  out=outs[j], workspace=ws)
+        host_out[j].copy_(o, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for i in range(W):
+            e2e_step(i)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for i in range(K):
+            e2e_step(i)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = _max_over_ranks(e0.elapsed_time(e1), dist, device)
+    e2e_tbs = world * K * bytes_per_call / (e2e_ms * 1e-3) / 1e12
+
+    # --- CPU baseline: the oracle on a bounded sample (rank 0, N=1 only)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        times = time_oracle(reps[0], args.cpu_seconds)
+        t = statistics.median(times)
+        cpu = {"value": bytes_per_call / t / 1e12, "unit": "TB/s", "cores": _cpu_cores(), "kind": "port",
+               "sample": f"{len(times)} whole {WORKLOAD} calls (B=4,q=4,kv=8192) of the numpy oracle, "
+                         f"median {t * 1e3:.1f} ms/call, {_cpu_model()}"}
+
+    if dist is not None:
+        dist.barrier()
+    if rank == 0:
+        traffic = _traffic(WORKLOAD)
+        line = {
+            "metric": METRIC, "value": round(value_tbs, 4), "unit": "TB/s", "n_gpus": world, "steps": K,
+            "warmup": W, "ms_per_step": round(t_ms / K, 6), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16 in, f32 accumulate", "data": "synthetic (seeded N(0,1) fp16)",
+            "config": {"workload": f"{WORKLOAD}: B={cfg['batch']} per GPU, q_len={cfg['q_len']}, "
+                                   f"kv_len={cfg['kv_len']}, Hq/Hkv=32/8, d=128, page 16, random pages, "
+                                   f"pool 1.5x",
+                       "global_batch": cfg["batch"] * world, "seq_len": cfg["kv_len"], "q_len": cfg["q_len"],
+                       "parallelism": f"batch-shard x{world}",
+                       "l2": f"inputs rotated over {REPLICAS} replicas "
+                             f"({REPLICAS * reps[0]['key_cache'].numel() * 4 / 1e6:.0f} MB > 126 MB L2)",
+                       "us_per_call": round(t_ms / K * 1e3, 3),
+                       "algorithmic_bytes_per_call": bytes_per_call},
+            "roofline": {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": peak_gbs, "unit": "GB/s",
+                         "frac": round(achieved_gbs / peak_gbs, 4), "peak_source": f"{peak_src} hbm_gbs (burst)",
+                         "traffic": traffic, "kernel": "sqa_split_kv_kernel",
+                         "kernel_us": round(kern_ms * 1e3, 3)},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_tbs, 4), "unit": "TB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "us_per_step": round(e2e_ms / K * 1e3, 3)},
+            "clocks": clocks.summary(),
+            "gpu_launches": 2 * K,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+def _oracle_sample(c, level):
+    """The workload restricted to a bounded sample: level 0 = the whole batch,
+    1 = one sequence (all 8 KV heads), 2 = one sequence and one KV head."""
+    if level == 0:
+        return c
+    d = dict(c)
+    d["query"], d["block_tables"], d["seq_lens"] = c["query"][:1], c["block_tables"][:1], c["seq_lens"][:1]
+    d["lens"] = c["lens"][:1]
+    if level == 2:
+        d["query"] = d["query"][:, :, :4].contiguous()
+        d["key_cache"] = c["key_cache"][:, :, :1]
+        d["value_cache"] = c["value_cache"][:, :, :1]
+        d["num_kv_heads"] = 1
+    return d
+
+
+def run_reference(args):
+    world, rank, _ = _dist()
+    if rank != 0:
+        return
+    import torch
+
+    from oracle import paged_mtp_attention_reference
+    from small_q_attention_b200.workloads import CONFIGS, algorithmic_bytes, make_config
+
+    c = make_config(WORKLOAD, seed=0, device="cpu", gen_device="cpu")
+    cfg = CONFIGS[WORKLOAD]
+
+    def one(d):
+        paged_mtp_attention_reference(d["query"], d["key_cache"], d["value_cache"], d["block_tables"],
+                                      d["seq_lens"], 16, d["num_kv_heads"])
+
+    # pick the largest sample whose K + W steps fit the time budget
+    level, d = 0, c
+    for level in range(3):
+        d = _oracle_sample(c, level)
+        one(d)
+        t0 = time.perf_counter()
+        one(d)
+        est = (time.perf_counter() - t0) * (args.steps + args.warmup)
+        if est <= args.reference_budget_s:
+            break
+    q = d["query"]
+    nbytes = algorithmic_bytes(q.shape[0], q.shape[1], d["lens"], q.shape[2], d["num_kv_heads"])
+    for _ in range(args.warmup):
+        one(d)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        one(d)
+    dt = time.perf_counter() - t0
+    v = args.steps * nbytes / dt / 1e12
+    cores = _cpu_cores()
+    sample = ["whole call (B=4, 8 KV heads)", "one sequence of the batch (8 KV heads)",
+              "one sequence, one KV head"][level]
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "TB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (CPU oracle)",
+        "data": "synthetic (seeded N(0,1) fp16, upcast to fp32)",
+        "config": {"workload": f"{WORKLOAD}: B={cfg['batch']}, q_len={cfg['q_len']}, kv_len={cfg['kv_len']}",
+                   "global_batch": cfg["batch"], "seq_len": cfg["kv_len"], "parallelism": "cpu, rank 0 only"},
+        "cpu_baseline": {"value": v, "unit": "TB/s", "cores": cores, "kind": "port",
+                         "sample": f"each step = {sample} of {WORKLOAD}, numpy restatement of "
+                                   f"reference.py:10-74 ({_cpu_model()}, torch {torch.__version__})"},
+        "e2e": {"value": v, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_matrix(args):
+    """Per-case p50 µs/call and TB/s over the 36-case matrix and the named configs."""
+    import torch
+
+    import small_q_attention_b200 as sqa
+    from small_q_attention_b200.workloads import CONFIGS, make_case, make_config, matrix_cases
+
+    torch.cuda.set_device(0)
+    peak_gbs, peak_src = _peaks()
+    rows = []
+    cases = [("matrix", c) for c in matrix_cases()] + [(n, None) for n in CONFIGS]
+    if args.only:
+        cases = [(n, c) for n, c in cases if n in args.only or (c and f"q{c['q_len']}" in args.only)]
+    for name, c in cases:
+        if c is None:
+            inst = [make_config(name, seed=s) for s in range(2)]
+            label = name
+        else:
+            inst = [make_case(c["batch"], c["q_len"], [c["kv_len"]] * c["batch"], pool_factor=1.0,
+                              page_mode=args.page_mode, seed=s) for s in range(2)]
+            label = f"q{c['q_len']}_kv{c['kv_len']}_b{c['batch']}"
+        nb = _case_bytes(inst[0])
+        # enough distinct replicas that consecutive calls do not hit in L2
+        n_rep = max(2, min(8, math.ceil(400e6 / max(1, inst[0]["key_cache"].numel() * 4))))
+        while len(inst) < n_rep:
+            inst.append(inst[len(inst) % 2])
+        outs = [torch.empty_like(x["query"]) for x in inst]
+        fn = lambda i: sqa.small_q_attention(  # noqa: E731
+            inst[i]["query"], inst[i]["key_cache"], inst[i]["value_cache"], inst[i]["block_tables"],
+            inst[i]["seq_lens"], 16, max(inst[i]["lens"]), out=outs[i])
+        for i in range(5):
+            fn(i % len(inst))
+        torch.cuda.synchronize()
+        s = torch.cuda.Stream()
+        g = torch.cuda.CUDAGraph()
+        reps = 20
+        with torch.cuda.graph(g, stream=s):
+            for i in range(reps):
+                fn(i % len(inst))
+        g.replay()
+        torch.cuda.synchronize()
+        samples = []
+        for _ in range(5):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            g.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            samples.append(e0.elapsed_time(e1) * 1e3 / reps)
+        us = statistics.median(samples)
+        row = {"case": label, "q_len": inst[0]["query"].shape[1], "batch": inst[0]["query"].shape[0],
+               "kv_len_max": max(inst[0]["lens"]), "page_mode": args.page_mode if c else "random",
+               "p50_us": round(us, 3), "min_us": round(min(samples), 3), "alg_bytes": nb,
+               "tb_s": round(nb / (us * 1e-6) / 1e12, 4),
+               "roofline_frac": round(nb / (us * 1e-6) / 1e9 / peak_gbs, 4), "peak_gbs": peak_gbs,
+               "peak_source": peak_src, "n_gpus": 1, "timing": "CUDA graph of 20 calls, median of 5"}
+        rows.append(row)
+        print(json.dumps(row), flush=True)
+        del g, inst, outs
+        torch.cuda.empty_cache()
+    if args.matrix:
+        Path(args.matrix).parent.mkdir(parents=True, exist_ok=True)
+        Path(args.matrix).write_text("".join(json.dumps(r) + "\n" for r in rows))
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--reference-budget-s", type=float, default=150.0)
+    ap.add_argument("--matrix", type=str, default=None, help="write the per-case matrix JSONL here")
+    ap.add_argument("--matrix-only", action="store_true", help="run only the matrix sweep")
+    ap.add_argument("--only", nargs="*", default=None)
+    ap.add_argument("--page-mode", default="random", choices=("random", "unique", "shared"))
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    elif args.matrix_only or args.matrix:
+        run_matrix(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

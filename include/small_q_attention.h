@@ -1,0 +1,156 @@
+/*
+ * small_q_attention.h -- C ABI of the B200 (sm_100a) small-q paged attention path.
+ *
+ * Operator: causal paged multi-token-prediction (MTP / speculative-decoding)
+ * attention with a uniform draft length q_len.  For batch element b, draft row
+ * qi and query head qh:
+ *
+ *   kvh   = qh / (Hq / Hkv)
+ *   valid = seq_lens[b] - q_len + qi + 1           (tokens 0 .. valid-1 visible)
+ *   out[b,qi,qh,:] = softmax(K[b,:valid,kvh] . q[b,qi,qh] / sqrt(128)) V[b,:valid,kvh]
+ *
+ * where token t of sequence b lives in page block_tables[b, t / 16], slot t % 16.
+ * This is the contract of the upstream paged_mtp_attention_reference
+ * (src/small_q_attention/reference.py:10-74) and of its CUDA entry points
+ * (src/small_q_attention/cuda.py:177-214 -> csrc/small_q_attention_ext.cu:1132-1210).
+ *
+ * Layout (all row-major, contiguous):
+ *   query        fp16  [batch, q_len, num_q_heads, 128]
+ *   key_cache    fp16  [num_pages, 16, num_kv_heads, 128]
+ *   value_cache  fp16  [num_pages, 16, num_kv_heads, 128]
+ *   block_tables int32 [batch, max_pages]   (row stride max_pages)
+ *   seq_lens     int32 [batch]              (total length incl. the q_len drafts)
+ *   out          fp16  [batch, q_len, num_q_heads, 128]
+ * Supported: head_dim 128, page_size 16, num_q_heads == 4 * num_kv_heads,
+ * 1 <= q_len <= 16.  All pointers are device pointers; query/out/caches must
+ * be 16-byte aligned.
+ *
+ * Nothing here allocates device memory: the caller passes a workspace of at
+ * least sqa_workspace_bytes() bytes (fp32 split-KV partials, the per-segment
+ * merge table and a device status word).  Every entry point is asynchronous on
+ * the given stream and returns a status code; no C++ exception crosses the ABI.
+ */
+#ifndef SMALL_Q_ATTENTION_H_
+#define SMALL_Q_ATTENTION_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SQA_API __attribute__((visibility("default")))
+#else
+#define SQA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SQA_HEAD_DIM 128
+#define SQA_PAGE_SIZE 16
+#define SQA_GQA_GROUP 4
+#define SQA_MAX_Q_LEN 16
+
+/* Host-side status codes returned by the entry points. */
+typedef enum sqa_status {
+  SQA_OK = 0,
+  SQA_ERR_INVALID_ARGUMENT = 1, /* null pointer, bad shape or misaligned pointer */
+  SQA_ERR_UNSUPPORTED = 2,      /* shape outside the supported contract        */
+  SQA_ERR_WORKSPACE_TOO_SMALL = 3,
+  SQA_ERR_CUDA = 4,             /* a CUDA runtime/driver call failed            */
+  SQA_ERR_DEVICE = 5            /* sqa_read_device_status found a device error  */
+} sqa_status;
+
+/* Bits of the device status word (sticky until cleared by sqa_read_device_status). */
+#define SQA_DEV_TIMEOUT 1u         /* a bounded wait gave up; output is not valid       */
+#define SQA_DEV_SEQ_TOO_LONG 2u    /* seq_lens[b] > 16 * max_pages: clamped to the table */
+#define SQA_DEV_SEQ_TOO_SHORT 4u   /* seq_lens[b] < q_len (full mode only)              */
+#define SQA_DEV_BAD_PAGE 8u        /* a page id outside [0, num_pages): read as page 0  */
+
+typedef struct sqa_args {
+  const void* query;           /* fp16 [batch, q_len, num_q_heads, 128]           */
+  const void* key_cache;       /* fp16 [num_pages, 16, num_kv_heads, 128]         */
+  const void* value_cache;     /* fp16 [num_pages, 16, num_kv_heads, 128]         */
+  const int32_t* block_tables; /* int32 [batch, max_pages]                        */
+  const int32_t* seq_lens;     /* int32 [batch]: tokens held for each sequence     */
+  /* Optional int32 [batch], NULL = seq_lens.  The causal length used for the
+   * spec-dec mask: row qi sees token t iff t < seq_lens[b] and
+   * t < mask_lens[b] - q_len + qi + 1.  A shard that holds tokens
+   * [offset, offset + seq_lens[b]) of a longer sequence passes
+   * mask_lens[b] = whole_length - offset. */
+  const int32_t* mask_lens;
+  /* Full mode: out != NULL, fp16 [batch, q_len, num_q_heads, 128].
+   * Partial mode: out == NULL and out_partial/out_lse != NULL: the normalised
+   * fp32 output [batch, q_len, num_q_heads, 128] and its natural-log
+   * log-sum-exp [batch, q_len, num_q_heads] (-inf for a row that sees no key),
+   * ready for sqa_merge_partials. */
+  void* out;
+  float* out_partial;
+  float* out_lse;
+  int32_t batch;
+  int32_t q_len;
+  int32_t num_q_heads;
+  int32_t num_kv_heads;
+  int32_t head_dim;            /* must be 128 */
+  int32_t page_size;           /* must be 16  */
+  int32_t num_pages;           /* pages in the cache pool                          */
+  int32_t max_pages;           /* block_tables row stride                          */
+  /* Upper bound of seq_lens (0 = unknown: 16 * max_pages is used).  Only sizes
+   * the launch; never read on the device, so no host synchronisation. */
+  int32_t max_seq_len;
+  /* Tuning: CTAs of the split-KV kernel (0 = auto: 2 per SM, fewer for short
+   * work) and the minimum pages one CTA takes (0 = auto). */
+  int32_t num_ctas;
+  int32_t min_pages_per_cta;
+} sqa_args;
+
+/* Workspace bytes sqa_forward needs for these arguments on `device`
+ * (-1 = the current device).  Depends only on shapes and tuning fields.
+ * Returns 0 and sets *status on invalid arguments. */
+SQA_API size_t sqa_workspace_bytes(const sqa_args* args, int device, int* status);
+
+/* Run the operator on `stream` (a cudaStream_t; NULL = legacy default stream).
+ * Replaces small_q_attention_v3(...) (csrc/small_q_attention_ext.cu:1132-1210),
+ * which the upstream binds as forward_v3 (:1384) and wraps in
+ * small_q_attention.cuda.forward_v3 (src/small_q_attention/cuda.py:177-214).
+ * Launches the split-KV partial kernel and, when a sequence was split over
+ * several CTAs, the log-sum-exp merge kernel.  No device allocation, no host
+ * synchronisation. */
+SQA_API int sqa_forward(const sqa_args* args, void* workspace, size_t workspace_bytes, void* stream);
+
+/* sqa_forward that also records the caller's CUDA events (cudaEvent_t, may be
+ * NULL) on `stream` immediately before and after the split-KV kernel launch,
+ * so the dominant kernel can be timed with events on its own stream.  Does
+ * the same work as sqa_forward.  No upstream counterpart (measurement hook). */
+SQA_API int sqa_forward_timed(const sqa_args* args, void* workspace, size_t workspace_bytes, void* stream,
+                              void* event_before, void* event_after);
+
+/* Merge num_parts partial results (e.g. one per GPU of a split sequence) into
+ * one.  parts_o: fp32 [num_parts, rows, 128]; parts_lse: fp32 [num_parts, rows]
+ * natural-log; rows = batch * q_len * num_q_heads.  Writes fp16 out[rows,128]
+ * when out != NULL, and/or fp32 out_o[rows,128] and out_lse[rows] when those
+ * are non-NULL.  Same arithmetic as the upstream split-KV merge
+ * (csrc/small_q_attention_ext.cu:339-366): a row whose parts all have
+ * lse = -inf gets 0. */
+SQA_API int sqa_merge_partials(const float* parts_o, const float* parts_lse, int32_t num_parts,
+                       int64_t rows, void* out, float* out_o, float* out_lse, void* stream);
+
+/* Read (and optionally clear) the sticky device status word in a workspace
+ * used by sqa_forward.  Synchronises `stream`.  *device_bits receives the
+ * SQA_DEV_* bits; returns SQA_ERR_DEVICE when any bit is set. */
+SQA_API int sqa_read_device_status(void* workspace, uint32_t* device_bits, int clear, void* stream);
+
+/* Zero a freshly allocated workspace's status word (asynchronous). */
+SQA_API int sqa_workspace_init(void* workspace, size_t workspace_bytes, void* stream);
+
+/* Static description of a status code. */
+SQA_API const char* sqa_status_string(int status);
+
+/* Version of this ABI (major * 100 + minor). */
+SQA_API int sqa_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SMALL_Q_ATTENTION_H_ */

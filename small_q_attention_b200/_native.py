@@ -1,0 +1,119 @@
+"""ctypes binding of the C ABI in ``include/small_q_attention.h``.
+
+The shared library is the only compute path: if it is missing or fails to
+load, every operator raises ``RuntimeError``; there is no CPU fallback.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libsqa_b200.so"
+
+# status codes (sqa_status)
+SQA_OK = 0
+SQA_ERR_INVALID_ARGUMENT = 1
+SQA_ERR_UNSUPPORTED = 2
+SQA_ERR_WORKSPACE_TOO_SMALL = 3
+SQA_ERR_CUDA = 4
+SQA_ERR_DEVICE = 5
+
+# device status bits (SQA_DEV_*)
+DEV_TIMEOUT = 1
+DEV_SEQ_TOO_LONG = 2
+DEV_SEQ_TOO_SHORT = 4
+DEV_BAD_PAGE = 8
+
+EXPORTED_SYMBOLS = (
+    "sqa_workspace_bytes",
+    "sqa_forward",
+    "sqa_forward_timed",
+    "sqa_merge_partials",
+    "sqa_read_device_status",
+    "sqa_workspace_init",
+    "sqa_status_string",
+    "sqa_abi_version",
+)
+
+
+class SqaArgs(ctypes.Structure):
+    """Mirror of ``struct sqa_args``."""
+
+    _fields_ = [
+        ("query", ctypes.c_void_p),
+        ("key_cache", ctypes.c_void_p),
+        ("value_cache", ctypes.c_void_p),
+        ("block_tables", ctypes.c_void_p),
+        ("seq_lens", ctypes.c_void_p),
+        ("mask_lens", ctypes.c_void_p),
+        ("out", ctypes.c_void_p),
+        ("out_partial", ctypes.c_void_p),
+        ("out_lse", ctypes.c_void_p),
+        ("batch", ctypes.c_int32),
+        ("q_len", ctypes.c_int32),
+        ("num_q_heads", ctypes.c_int32),
+        ("num_kv_heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("page_size", ctypes.c_int32),
+        ("num_pages", ctypes.c_int32),
+        ("max_pages", ctypes.c_int32),
+        ("max_seq_len", ctypes.c_int32),
+        ("num_ctas", ctypes.c_int32),
+        ("min_pages_per_cta", ctypes.c_int32),
+    ]
+
+
+_lib = None
+_lock = threading.Lock()
+
+
+def library(path: Path | None = None):
+    """Load (once) and return the native library; raise if it is unavailable."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    with _lock:
+        if _lib is not None and path is None:
+            return _lib
+        p = Path(path) if path is not None else LIB_PATH
+        if not p.exists():
+            raise RuntimeError(
+                f"native library {p} is missing; build it with "
+                "`python -m small_q_attention_b200.build` (nvcc, sm_100a)")
+        lib = ctypes.CDLL(str(p))
+        vp, i32, i64, sz = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_size_t
+        lib.sqa_workspace_bytes.argtypes = [ctypes.POINTER(SqaArgs), ctypes.c_int, ctypes.POINTER(ctypes.c_int)]
+        lib.sqa_workspace_bytes.restype = sz
+        lib.sqa_forward.argtypes = [ctypes.POINTER(SqaArgs), vp, sz, vp]
+        lib.sqa_forward.restype = ctypes.c_int
+        lib.sqa_forward_timed.argtypes = [ctypes.POINTER(SqaArgs), vp, sz, vp, vp, vp]
+        lib.sqa_forward_timed.restype = ctypes.c_int
+        lib.sqa_merge_partials.argtypes = [vp, vp, i32, i64, vp, vp, vp, vp]
+        lib.sqa_merge_partials.restype = ctypes.c_int
+        lib.sqa_read_device_status.argtypes = [vp, ctypes.POINTER(ctypes.c_uint32), ctypes.c_int, vp]
+        lib.sqa_read_device_status.restype = ctypes.c_int
+        lib.sqa_workspace_init.argtypes = [vp, sz, vp]
+        lib.sqa_workspace_init.restype = ctypes.c_int
+        lib.sqa_status_string.argtypes = [ctypes.c_int]
+        lib.sqa_status_string.restype = ctypes.c_char_p
+        lib.sqa_abi_version.argtypes = []
+        lib.sqa_abi_version.restype = ctypes.c_int
+        if path is None:
+            _lib = lib
+        return lib
+
+
+def status_string(code: int) -> str:
+    return library().sqa_status_string(int(code)).decode()
+
+
+def check(code: int, what: str) -> None:
+    """Map a C status code to the Python exception the upstream would raise."""
+    if code == SQA_OK:
+        return
+    msg = f"{what}: {status_string(code)} (status {code})"
+    if code in (SQA_ERR_INVALID_ARGUMENT, SQA_ERR_UNSUPPORTED):
+        raise ValueError(msg)
+    raise RuntimeError(msg)

@@ -1,0 +1,249 @@
+"""Public operator: causal paged MTP attention on B200 through the C ABI.
+
+``small_q_attention(query, key_cache, value_cache, block_tables, seq_lens,
+page_size, max_seq_len=0)`` keeps the positional contract of the upstream
+``small_q_attention.cuda.forward_v3`` (``src/small_q_attention/cuda.py:177-214``)
+and its error behaviour: ``RuntimeError`` without CUDA, ``ValueError`` for a
+tensor that is not on CUDA, not contiguous, of the wrong dtype or outside the
+shape contract (``cuda.py:197-211``).  It launches on the current torch
+stream (the upstream launches on the legacy default stream,
+``csrc/small_q_attention_ext.cu:1187``), never synchronises the host, and
+reuses one workspace per (device, stream) instead of allocating fp32 scratch
+on every call (``ext.cu:1183-1185``).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+
+import torch
+
+from . import _native
+
+HEAD_DIM = 128
+PAGE_SIZE = 16
+GQA_GROUP = 4
+MAX_Q_LEN = 16
+
+_ws_lock = threading.Lock()
+_workspaces: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def _stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _check_inputs(query, key_cache, value_cache, block_tables, seq_lens, page_size, mask_lens=None):
+    if not torch.cuda.is_available():
+        raise RuntimeError("CUDA is required for the small-q attention kernel")
+    tensors = [query, key_cache, value_cache, block_tables, seq_lens]
+    if mask_lens is not None:
+        tensors.append(mask_lens)
+    if any(not isinstance(t, torch.Tensor) or not t.is_cuda for t in tensors):
+        raise ValueError("all inputs must be CUDA tensors")
+    if any(t.device != query.device for t in tensors):
+        raise ValueError("all inputs must be on the same CUDA device")
+    if any(not t.is_contiguous() for t in tensors):
+        raise ValueError("all inputs must be contiguous")
+    if query.dtype != torch.float16 or key_cache.dtype != torch.float16 or value_cache.dtype != torch.float16:
+        raise ValueError("the kernel requires FP16 Q/K/V")
+    if any(t.dtype != torch.int32 for t in tensors[3:]):
+        raise ValueError("block_tables, seq_lens and mask_lens must be int32")
+    if query.dim() != 4 or key_cache.dim() != 4:
+        raise ValueError("query and key_cache must be 4-D")
+    if value_cache.shape != key_cache.shape:
+        raise ValueError("value_cache shape mismatch")
+    batch, q_len, hq, head_dim = query.shape
+    _, cache_page, hkv, cache_dim = key_cache.shape
+    if not (1 <= q_len <= MAX_Q_LEN):
+        raise ValueError(f"q_len must be in [1, {MAX_Q_LEN}]")
+    if head_dim != HEAD_DIM or cache_dim != HEAD_DIM:
+        raise ValueError("the kernel supports head_dim 128")
+    if hq % hkv != 0 or hq // hkv != GQA_GROUP:
+        raise ValueError("the kernel requires a GQA group size of exactly 4 (Hq/Hkv = 32/8)")
+    if int(page_size) != cache_page or cache_page != PAGE_SIZE:
+        raise ValueError("page_size must be 16 and match key_cache.shape[1]")
+    if block_tables.dim() != 2 or block_tables.shape[0] != batch or seq_lens.numel() != batch:
+        raise ValueError("invalid metadata: block_tables must be [batch, max_pages], seq_lens [batch]")
+    if mask_lens is not None and mask_lens.numel() != batch:
+        raise ValueError("mask_lens must have one entry per sequence")
+    if key_cache.shape[0] == 0 or block_tables.shape[1] == 0:
+        raise ValueError("empty KV cache is not supported")
+
+
+def _fill_args(query, key_cache, value_cache, block_tables, seq_lens, mask_lens, max_seq_len,
+               num_ctas, min_pages_per_cta) -> _native.SqaArgs:
+    a = _native.SqaArgs()
+    a.query = query.data_ptr()
+    a.key_cache = key_cache.data_ptr()
+    a.value_cache = value_cache.data_ptr()
+    a.block_tables = block_tables.data_ptr()
+    a.seq_lens = seq_lens.data_ptr()
+    a.mask_lens = mask_lens.data_ptr() if mask_lens is not None else None
+    a.batch, a.q_len, a.num_q_heads, a.head_dim = (int(x) for x in query.shape)
+    a.num_pages, a.page_size, a.num_kv_heads = (int(x) for x in key_cache.shape[:3])
+    a.max_pages = int(block_tables.shape[1])
+    a.max_seq_len = int(max_seq_len)
+    a.num_ctas = int(num_ctas)
+    a.min_pages_per_cta = int(min_pages_per_cta)
+    return a
+
+
+def workspace_for(args: _native.SqaArgs, device: torch.device, workspace: torch.Tensor | None = None):
+    """Return (pointer, bytes) of a workspace large enough for ``args``.
+
+    With ``workspace=None`` one uint8 buffer per (device, stream) is kept and
+    grown on demand; its status word starts zeroed.
+    """
+    lib = _native.library()
+    st = ctypes.c_int(0)
+    need = lib.sqa_workspace_bytes(ctypes.byref(args), device.index, ctypes.byref(st))
+    _native.check(st.value, "sqa_workspace_bytes")
+    if workspace is not None:
+        if workspace.device != device or not workspace.is_contiguous():
+            raise ValueError("workspace must be a contiguous tensor on the query's device")
+        if workspace.numel() * workspace.element_size() < need:
+            raise ValueError(f"workspace too small: need {need} bytes")
+        return workspace.data_ptr(), workspace.numel() * workspace.element_size()
+    key = (device.index, _stream_handle(device))
+    with _ws_lock:
+        ws = _workspaces.get(key)
+        if ws is None or ws.numel() < need:
+            ws = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device=device)
+            _workspaces[key] = ws
+    return ws.data_ptr(), ws.numel()
+
+
+def workspace_bytes(query, key_cache, value_cache, block_tables, seq_lens, page_size,
+                    max_seq_len: int = 0, *, num_ctas: int = 0, min_pages_per_cta: int = 0) -> int:
+    """Bytes of workspace ``small_q_attention`` needs for these shapes."""
+    _check_inputs(query, key_cache, value_cache, block_tables, seq_lens, page_size)
+    args = _fill_args(query, key_cache, value_cache, block_tables, seq_lens, None, max_seq_len,
+                      num_ctas, min_pages_per_cta)
+    st = ctypes.c_int(0)
+    need = _native.library().sqa_workspace_bytes(ctypes.byref(args), query.device.index, ctypes.byref(st))
+    _native.check(st.value, "sqa_workspace_bytes")
+    return int(need)
+
+
+def read_device_status(workspace_ptr: int, clear: bool = True, device=None) -> int:
+    """Synchronise and return the sticky SQA_DEV_* bits of a workspace."""
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    bits = ctypes.c_uint32(0)
+    code = _native.library().sqa_read_device_status(
+        ctypes.c_void_p(workspace_ptr), ctypes.byref(bits), int(clear), ctypes.c_void_p(_stream_handle(dev)))
+    if code not in (_native.SQA_OK, _native.SQA_ERR_DEVICE):
+        _native.check(code, "sqa_read_device_status")
+    return int(bits.value)
+
+
+def _raise_device_bits(bits: int) -> None:
+    if bits & _native.DEV_SEQ_TOO_SHORT:
+        raise ValueError("seq_lens must be at least q_len for MTP attention")
+    if bits & _native.DEV_SEQ_TOO_LONG:
+        raise ValueError("seq_lens exceeds page_size * block_tables.shape[1]")
+    if bits & _native.DEV_BAD_PAGE:
+        raise IndexError("block_tables holds a page id outside the cache")
+    if bits & _native.DEV_TIMEOUT:
+        raise RuntimeError("a bounded device wait timed out; the output is not valid")
+
+
+def _run(args, device, workspace, check):
+    ws_ptr, ws_bytes = workspace_for(args, device, workspace)
+    stream = _stream_handle(device)
+    with torch.cuda.device(device):
+        code = _native.library().sqa_forward(ctypes.byref(args), ctypes.c_void_p(ws_ptr),
+                                            ctypes.c_size_t(ws_bytes), ctypes.c_void_p(stream))
+        _native.check(code, "sqa_forward")
+        if check:
+            _raise_device_bits(read_device_status(ws_ptr, clear=True, device=device))
+
+
+def small_q_attention(query, key_cache, value_cache, block_tables, seq_lens, page_size: int,
+                      max_seq_len: int = 0, *, out=None, workspace=None, num_ctas: int = 0,
+                      min_pages_per_cta: int = 0, check: bool = False):
+    """Causal paged MTP attention; returns fp16 ``[batch, q_len, Hq, 128]``.
+
+    ``seq_lens[b]`` is the KV length including the ``q_len`` draft tokens and
+    draft row ``qi`` sees tokens ``< seq_lens[b] - q_len + qi + 1``
+    (``src/small_q_attention/reference.py:63``).  ``max_seq_len`` is an
+    optional upper bound of ``seq_lens`` that only sizes the launch (0: use the
+    page-table width); unlike the upstream (``ext.cu:1173-1176``) it is never
+    measured with a device-to-host copy.  ``check=True`` synchronises and
+    raises the exception the upstream CPU reference would raise for bad
+    metadata (``seq_lens < q_len``, page ids outside the pool).
+    """
+    _check_inputs(query, key_cache, value_cache, block_tables, seq_lens, page_size)
+    if out is None:
+        out = torch.empty_like(query)
+    elif out.shape != query.shape or out.dtype != torch.float16 or not out.is_contiguous() or out.device != query.device:
+        raise ValueError("out must be a contiguous fp16 tensor shaped like query")
+    args = _fill_args(query, key_cache, value_cache, block_tables, seq_lens, None, max_seq_len,
+                      num_ctas, min_pages_per_cta)
+    args.out = out.data_ptr()
+    _run(args, query.device, workspace, check)
+    return out
+
+
+def small_q_attention_partial(query, key_cache, value_cache, block_tables, seq_lens, page_size: int,
+                              mask_lens=None, max_seq_len: int = 0, *, out=None, out_lse=None,
+                              workspace=None, num_ctas: int = 0, min_pages_per_cta: int = 0,
+                              check: bool = False):
+    """Attention over the tokens this call holds; returns ``(O fp32, LSE fp32)``.
+
+    The shard form of the operator for splitting one sequence's KV range:
+    the cache/page table hold tokens ``[offset, offset + seq_lens[b])`` of a
+    sequence whose whole length minus ``offset`` is ``mask_lens[b]`` (default
+    ``seq_lens``).  ``O`` is the normalised output ``[B, q_len, Hq, 128]`` and
+    ``LSE`` the natural-log log-sum-exp ``[B, q_len, Hq]`` (-inf for a row
+    that sees no key here).  Combine shards with :func:`merge_partials`.
+    """
+    _check_inputs(query, key_cache, value_cache, block_tables, seq_lens, page_size, mask_lens)
+    if out is None:
+        out = torch.empty(query.shape, dtype=torch.float32, device=query.device)
+    if out_lse is None:
+        out_lse = torch.empty(query.shape[:3], dtype=torch.float32, device=query.device)
+    if out.dtype != torch.float32 or out.shape != query.shape or not out.is_contiguous():
+        raise ValueError("out must be a contiguous fp32 tensor shaped like query")
+    if out_lse.dtype != torch.float32 or out_lse.shape != query.shape[:3] or not out_lse.is_contiguous():
+        raise ValueError("out_lse must be a contiguous fp32 tensor [batch, q_len, Hq]")
+    args = _fill_args(query, key_cache, value_cache, block_tables, seq_lens, mask_lens, max_seq_len,
+                      num_ctas, min_pages_per_cta)
+    args.out_partial = out.data_ptr()
+    args.out_lse = out_lse.data_ptr()
+    _run(args, query.device, workspace, check)
+    return out, out_lse
+
+
+def merge_partials(parts_o, parts_lse, *, out=None, out_dtype=torch.float16, return_lse: bool = False):
+    """Log-sum-exp merge of stacked partials ``[n, ..., 128]`` / ``[n, ...]``.
+
+    Returns the merged output in ``out_dtype`` (fp16 or fp32) and, with
+    ``return_lse``, the merged LSE.  Same arithmetic as the upstream split-KV
+    merge (``csrc/small_q_attention_ext.cu:339-366``).
+    """
+    if not (parts_o.is_cuda and parts_lse.is_cuda):
+        raise ValueError("partials must be CUDA tensors")
+    if parts_o.dtype != torch.float32 or parts_lse.dtype != torch.float32:
+        raise ValueError("partials must be fp32")
+    if not (parts_o.is_contiguous() and parts_lse.is_contiguous()):
+        raise ValueError("partials must be contiguous")
+    if parts_o.shape[-1] != HEAD_DIM or parts_o.shape[:-1] != parts_lse.shape:
+        raise ValueError("parts_o must be [n, ..., 128] and parts_lse [n, ...]")
+    n = int(parts_o.shape[0])
+    rows = parts_lse[0].numel() if n else 0
+    shape = parts_o.shape[1:]
+    if out is None:
+        out = torch.empty(shape, dtype=out_dtype, device=parts_o.device)
+    lse = torch.empty(parts_lse.shape[1:], dtype=torch.float32, device=parts_o.device) if return_lse else None
+    o16 = out.data_ptr() if out.dtype == torch.float16 else None
+    o32 = out.data_ptr() if out.dtype == torch.float32 else None
+    with torch.cuda.device(parts_o.device):
+        code = _native.library().sqa_merge_partials(
+            ctypes.c_void_p(parts_o.data_ptr()), ctypes.c_void_p(parts_lse.data_ptr()), n, rows,
+            ctypes.c_void_p(o16), ctypes.c_void_p(o32),
+            ctypes.c_void_p(lse.data_ptr() if lse is not None else None),
+            ctypes.c_void_p(_stream_handle(parts_o.device)))
+    _native.check(code, "sqa_merge_partials")
+    return (out, lse) if return_lse else out

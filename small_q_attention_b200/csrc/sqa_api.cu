@@ -1,0 +1,304 @@
+// sqa_api.cu -- the extern "C" boundary (include/small_q_attention.h).
+//
+// Validates the contract on the host (no device reads), sizes the split-KV
+// launch from the SM count and the shapes, encodes the two TMA tensor maps
+// over the paged caches and launches the kernels on the caller's stream.
+// Errors are status codes; no exception leaves this file.
+#include <mutex>
+
+#include "../../include/small_q_attention.h"
+#include "sqa_internal.h"
+
+namespace sqa {
+namespace {
+
+constexpr int kAbiVersion = 100;
+constexpr size_t kAlign = 256;
+constexpr int kMaxDevices = 64;
+constexpr int kCtasPerSm = 2;
+// Shared memory one CTA may use so that kCtasPerSm fit on an SM
+// (228 KB per SM on sm_100, 1 KB reserved per CTA).
+constexpr int kSmemPerSm = 228 * 1024;
+constexpr int kSmemPerCta = kSmemPerSm / kCtasPerSm - 1024;
+constexpr int kDefaultMinPagesPerCta = 4;
+
+size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
+
+int sm_count(int device) {
+  static std::mutex mu;
+  static int cache[kMaxDevices] = {0};
+  if (device < 0 || device >= kMaxDevices) return 0;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[device] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return 0;
+    cache[device] = n;
+  }
+  return cache[device];
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*,
+                                   CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                   CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// [num_pages * 16 tokens, Hkv, 128] fp16 seen as a 3-D tensor; one box is
+// 64 dims x 1 head x 16 tokens (2 KB), 128-byte swizzled.
+bool encode_cache_map(CUtensorMap* map, const void* base, int num_pages, int hkv) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[3] = {(cuuint64_t)kHeadDim, (cuuint64_t)hkv, (cuuint64_t)num_pages * kPageSize};
+  const cuuint64_t strides[2] = {(cuuint64_t)kHeadDim * 2, (cuuint64_t)hkv * kHeadDim * 2};
+  const cuuint32_t box[3] = {64, 1, (cuuint32_t)kPageSize};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+struct Plan {
+  WarpShape shape;
+  int grid;
+  int stages;
+  int smem;
+  int segments;
+  int pieces;
+  size_t off_seg, off_lse, off_o, bytes;
+};
+
+int validate(const sqa_args* a) {
+  if (!a) return SQA_ERR_INVALID_ARGUMENT;
+  if (a->batch < 0 || a->q_len <= 0 || a->num_kv_heads <= 0 || a->num_pages <= 0 || a->max_pages <= 0)
+    return SQA_ERR_INVALID_ARGUMENT;
+  if (a->head_dim != kHeadDim || a->page_size != kPageSize) return SQA_ERR_UNSUPPORTED;
+  if (a->num_q_heads != kGroup * a->num_kv_heads) return SQA_ERR_UNSUPPORTED;
+  if (a->q_len > SQA_MAX_Q_LEN) return SQA_ERR_UNSUPPORTED;
+  if (a->max_seq_len < 0 || a->num_ctas < 0 || a->min_pages_per_cta < 0) return SQA_ERR_INVALID_ARGUMENT;
+  // unit indices are 32-bit on the device
+  if ((long long)a->batch * a->num_kv_heads * a->max_pages >= (1ll << 31)) return SQA_ERR_UNSUPPORTED;
+  if ((long long)a->num_pages * kPageSize >= (1ll << 31)) return SQA_ERR_UNSUPPORTED;
+  return SQA_OK;
+}
+
+int validate_pointers(const sqa_args* a) {
+  if (!a->query || !a->key_cache || !a->value_cache || !a->block_tables || !a->seq_lens)
+    return SQA_ERR_INVALID_ARGUMENT;
+  const bool full = a->out != nullptr;
+  const bool partial = a->out_partial != nullptr && a->out_lse != nullptr;
+  if (full == partial) return SQA_ERR_INVALID_ARGUMENT;  // exactly one output mode
+  if (!aligned16(a->query) || !aligned16(a->key_cache) || !aligned16(a->value_cache)) return SQA_ERR_INVALID_ARGUMENT;
+  if (full && !aligned16(a->out)) return SQA_ERR_INVALID_ARGUMENT;
+  if (partial && !aligned16(a->out_partial)) return SQA_ERR_INVALID_ARGUMENT;
+  if ((reinterpret_cast<uintptr_t>(a->block_tables) & 3u) || (reinterpret_cast<uintptr_t>(a->seq_lens) & 3u))
+    return SQA_ERR_INVALID_ARGUMENT;
+  return SQA_OK;
+}
+
+int make_plan(const sqa_args* a, int device, Plan* plan) {
+  const int sms = sm_count(device);
+  if (sms <= 0) return SQA_ERR_CUDA;
+  Plan pl;
+  pl.shape = warp_shape_for(a->q_len);
+  const int fixed = split_kv_smem_bytes(pl.shape, 0);
+  pl.stages = (kSmemPerCta - fixed) / (kStageBytes + 16);
+  if (pl.stages > kMaxStages) pl.stages = kMaxStages;
+  pl.smem = split_kv_smem_bytes(pl.shape, pl.stages);
+  pl.segments = a->batch * a->num_kv_heads;
+
+  long long pages_upper = a->max_pages;
+  if (a->max_seq_len > 0) {
+    const long long need = (a->max_seq_len + kPageSize - 1) / kPageSize;
+    if (need < pages_upper) pages_upper = need;
+  }
+  const long long units_upper = (long long)pl.segments * pages_upper;
+  const int min_pages = a->min_pages_per_cta > 0 ? a->min_pages_per_cta : kDefaultMinPagesPerCta;
+  long long grid = a->num_ctas > 0 ? a->num_ctas : (long long)sms * kCtasPerSm;
+  if (a->num_ctas <= 0) {
+    const long long by_work = (units_upper + min_pages - 1) / min_pages;
+    if (by_work < grid) grid = by_work;
+  }
+  if (grid < 1) grid = 1;
+  pl.grid = (int)grid;
+  pl.pieces = pl.grid + pl.segments;  // piece index = cta + segment < grid + segments - 1
+
+  pl.off_seg = kAlign;  // [0, 256): device status word
+  pl.off_lse = align_up(pl.off_seg + (size_t)pl.segments * sizeof(int2));
+  pl.off_o = align_up(pl.off_lse + (size_t)pl.pieces * pl.shape.rows_pad * sizeof(float));
+  pl.bytes = align_up(pl.off_o + (size_t)pl.pieces * pl.shape.rows_pad * kHeadDim * sizeof(float));
+  *plan = pl;
+  return SQA_OK;
+}
+
+int current_device(int device) {
+  if (device >= 0) return device;
+  int d = 0;
+  if (cudaGetDevice(&d) != cudaSuccess) return -1;
+  return d;
+}
+
+}  // namespace
+}  // namespace sqa
+
+using namespace sqa;
+
+extern "C" {
+
+int sqa_abi_version(void) { return kAbiVersion; }
+
+const char* sqa_status_string(int status) {
+  switch (status) {
+    case SQA_OK: return "ok";
+    case SQA_ERR_INVALID_ARGUMENT: return "invalid argument (null/misaligned pointer or bad shape)";
+    case SQA_ERR_UNSUPPORTED: return "unsupported shape (needs head_dim 128, page_size 16, Hq = 4*Hkv, 1 <= q_len <= 16)";
+    case SQA_ERR_WORKSPACE_TOO_SMALL: return "workspace too small";
+    case SQA_ERR_CUDA: return "CUDA call failed";
+    case SQA_ERR_DEVICE: return "device reported an error (see the SQA_DEV_* bits)";
+    default: return "unknown status";
+  }
+}
+
+size_t sqa_workspace_bytes(const sqa_args* args, int device, int* status) {
+  int st = validate(args);
+  Plan pl;
+  if (st == SQA_OK) {
+    const int dev = current_device(device);
+    st = dev < 0 ? SQA_ERR_CUDA : make_plan(args, dev, &pl);
+  }
+  if (status) *status = st;
+  return st == SQA_OK ? pl.bytes : 0;
+}
+
+int sqa_workspace_init(void* workspace, size_t workspace_bytes, void* stream) {
+  if (!workspace || workspace_bytes < kAlign) return SQA_ERR_INVALID_ARGUMENT;
+  return cudaMemsetAsync(workspace, 0, kAlign, reinterpret_cast<cudaStream_t>(stream)) == cudaSuccess
+             ? SQA_OK
+             : SQA_ERR_CUDA;
+}
+
+namespace {
+int forward_impl(const sqa_args* a, void* workspace, size_t workspace_bytes, void* stream_ptr,
+                 void* ev_before, void* ev_after) {
+  int st = validate(a);
+  if (st != SQA_OK) return st;
+  st = validate_pointers(a);
+  if (st != SQA_OK) return st;
+  if (a->batch == 0) return SQA_OK;
+  const int dev = current_device(-1);
+  if (dev < 0) return SQA_ERR_CUDA;
+  Plan pl;
+  st = make_plan(a, dev, &pl);
+  if (st != SQA_OK) return st;
+  if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & (kAlign - 1))) return SQA_ERR_INVALID_ARGUMENT;
+  if (workspace_bytes < pl.bytes) return SQA_ERR_WORKSPACE_TOO_SMALL;
+
+  CUtensorMap tm_k, tm_v;
+  if (!encode_cache_map(&tm_k, a->key_cache, a->num_pages, a->num_kv_heads) ||
+      !encode_cache_map(&tm_v, a->value_cache, a->num_pages, a->num_kv_heads))
+    return SQA_ERR_CUDA;
+
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  SplitKvParams p;
+  p.q = static_cast<const __half*>(a->query);
+  p.block_tables = a->block_tables;
+  p.seq_lens = a->seq_lens;
+  p.mask_lens = a->mask_lens;
+  p.out = static_cast<__half*>(a->out);
+  p.out_o = a->out_partial;
+  p.out_lse = a->out_lse;
+  p.ws_o = reinterpret_cast<float*>(ws + pl.off_o);
+  p.ws_lse = reinterpret_cast<float*>(ws + pl.off_lse);
+  p.seg_info = reinterpret_cast<int2*>(ws + pl.off_seg);
+  p.status = reinterpret_cast<unsigned int*>(ws);
+  p.batch = a->batch;
+  p.q_len = a->q_len;
+  p.hq = a->num_q_heads;
+  p.hkv = a->num_kv_heads;
+  p.max_pages = a->max_pages;
+  p.num_pages = a->num_pages;
+  p.num_stages = pl.stages;
+  p.scale_log2 = 1.4426950408889634f / sqrtf((float)kHeadDim);
+
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_ptr);
+  if (ev_before && cudaEventRecord(reinterpret_cast<cudaEvent_t>(ev_before), stream) != cudaSuccess)
+    return SQA_ERR_CUDA;
+  if (launch_split_kv(p, tm_k, tm_v, pl.grid, pl.smem, stream) != cudaSuccess) return SQA_ERR_CUDA;
+  if (ev_after && cudaEventRecord(reinterpret_cast<cudaEvent_t>(ev_after), stream) != cudaSuccess)
+    return SQA_ERR_CUDA;
+
+  MergeParams m;
+  m.parts_o = p.ws_o;
+  m.parts_lse = p.ws_lse;
+  m.seg_info = p.seg_info;
+  m.seq_lens = a->seq_lens;
+  m.out = p.out;
+  m.out_o = p.out_o;
+  m.out_lse = p.out_lse;
+  m.rows = 0;
+  m.num_parts = 0;
+  m.piece_rows = pl.shape.rows_pad;
+  m.batch = a->batch;
+  m.q_len = a->q_len;
+  m.hq = a->num_q_heads;
+  m.hkv = a->num_kv_heads;
+  m.max_pages = a->max_pages;
+  if (launch_segment_merge(m, pl.shape.rows_pad, stream) != cudaSuccess) return SQA_ERR_CUDA;
+  return SQA_OK;
+}
+}  // namespace
+
+int sqa_forward(const sqa_args* a, void* workspace, size_t workspace_bytes, void* stream) {
+  return forward_impl(a, workspace, workspace_bytes, stream, nullptr, nullptr);
+}
+
+int sqa_forward_timed(const sqa_args* a, void* workspace, size_t workspace_bytes, void* stream,
+                      void* event_before, void* event_after) {
+  return forward_impl(a, workspace, workspace_bytes, stream, event_before, event_after);
+}
+
+int sqa_merge_partials(const float* parts_o, const float* parts_lse, int32_t num_parts, int64_t rows,
+                       void* out, float* out_o, float* out_lse, void* stream) {
+  if (!parts_o || !parts_lse || num_parts <= 0 || rows < 0) return SQA_ERR_INVALID_ARGUMENT;
+  if (!out && !out_o && !out_lse) return SQA_ERR_INVALID_ARGUMENT;
+  if (!aligned16(parts_o) || (out && !aligned16(out)) || (out_o && !aligned16(out_o)))
+    return SQA_ERR_INVALID_ARGUMENT;
+  if (rows == 0) return SQA_OK;
+  if ((rows + 3) / 4 >= (1ll << 31)) return SQA_ERR_UNSUPPORTED;
+  MergeParams m = {};
+  m.parts_o = parts_o;
+  m.parts_lse = parts_lse;
+  m.out = static_cast<__half*>(out);
+  m.out_o = out_o;
+  m.out_lse = out_lse;
+  m.rows = rows;
+  m.num_parts = num_parts;
+  return launch_partials_merge(m, reinterpret_cast<cudaStream_t>(stream)) == cudaSuccess ? SQA_OK : SQA_ERR_CUDA;
+}
+
+int sqa_read_device_status(void* workspace, uint32_t* device_bits, int clear, void* stream_ptr) {
+  if (!workspace) return SQA_ERR_INVALID_ARGUMENT;
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_ptr);
+  uint32_t bits = 0;
+  if (cudaMemcpyAsync(&bits, workspace, sizeof(bits), cudaMemcpyDeviceToHost, stream) != cudaSuccess)
+    return SQA_ERR_CUDA;
+  if (clear && cudaMemsetAsync(workspace, 0, sizeof(bits), stream) != cudaSuccess) return SQA_ERR_CUDA;
+  if (cudaStreamSynchronize(stream) != cudaSuccess) return SQA_ERR_CUDA;
+  if (device_bits) *device_bits = bits;
+  return bits ? SQA_ERR_DEVICE : SQA_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,78 @@
+// sqa_internal.h -- declarations shared by the kernel and C-ABI translation units.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace sqa {
+
+constexpr int kHeadDim = 128;
+constexpr int kPageSize = 16;
+constexpr int kGroup = 4;                 // query heads per KV head
+constexpr int kConsumerWarps = 4;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;  // + one TMA producer warp
+constexpr int kStageBytes = 4 * 2048;     // K and V of one page of one KV head, two 64-dim halves each
+constexpr int kMaxStages = 16;
+constexpr int kCombineStride = kHeadDim + 4;  // fp32 row stride of the combine buffer (bank-conflict free)
+
+// Which warp shape a q_len uses.  A KV head owns R = 4 * q_len packed query
+// rows; each consumer warp holds 8 * nt of them (nt n8-tiles of the swapped
+// MMA), wr warps split the rows, and the 4 / wr token groups split the pages.
+struct WarpShape {
+  int nt;        // n8 tiles (rows / 8) per warp: 1 or 2
+  int wr;        // warps across the rows: 1, 2 or 4
+  int rows_pad;  // 8 * nt * wr >= 4 * q_len
+  int wt() const { return kConsumerWarps / wr; }
+};
+
+inline WarpShape warp_shape_for(int q_len) {
+  const int rows = kGroup * q_len;
+  if (rows <= 8) return {1, 1, 8};
+  if (rows <= 16) return {2, 1, 16};
+  if (rows <= 32) return {2, 2, 32};
+  return {2, 4, 64};
+}
+
+struct SplitKvParams {
+  const __half* q;              // [B, q_len, Hq, 128]
+  const int32_t* block_tables;  // [B, max_pages]
+  const int32_t* seq_lens;      // [B]
+  const int32_t* mask_lens;     // [B] or nullptr
+  __half* out;                  // full mode
+  float* out_o;                 // partial mode
+  float* out_lse;               // partial mode
+  float* ws_o;                  // [pieces, rows_pad, 128]
+  float* ws_lse;                // [pieces, rows_pad]
+  int2* seg_info;               // [B * Hkv]: (first piece index, piece count)
+  unsigned int* status;
+  int batch, q_len, hq, hkv, max_pages, num_pages;
+  int num_stages;
+  float scale_log2;             // head_dim^-0.5 * log2(e)
+};
+
+struct MergeParams {
+  const float* parts_o;         // piece i, row r at parts_o + (i * piece_rows + r) * 128 (+ first offset)
+  const float* parts_lse;
+  const int2* seg_info;         // nullptr: every segment has pieces [0, num_parts)
+  const int32_t* seq_lens;      // per-call merge: empty sequences are written as 0 / -inf
+  __half* out;
+  float* out_o;
+  float* out_lse;
+  long long rows;               // cross-device merge: total rows; per-call merge: unused
+  int num_parts;
+  int piece_rows;               // rows per piece (rows_pad for the per-call merge)
+  int batch, q_len, hq, hkv, max_pages;
+};
+
+// Launchers (stream-ordered, no allocation).  Return cudaGetLastError().
+cudaError_t launch_split_kv(const SplitKvParams& p, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
+                            int grid, int smem_bytes, cudaStream_t stream);
+cudaError_t launch_segment_merge(const MergeParams& p, int rows_pad, cudaStream_t stream);
+cudaError_t launch_partials_merge(const MergeParams& p, cudaStream_t stream);
+
+// Dynamic shared memory of the split-KV kernel for a warp shape and stage count.
+int split_kv_smem_bytes(const WarpShape& ws, int num_stages);
+
+}  // namespace sqa

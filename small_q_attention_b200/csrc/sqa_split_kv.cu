@@ -1,0 +1,541 @@
+// sqa_split_kv.cu -- the split-KV paged attention kernel for sm_100a.
+//
+// Work decomposition.  One "unit" is one 16-token page of one KV head of one
+// sequence; the units of (b, kvh) form segment s = b * Hkv + kvh.  All units
+// are laid end to end and cut into gridDim.x equal ranges, one per CTA, so
+// every CTA streams the same number of K/V bytes whatever the mix of lengths
+// (a ragged batch balances like a uniform one).  A CTA range may end inside a
+// segment or cover several short ones; each (CTA, segment) overlap is a
+// "piece".  A piece that is a whole segment writes the final output directly;
+// otherwise it writes a normalised fp32 partial and its log-sum-exp to slot
+// (blockIdx.x + s) of the workspace and the merge kernel combines them.  The
+// schedule is derived on the device from seq_lens, so the host never
+// synchronises.  (Upstream equivalent: a fixed chunk_keys split with
+// ceil(max_len / chunk_keys) chunks per row, csrc/small_q_attention_ext.cu:1178.)
+//
+// Data movement.  Warp 4 is the TMA producer: for each page it reads the page
+// id (32 ids per coalesced load, the next 32 prefetched), waits for a free
+// stage of the shared-memory ring and issues four 2 KB tensor loads (K and V,
+// two 64-dim halves each, 128-byte swizzled) that complete on the stage's
+// mbarrier.  Each K/V byte therefore crosses HBM exactly once per KV head
+// (the upstream v3 kernel re-reads K/V for every query row, ext.cu:462-508).
+//
+// Math.  Warps 0-3 are consumers.  The 4 query heads x q_len draft rows of a
+// KV head are packed as the N side of mma.sync m16n8k16 with the 16 tokens
+// of a page as M ("swapped" orientation): S^T = K_page . Q^T, so q_len = 2
+// (8 rows) fills the n8 tile with no padding.  The fp32 online softmax works
+// on the S^T fragments (row max over tokens = 3 shuffles), probabilities are
+// packed to fp16 and transposed in registers with movmatrix into the B
+// operand of O^T += V^T_page . P^T.  Q lives in registers for a whole piece.
+#include "sqa_internal.h"
+#include "sqa_ptx.cuh"
+
+namespace sqa {
+namespace {
+
+constexpr float kLn2 = 0.6931471805599453f;
+
+struct SegWalk {
+  int b;          // sequence
+  int h;          // KV head
+  int pg;         // first page of the current piece within the segment
+  int pages;      // pages of sequence b (clamped to the table width)
+  int seg_start;  // global unit index of (b, h, page 0)
+};
+
+__device__ __forceinline__ int seq_pages(const SplitKvParams& p, int b) {
+  const int len = max(__ldg(p.seq_lens + b), 0);
+  return min((len + kPageSize - 1) / kPageSize, p.max_pages);
+}
+
+__device__ __forceinline__ void next_segment(const SplitKvParams& p, SegWalk& w) {
+  w.seg_start += w.pages;
+  w.pg = 0;
+  if (++w.h == p.hkv) {
+    w.h = 0;
+    do {
+      ++w.b;
+      w.pages = (w.b < p.batch) ? seq_pages(p, w.b) : 0;
+    } while (w.pages == 0 && w.b < p.batch);
+  }
+}
+
+// Shared schedule, filled by warp 0 before the CTA-wide barrier.
+struct Schedule {
+  int start, end;      // this CTA's unit range
+  int per_cta;         // units per CTA
+  int b0, u_b0;        // sequence containing `start` and the units before it
+  int abort;           // set by a timed-out wait
+};
+
+// Warp 0: total units, this CTA's range and the sequence it starts in.
+__device__ void build_schedule(const SplitKvParams& p, Schedule* sch) {
+  const int lane = threadIdx.x & 31;
+  unsigned int flags = 0;
+  int total_pages = 0;
+  for (int base = 0; base < p.batch; base += 32) {
+    const int b = base + lane;
+    int pages = 0;
+    if (b < p.batch) {
+      const int len = __ldg(p.seq_lens + b);
+      pages = seq_pages(p, b);
+      if (len > p.max_pages * kPageSize) flags |= 2u;                 // SQA_DEV_SEQ_TOO_LONG
+      if (p.out != nullptr && len < p.q_len) flags |= 4u;             // SQA_DEV_SEQ_TOO_SHORT
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) pages += __shfl_xor_sync(0xffffffffu, pages, off);
+    total_pages += pages;
+  }
+  flags = __reduce_or_sync(0xffffffffu, flags);
+  if (blockIdx.x == 0 && lane == 0 && flags) atomicOr(p.status, flags);
+
+  const int total = total_pages * p.hkv;
+  const int per = max(1, (total + (int)gridDim.x - 1) / (int)gridDim.x);
+  const int start = min(total, (int)blockIdx.x * per);
+  const int end = min(total, start + per);
+
+  // Sequence containing unit `start`: first b whose inclusive unit prefix exceeds it.
+  int b0 = p.batch, u_b0 = 0;
+  if (start < end) {
+    int running = 0;  // units before this 32-sequence block
+    for (int base = 0; base < p.batch; base += 32) {
+      const int b = base + lane;
+      const int units = (b < p.batch) ? seq_pages(p, b) * p.hkv : 0;
+      int incl = units;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += y;
+      }
+      const unsigned hit = __ballot_sync(0xffffffffu, running + incl > start);
+      if (hit) {
+        const int l = __ffs(hit) - 1;
+        b0 = base + l;
+        u_b0 = running + __shfl_sync(0xffffffffu, incl - units, l);
+        break;
+      }
+      running += __shfl_sync(0xffffffffu, incl, 31);
+    }
+  }
+  if (lane == 0) {
+    sch->start = start;
+    sch->end = end;
+    sch->per_cta = per;
+    sch->b0 = b0;
+    sch->u_b0 = u_b0;
+    sch->abort = 0;
+  }
+}
+
+__device__ __forceinline__ SegWalk first_segment(const SplitKvParams& p, const Schedule& s) {
+  SegWalk w;
+  w.b = s.b0;
+  w.pages = (s.start < s.end) ? seq_pages(p, s.b0) : 1;
+  const int off = s.start - s.u_b0;
+  w.h = off / w.pages;
+  w.pg = off - w.h * w.pages;
+  w.seg_start = s.u_b0 + w.h * w.pages;
+  return w;
+}
+
+// ------------------------------------------------------------------ producer
+__device__ void producer_loop(const SplitKvParams& p, const Schedule& sch, const CUtensorMap* tm_k,
+                              const CUtensorMap* tm_v, uint8_t* stages, uint64_t* full,
+                              uint64_t* empty, volatile int* abort) {
+  const int lane = threadIdx.x & 31;
+  const uint64_t policy = l2_policy_evict_first();
+  SegWalk w = first_segment(p, sch);
+  int slot = 0;
+  uint32_t phase = 0;
+  unsigned int bad_page = 0;
+  int unit = sch.start;
+  while (unit < sch.end) {
+    const int seg_end = w.seg_start + w.pages;
+    const int n = min(sch.end, seg_end) - unit;
+    const int32_t* row = p.block_tables + (size_t)w.b * p.max_pages + w.pg;
+    int ids = (lane < n) ? __ldg(row + lane) : 0;
+    for (int c0 = 0; c0 < n; c0 += 32) {
+      const int cnt = min(32, n - c0);
+      // prefetch the next 32 page ids while this block is issued
+      const int nxt = c0 + 32 + lane;
+      const int ids_next = (nxt < n) ? __ldg(row + nxt) : 0;
+      for (int j = 0; j < cnt; ++j) {
+        int page = __shfl_sync(0xffffffffu, ids, j);
+        if (page < 0 || page >= p.num_pages) {
+          bad_page = 1;
+          page = 0;  // never hand TMA a coordinate outside the pool
+        }
+        if (lane == 0) {
+          const uint32_t e = smem_u32(empty + slot);
+          const uint32_t f = smem_u32(full + slot);
+          if (mbar_wait_bounded(e, phase ^ 1u, abort, p.status)) {
+            mbar_arrive_expect_tx(f, kStageBytes);
+            const uint32_t dst = smem_u32(stages + (size_t)slot * kStageBytes);
+            const int tok = page * kPageSize;
+            tma_load_3d(dst, tm_k, f, 0, w.h, tok, policy);
+            tma_load_3d(dst + 2048, tm_k, f, 64, w.h, tok, policy);
+            tma_load_3d(dst + 4096, tm_v, f, 0, w.h, tok, policy);
+            tma_load_3d(dst + 6144, tm_v, f, 64, w.h, tok, policy);
+          }
+        }
+        if (++slot == p.num_stages) {
+          slot = 0;
+          phase ^= 1u;
+        }
+      }
+      ids = ids_next;
+    }
+    unit += n;
+    if (unit >= seg_end) next_segment(p, w);
+    else w.pg += n;
+  }
+  if (__any_sync(0xffffffffu, bad_page) && lane == 0) atomicOr(p.status, 8u);  // SQA_DEV_BAD_PAGE
+}
+
+// ------------------------------------------------------------------ consumers
+template <int NT, int WR>
+__device__ void consumer_loop(const SplitKvParams& p, const Schedule& sch, uint8_t* stages,
+                              uint64_t* full, uint64_t* empty, float* cbuf, float* mbuf,
+                              float* lbuf, volatile int* abort) {
+  constexpr int WT = kConsumerWarps / WR;  // token groups
+  constexpr int ROWS_W = 8 * NT;           // rows per warp
+  constexpr int ROWS_PAD = ROWS_W * WR;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int tid = threadIdx.x;  // 0..127 over the consumer warps
+  const int wr = warp % WR;     // row slice
+  const int tg = warp / WR;     // token group
+  const int g = lane >> 2;      // fragment row group
+  const int t = lane & 3;       // fragment column pair
+  const int rows = kGroup * p.q_len;
+
+  // ldmatrix lane addressing inside a 128-byte-swizzled [16 tok][64 dim] half tile.
+  const int k_row = (lane & 7) + ((lane >> 3) & 1) * 8;  // K: token row of this lane's address
+  const int k_cb = lane >> 4;                             // K: +1 chunk for matrices 2, 3
+  const int v_row = (lane & 7) + (lane >> 4) * 8;         // V (trans): token row
+  const int v_cb = (lane >> 3) & 1;                       // V: +1 chunk for matrices 1, 3
+
+  SegWalk w = first_segment(p, sch);
+  int slot = 0;
+  uint32_t phase = 0;
+  int gi = 0;  // CTA-wide page counter (selects the token group)
+  int unit = sch.start;
+  while (unit < sch.end) {
+    const int s = w.b * p.hkv + w.h;
+    const int seg_end = w.seg_start + w.pages;
+    const int n = min(sch.end, seg_end) - unit;
+    const bool whole = (unit == w.seg_start) && (seg_end <= sch.end);
+    if (tid == 0 && unit == w.seg_start) {
+      const int last_cta = (seg_end - 1) / sch.per_cta;
+      p.seg_info[s] = make_int2((int)blockIdx.x + s, last_cta - (int)blockIdx.x + 1);
+    }
+
+    const int len_raw = __ldg(p.seq_lens + w.b);
+    const int len = min(len_raw, w.pages * kPageSize);
+    const int mlen = p.mask_lens ? __ldg(p.mask_lens + w.b) : len_raw;
+    const int thr_min = min(len, mlen - p.q_len + 1);  // visible tokens of draft row 0
+
+    // Q^T fragments (B operand of S^T = K Q^T) for this warp's rows, and the
+    // per-thread causal limits of its two fragment columns per n-tile.
+    uint32_t qf[NT][8][2];
+    int thr[NT];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const int row = wr * ROWS_W + nt * 8 + g;
+      const bool ok = row < rows;
+      const __half* qp = p.q + ((size_t)(w.b * p.q_len + (row >> 2)) * p.hq + w.h * kGroup + (row & 3)) * kHeadDim;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        qf[nt][kk][0] = ok ? __ldg(reinterpret_cast<const uint32_t*>(qp + kk * 16 + 2 * t)) : 0u;
+        qf[nt][kk][1] = ok ? __ldg(reinterpret_cast<const uint32_t*>(qp + kk * 16 + 8 + 2 * t)) : 0u;
+      }
+      const int qi = (wr * ROWS_W + nt * 8 + 2 * t) >> 2;  // both columns share qi
+      thr[nt] = min(len, mlen - p.q_len + qi + 1);
+    }
+
+    float m_run[NT][2], l_run[NT][2];
+    float o[8][NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      m_run[nt][0] = m_run[nt][1] = -INFINITY;
+      l_run[nt][0] = l_run[nt][1] = 0.f;
+#pragma unroll
+      for (int md = 0; md < 8; ++md)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[md][nt][e] = 0.f;
+    }
+
+    for (int j = 0; j < n; ++j, ++gi) {
+      const int my_slot = slot;
+      const uint32_t my_phase = phase;
+      if (++slot == p.num_stages) {
+        slot = 0;
+        phase ^= 1u;
+      }
+      if ((gi % WT) != tg) continue;
+
+      mbar_wait_bounded(smem_u32(full + my_slot), my_phase, abort, p.status);
+      uint8_t* st = stages + (size_t)my_slot * kStageBytes;
+      const uint32_t k_base = smem_u32(st);
+      const uint32_t v_base = k_base + 4096;
+      const int tok0 = (w.pg + j) * kPageSize;
+
+      // Tokens at or past the sequence end hold whatever the pool has there:
+      // zero their V rows so that p = 0 never meets a NaN/Inf.
+      const bool tail = tok0 + kPageSize > len;
+      if (tail) {
+        const int first = max(len - tok0, 0);
+        for (int c = lane; c < (kPageSize - first) * 16; c += 32) {
+          const int r = first + (c >> 4);
+          *reinterpret_cast<uint4*>(st + 4096 + ((c >> 3) & 1) * 2048 + r * 128 + (c & 7) * 16) =
+              make_uint4(0u, 0u, 0u, 0u);
+        }
+        __syncwarp();
+      }
+
+      // ---- S^T[16 tok x 8*NT rows] = K_page . Q^T, two k-halves in flight
+      float sa[NT][4], sb[NT][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sa[nt][e] = sb[nt][e] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        uint32_t a[4];
+        const int chunk = (((kk & 3) << 1) | k_cb) ^ (k_row & 7);
+        ldsm_x4(a, k_base + (kk >> 2) * 2048 + k_row * 128 + chunk * 16);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          if (kk & 1) mma_16816(sb[nt], a, qf[nt][kk][0], qf[nt][kk][1]);
+          else mma_16816(sa[nt], a, qf[nt][kk][0], qf[nt][kk][1]);
+        }
+      }
+
+      // ---- online softmax over the page's tokens (base 2, scaled)
+      const bool masked = tok0 + kPageSize > thr_min;
+      uint32_t pb[NT][2];
+      float alpha[NT][2];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        float x[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          x[e] = (sa[nt][e] + sb[nt][e]) * p.scale_log2;
+          if (masked && tok0 + g + ((e >> 1) << 3) >= thr[nt]) x[e] = -INFINITY;
+        }
+        float mx0 = fmaxf(x[0], x[2]), mx1 = fmaxf(x[1], x[3]);
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+          mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+          mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+        }
+        const float mn0 = fmaxf(m_run[nt][0], mx0), mn1 = fmaxf(m_run[nt][1], mx1);
+        const float base0 = (mn0 == -INFINITY) ? 0.f : mn0;
+        const float base1 = (mn1 == -INFINITY) ? 0.f : mn1;
+        alpha[nt][0] = ex2(m_run[nt][0] - base0);
+        alpha[nt][1] = ex2(m_run[nt][1] - base1);
+        m_run[nt][0] = mn0;
+        m_run[nt][1] = mn1;
+        const float p0 = ex2(x[0] - base0), p1 = ex2(x[1] - base1);
+        const float p2 = ex2(x[2] - base0), p3 = ex2(x[3] - base1);
+        l_run[nt][0] = l_run[nt][0] * alpha[nt][0] + (p0 + p2);
+        l_run[nt][1] = l_run[nt][1] * alpha[nt][1] + (p1 + p3);
+        // [tok g | tok g+8][rows 2t, 2t+1] -> transpose -> B fragment [tok 2t.., 2t+8..][row g]
+        pb[nt][0] = movmatrix_trans(pack_half2(p0, p1));
+        pb[nt][1] = movmatrix_trans(pack_half2(p2, p3));
+      }
+      bool rescale = false;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) rescale |= (alpha[nt][0] != 1.f) | (alpha[nt][1] != 1.f);
+      if (__any_sync(0xffffffffu, rescale)) {
+#pragma unroll
+        for (int md = 0; md < 8; ++md)
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            o[md][nt][0] *= alpha[nt][0];
+            o[md][nt][1] *= alpha[nt][1];
+            o[md][nt][2] *= alpha[nt][0];
+            o[md][nt][3] *= alpha[nt][1];
+          }
+      }
+
+      // ---- O^T[128 dim x rows] += V^T_page . P^T
+#pragma unroll
+      for (int md = 0; md < 8; ++md) {
+        uint32_t a[4];
+        const int chunk = (((md & 3) << 1) | v_cb) ^ (v_row & 7);
+        ldsm_x4_trans(a, v_base + (md >> 2) * 2048 + v_row * 128 + chunk * 16);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) mma_16816(o[md][nt], a, pb[nt][0], pb[nt][1]);
+      }
+
+      if (tail) fence_proxy_async_smem();  // generic writes above vs the next TMA into this stage
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(empty + my_slot));
+    }
+
+    // ---- piece epilogue: combine the token groups through shared memory
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        float l = l_run[nt][c];
+        l += __shfl_xor_sync(0xffffffffu, l, 4);
+        l += __shfl_xor_sync(0xffffffffu, l, 8);
+        l += __shfl_xor_sync(0xffffffffu, l, 16);
+        l_run[nt][c] = l;
+      }
+    if (g == 0) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const int row = wr * ROWS_W + nt * 8 + 2 * t + c;
+          mbuf[tg * ROWS_PAD + row] = m_run[nt][c];
+          lbuf[tg * ROWS_PAD + row] = l_run[nt][c];
+        }
+    }
+#pragma unroll
+    for (int md = 0; md < 8; ++md)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int row = wr * ROWS_W + nt * 8 + 2 * t + (e & 1);
+          const int d = md * 16 + g + ((e >> 1) << 3);
+          cbuf[(tg * ROWS_PAD + row) * kCombineStride + d] = o[md][nt][e];
+        }
+    named_bar_sync(1, kConsumerWarps * 32);
+
+    const int piece = (int)blockIdx.x + s;
+    for (int item = tid; item < rows * 32; item += kConsumerWarps * 32) {
+      const int row = item >> 5;
+      const int c4 = (item & 31) * 4;
+      float mmax = -INFINITY;
+#pragma unroll
+      for (int x = 0; x < WT; ++x) mmax = fmaxf(mmax, mbuf[x * ROWS_PAD + row]);
+      const float base = (mmax == -INFINITY) ? 0.f : mmax;
+      float L = 0.f;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int x = 0; x < WT; ++x) {
+        const float wgt = ex2(mbuf[x * ROWS_PAD + row] - base);
+        L += wgt * lbuf[x * ROWS_PAD + row];
+        const float4 v = *reinterpret_cast<const float4*>(cbuf + (x * ROWS_PAD + row) * kCombineStride + c4);
+        acc.x += wgt * v.x;
+        acc.y += wgt * v.y;
+        acc.z += wgt * v.z;
+        acc.w += wgt * v.w;
+      }
+      const float inv = (L > 0.f) ? 1.f / L : 0.f;
+      acc.x *= inv;
+      acc.y *= inv;
+      acc.z *= inv;
+      acc.w *= inv;
+      const float lse = (L > 0.f) ? (mmax + __log2f(L)) * kLn2 : -INFINITY;
+      const size_t out_row = (size_t)(w.b * p.q_len + (row >> 2)) * p.hq + w.h * kGroup + (row & 3);
+      if (whole) {
+        if (p.out != nullptr) {
+          uint2 h;
+          h.x = pack_half2(acc.x, acc.y);
+          h.y = pack_half2(acc.z, acc.w);
+          *reinterpret_cast<uint2*>(p.out + out_row * kHeadDim + c4) = h;
+        } else {
+          *reinterpret_cast<float4*>(p.out_o + out_row * kHeadDim + c4) = acc;
+          if (c4 == 0) p.out_lse[out_row] = lse;
+        }
+      } else {
+        *reinterpret_cast<float4*>(p.ws_o + ((size_t)piece * ROWS_PAD + row) * kHeadDim + c4) = acc;
+        if (c4 == 0) p.ws_lse[(size_t)piece * ROWS_PAD + row] = lse;
+      }
+    }
+    named_bar_sync(1, kConsumerWarps * 32);
+
+    unit += n;
+    if (unit >= seg_end) next_segment(p, w);
+    else w.pg += n;
+  }
+}
+
+template <int NT, int WR>
+__global__ void __launch_bounds__(kThreads, 2)
+    sqa_split_kv_kernel(const SplitKvParams p, const __grid_constant__ CUtensorMap tm_k,
+                        const __grid_constant__ CUtensorMap tm_v) {
+  constexpr int WT = kConsumerWarps / WR;
+  constexpr int ROWS_PAD = 8 * NT * WR;
+  extern __shared__ uint8_t smem_raw[];
+  // 128-byte swizzled TMA destinations want 1024-byte alignment.
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stages = smem;
+  float* cbuf = reinterpret_cast<float*>(smem + (size_t)p.num_stages * kStageBytes);
+  float* mbuf = cbuf + WT * ROWS_PAD * kCombineStride;
+  float* lbuf = mbuf + WT * ROWS_PAD;
+  uint64_t* full = reinterpret_cast<uint64_t*>(lbuf + WT * ROWS_PAD);
+  uint64_t* empty = full + p.num_stages;
+  Schedule* sch = reinterpret_cast<Schedule*>(empty + p.num_stages);
+
+  const int warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < p.num_stages; ++i) {
+      mbar_init(smem_u32(full + i), 1);
+      mbar_init(smem_u32(empty + i), WR);
+    }
+    fence_mbar_init();
+  }
+  if (warp == kConsumerWarps && (threadIdx.x & 31) == 0) {
+    prefetch_tensormap(&tm_k);
+    prefetch_tensormap(&tm_v);
+  }
+  if (warp == 0) build_schedule(p, sch);
+  __syncthreads();
+
+  const Schedule s = *sch;
+  volatile int* abort = &sch->abort;
+  if (warp == kConsumerWarps) {
+    producer_loop(p, s, &tm_k, &tm_v, stages, full, empty, abort);
+  } else {
+    consumer_loop<NT, WR>(p, s, stages, full, empty, cbuf, mbuf, lbuf, abort);
+  }
+}
+
+template <int NT, int WR>
+cudaError_t launch_shape(const SplitKvParams& p, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
+                         int grid, int smem_bytes, cudaStream_t stream) {
+  auto kernel = sqa_split_kv_kernel<NT, WR>;
+  // Raise the dynamic shared-memory limit once per device (the size is fixed
+  // per warp shape), outside any stream capture that may follow.
+  static int configured[64] = {0};
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  if (dev < 0 || dev >= 64 || configured[dev] < smem_bytes) {
+    err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+    if (err != cudaSuccess) return err;
+    if (dev >= 0 && dev < 64) configured[dev] = smem_bytes;
+  }
+  kernel<<<grid, kThreads, smem_bytes, stream>>>(p, tm_k, tm_v);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+int split_kv_smem_bytes(const WarpShape& ws, int num_stages) {
+  const int rows = ws.wt() * ws.rows_pad;
+  return 1024                                   // alignment slack
+         + num_stages * kStageBytes             // K/V ring
+         + rows * kCombineStride * 4            // combine buffer
+         + 2 * rows * 4                         // m, l
+         + 2 * num_stages * 8                   // full / empty barriers
+         + 64;                                  // schedule
+}
+
+cudaError_t launch_split_kv(const SplitKvParams& p, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
+                            int grid, int smem_bytes, cudaStream_t stream) {
+  const WarpShape ws = warp_shape_for(p.q_len);
+  if (ws.nt == 1) return launch_shape<1, 1>(p, tm_k, tm_v, grid, smem_bytes, stream);
+  if (ws.wr == 1) return launch_shape<2, 1>(p, tm_k, tm_v, grid, smem_bytes, stream);
+  if (ws.wr == 2) return launch_shape<2, 2>(p, tm_k, tm_v, grid, smem_bytes, stream);
+  return launch_shape<2, 4>(p, tm_k, tm_v, grid, smem_bytes, stream);
+}
+
+}  // namespace sqa

@@ -1,0 +1,270 @@
+"""GPU parity of the sm_100a kernel against the CPU oracle and the golden vectors.
+
+Tolerance (from the operator's contract): fp16 outputs with fp32 accumulation
+must satisfy ``|out - ref| <= 2e-2 + 1e-2 * |ref|`` element-wise and
+``max |out - ref| <= 2e-2``.  Page-table and mask indexing must be exact:
+the one-hot test makes any wrong token move an output by >= 16/128.
+"""
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import merge_partials as oracle_merge
+from oracle import paged_mtp_attention_partial, paged_mtp_attention_reference
+
+pytestmark = pytest.mark.gpu
+
+ATOL = 2e-2
+RTOL = 1e-2
+GOLDEN = sorted((Path(__file__).parent / "golden").glob("*.npz"))
+
+
+@pytest.fixture(scope="module")
+def sqa():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    import small_q_attention_b200 as m
+    from small_q_attention_b200 import _native
+
+    _native.library()  # fail loudly if the native library is missing
+    return m
+
+
+def assert_close(out, ref):
+    out = out.float().cpu().numpy() if isinstance(out, torch.Tensor) else out
+    ref = ref.float().cpu().numpy() if isinstance(ref, torch.Tensor) else ref
+    assert out.shape == ref.shape
+    assert np.isfinite(out).all()
+    err = np.abs(out - ref)
+    bound = ATOL + RTOL * np.abs(ref)
+    bad = err > bound
+    assert not bad.any(), f"{bad.sum()} elements out of tolerance; max err {err.max():.3e}"
+    assert err.max() <= ATOL, f"max abs err {err.max():.3e}"
+
+
+def case(q_len, lens, *, hkv=8, pool_factor=1.5, page_mode="random", seed=0, k_outlier_frac=0.0):
+    from small_q_attention_b200.workloads import make_case
+
+    return make_case(len(lens), q_len, lens, hkv=hkv, pool_factor=pool_factor, page_mode=page_mode,
+                     seed=seed, device="cuda", gen_device="cpu", k_outlier_frac=k_outlier_frac)
+
+
+def run(sqa, c, **kw):
+    return sqa.small_q_attention(c["query"], c["key_cache"], c["value_cache"], c["block_tables"],
+                                 c["seq_lens"], c["page_size"], check=True, **kw)
+
+
+def oracle(c):
+    return paged_mtp_attention_reference(c["query"], c["key_cache"], c["value_cache"], c["block_tables"],
+                                         c["seq_lens"], c["page_size"], c["num_kv_heads"])
+
+
+@pytest.mark.parametrize("path", [p for p in GOLDEN if not p.stem.startswith("upstream_")],
+                         ids=lambda p: p.stem)
+def test_golden_vectors(sqa, path):
+    with np.load(path) as z:
+        c = {k: z[k] for k in z.files}
+    t = lambda k: torch.from_numpy(c[k]).cuda()  # noqa: E731
+    out = sqa.small_q_attention(t("query"), t("key_cache"), t("value_cache"), t("block_tables"),
+                                t("seq_lens"), int(c["page_size"]), check=True)
+    assert_close(out, c["expected"])
+
+
+PARITY = [
+    # (q_len, lens, hkv, page_mode)
+    (2, [33], 8, "random"),
+    (2, [1024], 8, "random"),
+    (2, [8192], 8, "unique"),
+    (4, [4, 16, 17, 1000], 8, "random"),
+    (4, [8192] * 4, 8, "random"),
+    (8, [33], 8, "random"),
+    (8, [8192], 8, "unique"),
+    (8, [2048, 8, 9, 300], 2, "random"),
+    (16, [16, 17, 31, 32, 33], 2, "random"),
+    (16, [4096], 8, "random"),
+    (1, [1, 2, 15, 16, 17, 500], 4, "random"),
+    (3, [3, 100, 257], 8, "random"),
+    (5, [5, 64, 1023], 2, "random"),
+    (12, [12, 200, 777], 2, "random"),
+    (2, [1024] * 16, 8, "shared"),
+]
+
+
+@pytest.mark.parametrize("q_len,lens,hkv,page_mode", PARITY,
+                         ids=[f"q{q}-n{len(l)}-kv{max(l)}-h{h}-{m}" for q, l, h, m in PARITY])
+def test_parity_vs_oracle(sqa, q_len, lens, hkv, page_mode):
+    c = case(q_len, lens, hkv=hkv, page_mode=page_mode, seed=len(lens) * 100 + q_len)
+    assert_close(run(sqa, c), oracle(c))
+
+
+@pytest.mark.parametrize("num_ctas", [1, 2, 3, 7, 64, 148, 296, 1000])
+def test_forced_splits_merge(sqa, num_ctas):
+    """Every CTA count splits segments differently; all must give the same answer."""
+    c = case(4, [40, 700, 16, 1500, 4], hkv=2, seed=7)
+    ref = oracle(c)
+    assert_close(run(sqa, c, num_ctas=num_ctas, min_pages_per_cta=1), ref)
+
+
+def test_outlier_keys_softmax_range(sqa):
+    c = case(4, [3000, 517, 9000], seed=11, k_outlier_frac=0.05)
+    assert_close(run(sqa, c), oracle(c))
+
+
+def test_max_seq_len_hint_does_not_change_result(sqa):
+    c = case(8, [1000, 2000], hkv=2, seed=3)
+    a = run(sqa, c)
+    b = run(sqa, c, max_seq_len=2000)
+    assert_close(a, oracle(c))
+    assert_close(b, oracle(c))
+
+
+@pytest.mark.parametrize("q_len", [1, 2, 4, 8, 16])
+def test_one_hot_indexing_exact(sqa, q_len):
+    """Q = K = 0 and V[t, d] = 16 * (d == t): output bin d is 16 / visible
+    when token d is visible to the row.  A wrong page, slot or mask moves a
+    bin by >= 0.125."""
+    from tests.test_oracle_known import one_hot_case
+
+    lens = [q_len, 17, 33, 64, 100, 128]
+    q, k, v, table, lens_np, expected = one_hot_case(q_len, lens, num_kv_heads=2, seed=q_len)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()  # noqa: E731
+    out = sqa.small_q_attention(t(q), t(k), t(v), t(table), t(lens_np), 16, check=True)
+    assert_close(out, expected)
+    # exactness: every bin is 16/visible or 0; fp16 rounding is the only error
+    np.testing.assert_allclose(out.float().cpu().numpy(), expected, rtol=2e-3, atol=1e-3)
+
+
+def test_nan_beyond_sequence_end_is_never_used(sqa):
+    """Slots past seq_len in the last page hold NaN: the output must not see them."""
+    c = case(4, [37, 50, 16], hkv=2, seed=5)
+    ref = oracle(c)
+    kc, vc = c["key_cache"].clone(), c["value_cache"].clone()
+    table = c["block_tables"].cpu()
+    for b, n in enumerate(c["lens"]):
+        last = int(table[b, (n - 1) // 16])
+        if n % 16:
+            kc[last, n % 16:] = float("nan")
+            vc[last, n % 16:] = float("nan")
+    out = sqa.small_q_attention(c["query"], kc, vc, c["block_tables"], c["seq_lens"], 16, check=True)
+    assert_close(out, ref)
+
+
+def test_page_permutation_is_bit_exact(sqa):
+    """Moving pages to other physical slots (and updating the table) must not
+    change a single bit of the output."""
+    c = case(8, [3000, 1200], hkv=8, seed=9, pool_factor=2.0)
+    a = run(sqa, c)
+    pool = c["key_cache"].shape[0]
+    perm = torch.randperm(pool, generator=torch.Generator().manual_seed(1))
+    inv = torch.empty_like(perm)
+    inv[perm] = torch.arange(pool)
+    kc = c["key_cache"][perm.cuda()].contiguous()  # new slot i holds old page perm[i]
+    vc = c["value_cache"][perm.cuda()].contiguous()
+    table = c["block_tables"].clone()
+    n_used = [(n + 15) // 16 for n in c["lens"]]
+    for b, n in enumerate(n_used):
+        table[b, :n] = inv.cuda()[table[b, :n].long()].to(torch.int32)
+    b_out = sqa.small_q_attention(c["query"], kc, vc, table, c["seq_lens"], 16, check=True)
+    assert torch.equal(a, b_out)
+
+
+def test_partial_shards_merge_to_whole(sqa):
+    """Split one sequence's pages into 4 shards (last shard shorter than q_len),
+    run the shard form on each and merge: equals the whole operator."""
+    q_len, n, hkv = 16, 5000, 8
+    c = case(q_len, [n], hkv=hkv, seed=21, pool_factor=1.0)
+    ref = oracle(c)
+    pages = (n + 15) // 16
+    cuts = [0, 100, 200, 312, pages]  # tokens [4992, 5000) in the last shard: 8 < q_len
+    table = c["block_tables"]
+    parts_o, parts_lse = [], []
+    for lo, hi in zip(cuts[:-1], cuts[1:]):
+        held = min(n, hi * 16) - lo * 16
+        shard_table = table[:, lo:hi].contiguous()
+        seq = torch.tensor([held], dtype=torch.int32, device="cuda")
+        mlen = torch.tensor([n - lo * 16], dtype=torch.int32, device="cuda")
+        o, lse = sqa.small_q_attention_partial(c["query"], c["key_cache"], c["value_cache"], shard_table,
+                                               seq, 16, mask_lens=mlen, check=True)
+        ro, rl = paged_mtp_attention_partial(c["query"], c["key_cache"], c["value_cache"], shard_table, seq,
+                                             mlen, 16, hkv)
+        assert_close(o, ro)
+        lse_np = lse.cpu().numpy()
+        assert np.array_equal(np.isneginf(lse_np), np.isneginf(rl))
+        fin = np.isfinite(rl)
+        np.testing.assert_allclose(lse_np[fin], rl[fin], rtol=1e-4, atol=1e-3)
+        parts_o.append(o)
+        parts_lse.append(lse)
+    merged = sqa.merge_partials(torch.stack(parts_o), torch.stack(parts_lse))
+    assert_close(merged, ref)
+    ro, _ = oracle_merge([p.cpu().numpy() for p in parts_o], [p.cpu().numpy() for p in parts_lse])
+    assert_close(merged, ro)
+
+
+def test_forward_v3_compat(sqa):
+    from small_q_attention_b200.cuda import forward_v3, forward_v4, forward_v5
+
+    c = case(4, [1024, 33], seed=13)
+    ref = oracle(c)
+    args = (c["query"], c["key_cache"], c["value_cache"], c["block_tables"], c["seq_lens"], 16)
+    assert_close(forward_v3(*args, 512, 1024), ref)
+    assert_close(forward_v4(*args), ref)
+    assert_close(forward_v5(*args, 256, 4), ref)
+    with pytest.raises(ValueError):
+        forward_v3(*args, 0)
+
+
+def test_device_status_errors(sqa):
+    c = case(4, [40, 20], hkv=2, seed=17)
+    bad = c["block_tables"].clone()
+    bad[1, 0] = c["key_cache"].shape[0] + 5
+    with pytest.raises(IndexError):
+        sqa.small_q_attention(c["query"], c["key_cache"], c["value_cache"], bad, c["seq_lens"], 16, check=True)
+    short = torch.tensor([40, 3], dtype=torch.int32, device="cuda")
+    with pytest.raises(ValueError):
+        sqa.small_q_attention(c["query"], c["key_cache"], c["value_cache"], c["block_tables"], short, 16,
+                              check=True)
+    too_long = torch.tensor([40, 16 * c["block_tables"].shape[1] + 1], dtype=torch.int32, device="cuda")
+    with pytest.raises(ValueError):
+        sqa.small_q_attention(c["query"], c["key_cache"], c["value_cache"], c["block_tables"], too_long, 16,
+                              check=True)
+    # the status word was cleared by each check: a good call passes
+    assert_close(run(sqa, c), oracle(c))
+
+
+def test_python_boundary_errors(sqa):
+    c = case(2, [64], hkv=2, seed=1)
+    args = [c["query"], c["key_cache"], c["value_cache"], c["block_tables"], c["seq_lens"], 16]
+    with pytest.raises(ValueError):
+        sqa.small_q_attention(c["query"].float(), *args[1:])
+    with pytest.raises(ValueError):
+        sqa.small_q_attention(c["query"].cpu(), *args[1:])
+    with pytest.raises(ValueError):
+        sqa.small_q_attention(*args[:5], 8)
+    with pytest.raises(ValueError):
+        sqa.small_q_attention(c["query"][:, :, :4].contiguous(), *args[1:])  # group 2
+    with pytest.raises(ValueError):
+        big = torch.zeros(1, 17, 8, 128, dtype=torch.float16, device="cuda")
+        sqa.small_q_attention(big, *args[1:])
+
+
+def test_non_default_stream_and_out(sqa):
+    c = case(8, [777, 1500], hkv=8, seed=23)
+    ref = oracle(c)
+    s = torch.cuda.Stream()
+    out = torch.empty_like(c["query"])
+    with torch.cuda.stream(s):
+        r = sqa.small_q_attention(c["query"], c["key_cache"], c["value_cache"], c["block_tables"],
+                                  c["seq_lens"], 16, out=out)
+    s.synchronize()
+    assert r is out
+    assert_close(out, ref)
+
+
+def test_repeated_calls_are_deterministic(sqa):
+    c = case(4, [5000, 300, 2000], seed=29)
+    a = run(sqa, c)
+    for _ in range(3):
+        assert torch.equal(a, run(sqa, c))

@@ -1,0 +1,115 @@
+"""The C-ABI library loads on any host and exports what ``include/*.h`` declares.
+
+No kernel runs here: every call below is rejected by host-side validation
+before any CUDA work, so these tests need no GPU.
+"""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from small_q_attention_b200 import _native, build
+
+    build.build()  # no-op when the in-tree library is up to date
+    return _native.library()
+
+
+def declared_symbols():
+    names = []
+    for h in (ROOT / "include").glob("*.h"):
+        names += re.findall(r"^SQA_API\s+[\w\s\*]+?\b(sqa_\w+)\s*\(", h.read_text(), flags=re.M)
+    return sorted(set(names))
+
+
+def test_header_declares_the_entry_points():
+    names = declared_symbols()
+    assert {"sqa_forward", "sqa_workspace_bytes", "sqa_merge_partials", "sqa_status_string"} <= set(names)
+
+
+def test_every_declared_symbol_is_exported(lib):
+    from small_q_attention_b200 import _native
+
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+    assert set(declared_symbols()) <= set(_native.EXPORTED_SYMBOLS)
+
+
+def test_abi_version_and_status_strings(lib):
+    assert lib.sqa_abi_version() == 100
+    for code in range(6):
+        assert lib.sqa_status_string(code).decode()
+    assert lib.sqa_status_string(99).decode() == "unknown status"
+
+
+def good_args():
+    from small_q_attention_b200._native import SqaArgs
+
+    a = SqaArgs()
+    a.query = a.key_cache = a.value_cache = a.block_tables = a.seq_lens = a.out = 256
+    a.batch, a.q_len, a.num_q_heads, a.num_kv_heads = 4, 4, 32, 8
+    a.head_dim, a.page_size, a.num_pages, a.max_pages = 128, 16, 1024, 512
+    return a
+
+
+@pytest.mark.parametrize("field,value,code", [
+    ("head_dim", 64, 2), ("page_size", 32, 2), ("num_q_heads", 16, 2), ("q_len", 17, 2),
+    ("q_len", 0, 1), ("num_pages", 0, 1), ("max_pages", 0, 1), ("batch", -1, 1), ("num_ctas", -1, 1),
+])
+def test_forward_rejects_bad_shapes(lib, field, value, code):
+    a = good_args()
+    setattr(a, field, value)
+    assert lib.sqa_forward(ctypes.byref(a), None, 0, None) == code
+    st = ctypes.c_int(-1)
+    assert lib.sqa_workspace_bytes(ctypes.byref(a), 0, ctypes.byref(st)) == 0
+    assert st.value == code
+
+
+def test_forward_rejects_null_and_misaligned_pointers(lib):
+    a = good_args()
+    a.query = None
+    assert lib.sqa_forward(ctypes.byref(a), None, 0, None) == 1
+    a = good_args()
+    a.key_cache = 258  # not 16-byte aligned
+    assert lib.sqa_forward(ctypes.byref(a), None, 0, None) == 1
+    a = good_args()
+    a.out_partial = 512  # both output modes at once
+    a.out_lse = 1024
+    assert lib.sqa_forward(ctypes.byref(a), None, 0, None) == 1
+    assert lib.sqa_forward(None, None, 0, None) == 1
+
+
+def test_merge_rejects_bad_arguments(lib):
+    assert lib.sqa_merge_partials(None, None, 2, 10, None, None, None, None) == 1
+    assert lib.sqa_merge_partials(256, 256, 0, 10, 256, None, None, None) == 1
+    assert lib.sqa_merge_partials(256, 256, 2, 10, None, None, None, None) == 1
+    assert lib.sqa_merge_partials(258, 256, 2, 10, 256, None, None, None) == 1
+
+
+def test_python_layer_maps_codes_to_exceptions():
+    from small_q_attention_b200 import _native
+
+    with pytest.raises(ValueError):
+        _native.check(2, "x")
+    with pytest.raises(RuntimeError):
+        _native.check(4, "x")
+    _native.check(0, "x")
+
+
+def test_operator_requires_cuda_without_fallback():
+    torch = pytest.importorskip("torch")
+    if torch.cuda.is_available():
+        pytest.skip("this host has a GPU")
+    from small_q_attention_b200 import small_q_attention
+
+    q = torch.zeros(1, 2, 32, 128, dtype=torch.float16)
+    cache = torch.zeros(4, 16, 8, 128, dtype=torch.float16)
+    with pytest.raises(RuntimeError):
+        small_q_attention(q, cache, cache, torch.zeros(1, 4, dtype=torch.int32),
+                          torch.tensor([32], dtype=torch.int32), 16)
