@@ -143,6 +143,29 @@ SQA_API int sqa_read_device_status(void* workspace, uint32_t* device_bits, int c
 /* Zero a freshly allocated workspace's status word (asynchronous). */
 SQA_API int sqa_workspace_init(void* workspace, size_t workspace_bytes, void* stream);
 
+/* Size of the scratch array built into the library for sqa_forward_noalloc. */
+#define SQA_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+/* sqa_forward for callers that cannot allocate device memory: the workspace
+ * comes from a SQA_NOALLOC_SCRATCH_BYTES array of device memory inside this
+ * library instead of from the caller.  Callers that cannot allocate include
+ * bindings that call this C ABI directly from a language without a CUDA
+ * allocator, and serving engines that give almost all of HBM to their
+ * KV-cache pool and forbid allocations (which could fail, and which
+ * synchronise the device) in the middle of a decode step.
+ * - Every GPU that loads the library holds the array until the process exits.
+ * - The first call with a device current looks up the array's device address
+ *   on that device; make that first call before any stream capture.
+ * - Shapes whose sqa_workspace_bytes() exceeds SQA_NOALLOC_SCRATCH_BYTES are
+ *   rejected with SQA_ERR_WORKSPACE_TOO_SMALL.
+ * - All calls share the one array: calls that overlap on the GPU (other
+ *   streams, other threads) race and must be serialised by the caller.
+ * - The device status bits are cleared at the start of every call and are not
+ *   reported; host-side validation is the same as sqa_forward's.
+ * No counterpart in the reference (its launcher allocates scratch per call
+ * with torch::empty, csrc/small_q_attention_ext.cu:1183-1185). */
+SQA_API int sqa_forward_noalloc(const sqa_args* args, void* stream);
+
 /* Static description of a status code. */
 SQA_API const char* sqa_status_string(int status);
 

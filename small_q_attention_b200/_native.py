@@ -30,6 +30,7 @@ EXPORTED_SYMBOLS = (
     "sqa_workspace_bytes",
     "sqa_forward",
     "sqa_forward_timed",
+    "sqa_forward_noalloc",
     "sqa_merge_partials",
     "sqa_read_device_status",
     "sqa_workspace_init",
@@ -90,6 +91,8 @@ def library(path: Path | None = None):
         lib.sqa_forward.restype = ctypes.c_int
         lib.sqa_forward_timed.argtypes = [ctypes.POINTER(SqaArgs), vp, sz, vp, vp, vp]
         lib.sqa_forward_timed.restype = ctypes.c_int
+        lib.sqa_forward_noalloc.argtypes = [ctypes.POINTER(SqaArgs), vp]
+        lib.sqa_forward_noalloc.restype = ctypes.c_int
         lib.sqa_merge_partials.argtypes = [vp, vp, i32, i64, vp, vp, vp, vp]
         lib.sqa_merge_partials.restype = ctypes.c_int
         lib.sqa_read_device_status.argtypes = [vp, ctypes.POINTER(ctypes.c_uint32), ctypes.c_int, vp]

@@ -20,7 +20,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB_DIR = PKG / "_lib"
 LIB_PATH = LIB_DIR / "libsqa_b200.so"
-SOURCES = ["sqa_split_kv.cu", "sqa_merge.cu", "sqa_api.cu"]
+SOURCES = ["sqa_split_kv.cu", "sqa_merge.cu", "sqa_api.cu", "sqa_noalloc.cu"]
 HEADERS = ["sqa_internal.h", "sqa_ptx.cuh"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [

@@ -1,0 +1,97 @@
+"""sqa_forward_noalloc: the entry point for callers that cannot allocate device memory.
+
+Callers such as a direct C-ABI binding with no CUDA allocator of its own, or a
+serving engine that has handed nearly all of HBM to its KV-cache pool, cannot
+provide the workspace sqa_forward needs; sqa_forward_noalloc uses a scratch
+array built into the library instead.  These tests call it through the C ABI
+(ctypes) and compare its output with sqa_forward's, within the parity
+tolerance of the other GPU tests, on two calls in a row with different shapes
+(the second call runs on scratch that still holds the first call's data).
+This file is named so that pytest collects it last.
+"""
+
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+ATOL = 2e-2
+RTOL = 1e-2
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from small_q_attention_b200 import _native
+
+    return _native.library()
+
+
+def _case(q_len, lens, seed):
+    from small_q_attention_b200.workloads import make_case
+
+    return make_case(len(lens), q_len, lens, hkv=8, pool_factor=1.5, seed=seed, device="cuda",
+                     gen_device="cpu")
+
+
+def _args(c, out):
+    from small_q_attention_b200.attention import _fill_args
+
+    a = _fill_args(c["query"], c["key_cache"], c["value_cache"], c["block_tables"], c["seq_lens"], None,
+                   0, 0, 0)
+    a.out = out.data_ptr()
+    return a
+
+
+def _with_workspace(lib, c):
+    """Output of the existing entry point, sqa_forward, with a caller workspace."""
+    out = torch.empty_like(c["query"])
+    a = _args(c, out)
+    st = ctypes.c_int(0)
+    need = lib.sqa_workspace_bytes(ctypes.byref(a), torch.cuda.current_device(), ctypes.byref(st))
+    assert st.value == 0
+    ws = torch.zeros(need, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    assert lib.sqa_forward(ctypes.byref(a), ctypes.c_void_p(ws.data_ptr()), ctypes.c_size_t(need),
+                           ctypes.c_void_p(stream)) == 0
+    torch.cuda.synchronize()
+    return out
+
+
+def _no_alloc(lib, c):
+    out = torch.empty_like(c["query"])
+    a = _args(c, out)
+    stream = torch.cuda.current_stream().cuda_stream
+    assert lib.sqa_forward_noalloc(ctypes.byref(a), ctypes.c_void_p(stream)) == 0
+    torch.cuda.synchronize()
+    return out
+
+
+def _assert_close(out, ref):
+    o, r = out.float().cpu().numpy(), ref.float().cpu().numpy()
+    assert np.isfinite(o).all()
+    err = np.abs(o - r)
+    assert (err <= ATOL + RTOL * np.abs(r)).all() and err.max() <= ATOL, f"max err {err.max():.3e}"
+
+
+def test_no_alloc_matches_workspace_entry_two_calls(lib):
+    first = _case(8, [8192, 777, 33, 4000], seed=31)     # split sequences -> merge partials
+    second = _case(2, [1024, 16, 5000], seed=32)          # other shape, stale scratch from the first
+    for c in (first, second):
+        _assert_close(_no_alloc(lib, c), _with_workspace(lib, c))
+
+
+def test_no_alloc_rejects_shapes_beyond_the_scratch(lib):
+    from small_q_attention_b200._native import SQA_ERR_WORKSPACE_TOO_SMALL, SqaArgs
+
+    a = SqaArgs()
+    dummy = torch.zeros(1024, dtype=torch.float16, device="cuda")
+    a.query = a.key_cache = a.value_cache = a.block_tables = a.seq_lens = a.out = dummy.data_ptr()
+    a.batch, a.q_len, a.num_q_heads, a.num_kv_heads = 4096, 16, 32, 8
+    a.head_dim, a.page_size, a.num_pages, a.max_pages = 128, 16, 1 << 20, 64
+    stream = torch.cuda.current_stream().cuda_stream
+    assert lib.sqa_forward_noalloc(ctypes.byref(a), ctypes.c_void_p(stream)) == SQA_ERR_WORKSPACE_TOO_SMALL
