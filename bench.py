@@ -450,32 +450,41 @@ def run_matrix(args):
     torch.cuda.set_device(0)
     peak_gbs, peak_src = _peaks()
     rows = []
+    # one explicit workspace, large enough for every case (16 KV-head segments x 64 rows worst case)
+    ws = torch.zeros(64 << 20, dtype=torch.uint8, device="cuda")
     cases = [("matrix", c) for c in matrix_cases()] + [(n, None) for n in CONFIGS]
     if args.only:
         cases = [(n, c) for n, c in cases if n in args.only or (c and f"q{c['q_len']}" in args.only)]
     for name, c in cases:
         if c is None:
-            inst = [make_config(name, seed=s) for s in range(2)]
+            first = make_config(name, seed=0)
             label = name
         else:
-            inst = [make_case(c["batch"], c["q_len"], [c["kv_len"]] * c["batch"], pool_factor=1.0,
-                              page_mode=args.page_mode, seed=s) for s in range(2)]
+            first = make_case(c["batch"], c["q_len"], [c["kv_len"]] * c["batch"], pool_factor=1.0,
+                              page_mode=args.page_mode, seed=0)
             label = f"q{c['q_len']}_kv{c['kv_len']}_b{c['batch']}"
-        nb = _case_bytes(inst[0])
-        # enough distinct replicas that consecutive calls do not hit in L2
-        n_rep = max(2, min(8, math.ceil(400e6 / max(1, inst[0]["key_cache"].numel() * 4))))
-        while len(inst) < n_rep:
-            inst.append(inst[len(inst) % 2])
+        nb = _case_bytes(first)
+        # distinct input copies so that consecutive calls never find K/V in L2:
+        # at least 2 and enough for >= 400 MB of caches in rotation (at most 64)
+        cache_bytes = first["key_cache"].numel() * 4
+        n_rep = max(2, min(64, math.ceil(400e6 / max(1, cache_bytes))))
+        inst = [first]
+        for s_ in range(1, n_rep):
+            if c is None:
+                inst.append(make_config(name, seed=s_))
+            else:
+                inst.append(make_case(c["batch"], c["q_len"], [c["kv_len"]] * c["batch"], pool_factor=1.0,
+                                      page_mode=args.page_mode, seed=s_))
         outs = [torch.empty_like(x["query"]) for x in inst]
         fn = lambda i: sqa.small_q_attention(  # noqa: E731
             inst[i]["query"], inst[i]["key_cache"], inst[i]["value_cache"], inst[i]["block_tables"],
-            inst[i]["seq_lens"], 16, max(inst[i]["lens"]), out=outs[i])
+            inst[i]["seq_lens"], 16, max(inst[i]["lens"]), out=outs[i], workspace=ws)
         for i in range(5):
             fn(i % len(inst))
         torch.cuda.synchronize()
         s = torch.cuda.Stream()
         g = torch.cuda.CUDAGraph()
-        reps = 20
+        reps = max(20, n_rep)  # every replica once per replay
         with torch.cuda.graph(g, stream=s):
             for i in range(reps):
                 fn(i % len(inst))
@@ -490,12 +499,17 @@ def run_matrix(args):
             torch.cuda.synchronize()
             samples.append(e0.elapsed_time(e1) * 1e3 / reps)
         us = statistics.median(samples)
+        bits = sqa.read_device_status(ws.data_ptr(), clear=True)
+        if bits:
+            detail = int(ws[4:8].view(torch.int32).item())
+            raise RuntimeError(f"{label}: device status bits {bits:#x}, detail {detail:#010x}")
         row = {"case": label, "q_len": inst[0]["query"].shape[1], "batch": inst[0]["query"].shape[0],
                "kv_len_max": max(inst[0]["lens"]), "page_mode": args.page_mode if c else "random",
                "p50_us": round(us, 3), "min_us": round(min(samples), 3), "alg_bytes": nb,
                "tb_s": round(nb / (us * 1e-6) / 1e12, 4),
                "roofline_frac": round(nb / (us * 1e-6) / 1e9 / peak_gbs, 4), "peak_gbs": peak_gbs,
-               "peak_source": peak_src, "n_gpus": 1, "timing": "CUDA graph of 20 calls, median of 5"}
+               "peak_source": peak_src, "n_gpus": 1, "replicas": n_rep,
+               "timing": f"CUDA graph of {reps} back-to-back calls over rotating replicas, median of 5"}
         rows.append(row)
         print(json.dumps(row), flush=True)
         del g, inst, outs

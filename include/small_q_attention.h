@@ -66,6 +66,8 @@ typedef enum sqa_status {
 #define SQA_DEV_SEQ_TOO_LONG 2u    /* seq_lens[b] > 16 * max_pages: clamped to the table */
 #define SQA_DEV_SEQ_TOO_SHORT 4u   /* seq_lens[b] < q_len (full mode only)              */
 #define SQA_DEV_BAD_PAGE 8u        /* a page id outside [0, num_pages): read as page 0  */
+#define SQA_DEV_CHECK 16u          /* a -DSQA_DEBUG_CHECKS bounds check failed; the word
+                                      after the status word holds (check << 24) | index  */
 
 typedef struct sqa_args {
   const void* query;           /* fp16 [batch, q_len, num_q_heads, 128]           */

@@ -7,10 +7,13 @@ load, every operator raises ``RuntimeError``; there is no CPU fallback.
 from __future__ import annotations
 
 import ctypes
+import os
 import threading
 from pathlib import Path
 
-LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libsqa_b200.so"
+# SQA_LIB_PATH selects another build of the library (for example one compiled
+# with -DSQA_DEBUG_CHECKS); the default is the in-tree release build.
+LIB_PATH = Path(os.environ.get("SQA_LIB_PATH") or Path(__file__).resolve().parent / "_lib" / "libsqa_b200.so")
 
 # status codes (sqa_status)
 SQA_OK = 0
@@ -25,6 +28,7 @@ DEV_TIMEOUT = 1
 DEV_SEQ_TOO_LONG = 2
 DEV_SEQ_TOO_SHORT = 4
 DEV_BAD_PAGE = 8
+DEV_CHECK = 16
 
 EXPORTED_SYMBOLS = (
     "sqa_workspace_bytes",

@@ -4,6 +4,7 @@
 // launch from the SM count and the shapes, encodes the two TMA tensor maps
 // over the paged caches and launches the kernels on the caller's stream.
 // Errors are status codes; no exception leaves this file.
+#include <cstdio>
 #include <mutex>
 
 #include "../../include/small_q_attention.h"
@@ -71,6 +72,25 @@ bool encode_cache_map(CUtensorMap* map, const void* base, int num_pages, int hkv
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Debug builds synchronise after each launch (outside stream capture) and
+// report which kernel failed, so a device fault is tied to one launch.
+#ifdef SQA_DEBUG_CHECKS
+bool debug_sync(cudaStream_t stream, const char* what, int grid, int smem, const sqa_args* a) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return true;
+  const cudaError_t e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) {
+    fprintf(stderr, "sqa debug: %s failed: %s (grid %d smem %d batch %d q_len %d hkv %d pages %d max_pages %d)\n",
+            what, cudaGetErrorString(e), grid, smem, a->batch, a->q_len, a->num_kv_heads, a->num_pages,
+            a->max_pages);
+    return false;
+  }
+  return true;
+}
+#else
+inline bool debug_sync(cudaStream_t, const char*, int, int, const sqa_args*) { return true; }
+#endif
+
 struct Plan {
   WarpShape shape;
   int grid;
@@ -115,7 +135,7 @@ int make_plan(const sqa_args* a, int device, Plan* plan) {
   Plan pl;
   pl.shape = warp_shape_for(a->q_len);
   const int fixed = split_kv_smem_bytes(pl.shape, 0);
-  pl.stages = (kSmemPerCta - fixed) / (kStageBytes + 16);
+  pl.stages = (kSmemPerCta - fixed) / (kStageBytes + 24);
   if (pl.stages > kMaxStages) pl.stages = kMaxStages;
   pl.smem = split_kv_smem_bytes(pl.shape, pl.stages);
   pl.segments = a->batch * a->num_kv_heads;
@@ -231,12 +251,14 @@ int forward_impl(const sqa_args* a, void* workspace, size_t workspace_bytes, voi
   p.max_pages = a->max_pages;
   p.num_pages = a->num_pages;
   p.num_stages = pl.stages;
+  p.num_pieces = pl.pieces;
   p.scale_log2 = 1.4426950408889634f / sqrtf((float)kHeadDim);
 
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_ptr);
   if (ev_before && cudaEventRecord(reinterpret_cast<cudaEvent_t>(ev_before), stream) != cudaSuccess)
     return SQA_ERR_CUDA;
   if (launch_split_kv(p, tm_k, tm_v, pl.grid, pl.smem, stream) != cudaSuccess) return SQA_ERR_CUDA;
+  if (!debug_sync(stream, "split-KV kernel", pl.grid, pl.smem, a)) return SQA_ERR_CUDA;
   if (ev_after && cudaEventRecord(reinterpret_cast<cudaEvent_t>(ev_after), stream) != cudaSuccess)
     return SQA_ERR_CUDA;
 
@@ -248,8 +270,9 @@ int forward_impl(const sqa_args* a, void* workspace, size_t workspace_bytes, voi
   m.out = p.out;
   m.out_o = p.out_o;
   m.out_lse = p.out_lse;
+  m.status = p.status;
   m.rows = 0;
-  m.num_parts = 0;
+  m.num_parts = pl.pieces;
   m.piece_rows = pl.shape.rows_pad;
   m.batch = a->batch;
   m.q_len = a->q_len;
@@ -257,6 +280,7 @@ int forward_impl(const sqa_args* a, void* workspace, size_t workspace_bytes, voi
   m.hkv = a->num_kv_heads;
   m.max_pages = a->max_pages;
   if (launch_segment_merge(m, pl.shape.rows_pad, stream) != cudaSuccess) return SQA_ERR_CUDA;
+  if (!debug_sync(stream, "merge kernel", pl.segments, 0, a)) return SQA_ERR_CUDA;
   return SQA_OK;
 }
 }  // namespace

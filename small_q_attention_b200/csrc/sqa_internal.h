@@ -49,6 +49,7 @@ struct SplitKvParams {
   unsigned int* status;
   int batch, q_len, hq, hkv, max_pages, num_pages;
   int num_stages;
+  int num_pieces;               // workspace partial slots
   float scale_log2;             // head_dim^-0.5 * log2(e)
 };
 
@@ -57,11 +58,12 @@ struct MergeParams {
   const float* parts_lse;
   const int2* seg_info;         // nullptr: every segment has pieces [0, num_parts)
   const int32_t* seq_lens;      // per-call merge: empty sequences are written as 0 / -inf
+  unsigned int* status;         // per-call merge: device status word
   __half* out;
   float* out_o;
   float* out_lse;
   long long rows;               // cross-device merge: total rows; per-call merge: unused
-  int num_parts;
+  int num_parts;                // cross-device merge: parts; per-call merge: workspace partial slots
   int piece_rows;               // rows per piece (rows_pad for the per-call merge)
   int batch, q_len, hq, hkv, max_pages;
 };

@@ -83,6 +83,7 @@ __global__ void __launch_bounds__(128) sqa_segment_merge_kernel(const MergeParam
   }
   const int2 info = p.seg_info[s];
   if (info.y <= 1) return;  // written directly by the split-KV kernel
+  if (!SQA_CHECK(info.x >= 0 && info.x + info.y <= p.num_parts, p.status, 8, s)) return;
   const size_t first = (size_t)info.x * p.piece_rows + row;
   merge_row(p.parts_o + first * kHeadDim, (size_t)p.piece_rows * kHeadDim, p.parts_lse + first,
             (size_t)p.piece_rows, info.y, out, out_o, out_lse);

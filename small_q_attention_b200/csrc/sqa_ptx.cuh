@@ -27,6 +27,23 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
   return t;
 }
 
+// Debug builds (-DSQA_DEBUG_CHECKS) verify every computed index before use.
+// A failed check sets SQA_DEV_CHECK in the status word, stores
+// (check << 24) | (index & 0xffffff) in the word after it (first failure
+// wins) and skips the access.  Release builds compile the checks away.
+#ifdef SQA_DEBUG_CHECKS
+__device__ __forceinline__ bool debug_check(bool ok, unsigned int* status, unsigned int check, long long index) {
+  if (!ok) {
+    atomicOr(status, 16u /* SQA_DEV_CHECK */);
+    atomicCAS(status + 1, 0u, (check << 24) | (unsigned int)(index & 0xffffff));
+  }
+  return ok;
+}
+#define SQA_CHECK(ok, status, check, index) debug_check((ok), (status), (check), (index))
+#else
+#define SQA_CHECK(ok, status, check, index) true
+#endif
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
@@ -72,7 +89,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // flag: once any thread has timed out, every later wait returns at once so
 // that all warps still reach the same named barriers and the kernel ends.
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
-                                                  volatile int* abort, unsigned int* status) {
+                                                  volatile int* abort, unsigned int* status,
+                                                  unsigned int debug_kind = 0, unsigned int debug_index = 0) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   for (uint32_t it = 1;; ++it) {
@@ -81,8 +99,33 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
     if ((it & 63u) == 0u && global_timer_ns() - t0 > kWaitLimitNs) {
       *abort = 1;
       atomicOr(status, 1u /* SQA_DEV_TIMEOUT */);
+#ifdef SQA_DEBUG_CHECKS
+      // first timeout wins: status[2..9] = 1, kind, cta, page counter, parity, warp, raw barrier word
+      if (atomicCAS(status + 2, 0u, 1u) == 0u) {
+        uint64_t raw;
+        asm volatile("ld.shared.b64 %0, [%1];" : "=l"(raw) : "r"(bar));
+        status[3] = debug_kind;
+        status[4] = blockIdx.x;
+        status[5] = debug_index;
+        status[6] = parity;
+        status[7] = threadIdx.x >> 5;
+        status[8] = (unsigned int)raw;
+        status[9] = (unsigned int)(raw >> 32);
+      }
+#endif
       return false;
     }
+  }
+}
+
+// Wait (bounded, ignoring the abort flag) for a phase that is known to have
+// been armed: used to drain this CTA's own bulk copies before it exits.
+__device__ __forceinline__ bool mbar_drain(uint32_t bar, uint32_t parity, uint64_t limit_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 63u) == 0u && global_timer_ns() - t0 > limit_ns) return false;
   }
 }
 

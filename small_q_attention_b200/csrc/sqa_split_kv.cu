@@ -139,15 +139,29 @@ __device__ __forceinline__ SegWalk first_segment(const SplitKvParams& p, const S
 }
 
 // ------------------------------------------------------------------ producer
+// Ring protocol.  Page i (the CTA's i-th page) goes to data stage i % S and
+// completes on full barrier i % (2S); its stage is released on empty barrier
+// i % S.  The token groups consume pages out of order, so one stage's
+// consecutive fills are waited on by different groups.  With full barriers
+// indexed modulo 2S, the previous fill of barrier i % 2S is page i - 2S, which
+// is always complete when page i is awaited (page i - S has been issued,
+// which needed page i - 2S consumed), so a parity wait sees only the two
+// phases it can tell apart.
+#ifdef SQA_DEBUG_CHECKS
+__shared__ volatile int debug_progress[4];
+#endif
+
 __device__ void producer_loop(const SplitKvParams& p, const Schedule& sch, const CUtensorMap* tm_k,
                               const CUtensorMap* tm_v, uint8_t* stages, uint64_t* full,
                               uint64_t* empty, volatile int* abort) {
   const int lane = threadIdx.x & 31;
   const uint64_t policy = l2_policy_evict_first();
+  const int S = p.num_stages;
   SegWalk w = first_segment(p, sch);
-  int slot = 0;
+  int slot = 0, fslot = 0;  // data stage i % S, full barrier i % 2S
   uint32_t phase = 0;
   unsigned int bad_page = 0;
+  int issued = 0;  // pages whose loads were issued (a prefix of the range)
   int unit = sch.start;
   while (unit < sch.end) {
     const int seg_end = w.seg_start + w.pages;
@@ -165,10 +179,31 @@ __device__ void producer_loop(const SplitKvParams& p, const Schedule& sch, const
           bad_page = 1;
           page = 0;  // never hand TMA a coordinate outside the pool
         }
-        if (lane == 0) {
-          const uint32_t e = smem_u32(empty + slot);
-          const uint32_t f = smem_u32(full + slot);
-          if (mbar_wait_bounded(e, phase ^ 1u, abort, p.status)) {
+        const bool in_range = SQA_CHECK(slot < S && fslot < 2 * S, p.status, 1, slot) &&
+                              SQA_CHECK(w.b < p.batch && w.h < p.hkv, p.status, 2, w.b) &&
+                              SQA_CHECK(w.pg + c0 + j < p.max_pages, p.status, 3, w.pg + c0 + j);
+        if (lane == 0 && in_range) {
+          const bool got = mbar_wait_bounded(smem_u32(empty + slot), phase ^ 1u, abort, p.status, 1, issued);
+#ifdef SQA_DEBUG_CHECKS
+          if (!got && p.status[2] == 1u && p.status[4] == blockIdx.x && atomicCAS(p.status + 10, 0u, 1u) == 0u) {
+            unsigned int fb = 0, eb = 0;  // phase bits of every barrier
+            for (int k2 = 0; k2 < 2 * S; ++k2) {
+              uint64_t r;
+              asm volatile("ld.shared.b64 %0, [%1];" : "=l"(r) : "r"(smem_u32(full + k2)));
+              fb |= (unsigned int)(r >> 63) << k2;
+            }
+            for (int k2 = 0; k2 < S; ++k2) {
+              uint64_t r;
+              asm volatile("ld.shared.b64 %0, [%1];" : "=l"(r) : "r"(smem_u32(empty + k2)));
+              eb |= (unsigned int)(r >> 63) << k2;
+            }
+            p.status[15] = fb;
+            p.status[16] = eb;
+            for (int k2 = 0; k2 < 4; ++k2) p.status[11 + k2] = debug_progress[k2];
+          }
+#endif
+          if (got) {
+            const uint32_t f = smem_u32(full + fslot);
             mbar_arrive_expect_tx(f, kStageBytes);
             const uint32_t dst = smem_u32(stages + (size_t)slot * kStageBytes);
             const int tok = page * kPageSize;
@@ -176,12 +211,14 @@ __device__ void producer_loop(const SplitKvParams& p, const Schedule& sch, const
             tma_load_3d(dst + 2048, tm_k, f, 64, w.h, tok, policy);
             tma_load_3d(dst + 4096, tm_v, f, 0, w.h, tok, policy);
             tma_load_3d(dst + 6144, tm_v, f, 64, w.h, tok, policy);
+            ++issued;
           }
         }
-        if (++slot == p.num_stages) {
+        if (++slot == S) {
           slot = 0;
           phase ^= 1u;
         }
+        if (++fslot == 2 * S) fslot = 0;
       }
       ids = ids_next;
     }
@@ -190,6 +227,17 @@ __device__ void producer_loop(const SplitKvParams& p, const Schedule& sch, const
     else w.pg += n;
   }
   if (__any_sync(0xffffffffu, bad_page) && lane == 0) atomicOr(p.status, 8u);  // SQA_DEV_BAD_PAGE
+  // No bulk copy may still be landing in this CTA's shared memory when it
+  // exits.  On the normal path the consumers have already waited for every
+  // page, so this returns at once; after an abort it bounds the wait.
+  if (lane == 0) {
+    const int bars = min(issued, 2 * S);
+    for (int k = 0; k < bars; ++k) {
+      const int last = k + 2 * S * ((issued - 1 - k) / (2 * S));  // last page on barrier k
+      if (!mbar_drain(smem_u32(full + k), (uint32_t)(last / (2 * S)) & 1u, 100000000ull))
+        atomicOr(p.status, 1u);  // SQA_DEV_TIMEOUT
+    }
+  }
 }
 
 // ------------------------------------------------------------------ consumers
@@ -216,8 +264,8 @@ __device__ void consumer_loop(const SplitKvParams& p, const Schedule& sch, uint8
   const int v_cb = (lane >> 3) & 1;                       // V: +1 chunk for matrices 1, 3
 
   SegWalk w = first_segment(p, sch);
-  int slot = 0;
-  uint32_t phase = 0;
+  int slot = 0, fslot = 0;  // data stage gi % S, full barrier gi % 2S
+  uint32_t fphase = 0;
   int gi = 0;  // CTA-wide page counter (selects the token group)
   int unit = sch.start;
   while (unit < sch.end) {
@@ -225,7 +273,7 @@ __device__ void consumer_loop(const SplitKvParams& p, const Schedule& sch, uint8
     const int seg_end = w.seg_start + w.pages;
     const int n = min(sch.end, seg_end) - unit;
     const bool whole = (unit == w.seg_start) && (seg_end <= sch.end);
-    if (tid == 0 && unit == w.seg_start) {
+    if (tid == 0 && unit == w.seg_start && SQA_CHECK(s < p.batch * p.hkv, p.status, 7, s)) {
       const int last_cta = (seg_end - 1) / sch.per_cta;
       p.seg_info[s] = make_int2((int)blockIdx.x + s, last_cta - (int)blockIdx.x + 1);
     }
@@ -267,14 +315,19 @@ __device__ void consumer_loop(const SplitKvParams& p, const Schedule& sch, uint8
 
     for (int j = 0; j < n; ++j, ++gi) {
       const int my_slot = slot;
-      const uint32_t my_phase = phase;
-      if (++slot == p.num_stages) {
-        slot = 0;
-        phase ^= 1u;
+      const int my_fslot = fslot;
+      const uint32_t my_fphase = fphase;
+      if (++slot == p.num_stages) slot = 0;
+      if (++fslot == 2 * p.num_stages) {
+        fslot = 0;
+        fphase ^= 1u;
       }
       if ((gi % WT) != tg) continue;
-
-      mbar_wait_bounded(smem_u32(full + my_slot), my_phase, abort, p.status);
+      if (!SQA_CHECK(my_slot < p.num_stages, p.status, 4, my_slot)) continue;
+#ifdef SQA_DEBUG_CHECKS
+      if (lane == 0) debug_progress[warp] = gi;
+#endif
+      mbar_wait_bounded(smem_u32(full + my_fslot), my_fphase, abort, p.status, 3, gi);
       uint8_t* st = stages + (size_t)my_slot * kStageBytes;
       const uint32_t k_base = smem_u32(st);
       const uint32_t v_base = k_base + 4096;
@@ -408,7 +461,8 @@ __device__ void consumer_loop(const SplitKvParams& p, const Schedule& sch, uint8
     named_bar_sync(1, kConsumerWarps * 32);
 
     const int piece = (int)blockIdx.x + s;
-    for (int item = tid; item < rows * 32; item += kConsumerWarps * 32) {
+    const bool piece_ok = whole || SQA_CHECK(piece < p.num_pieces, p.status, 5, piece);
+    for (int item = tid; piece_ok && item < rows * 32; item += kConsumerWarps * 32) {
       const int row = item >> 5;
       const int c4 = (item & 31) * 4;
       float mmax = -INFINITY;
@@ -434,6 +488,7 @@ __device__ void consumer_loop(const SplitKvParams& p, const Schedule& sch, uint8
       acc.w *= inv;
       const float lse = (L > 0.f) ? (mmax + __log2f(L)) * kLn2 : -INFINITY;
       const size_t out_row = (size_t)(w.b * p.q_len + (row >> 2)) * p.hq + w.h * kGroup + (row & 3);
+      if (!SQA_CHECK(out_row < (size_t)p.batch * p.q_len * p.hq, p.status, 6, (long long)out_row)) continue;
       if (whole) {
         if (p.out != nullptr) {
           uint2 h;
@@ -470,16 +525,14 @@ __global__ void __launch_bounds__(kThreads, 2)
   float* cbuf = reinterpret_cast<float*>(smem + (size_t)p.num_stages * kStageBytes);
   float* mbuf = cbuf + WT * ROWS_PAD * kCombineStride;
   float* lbuf = mbuf + WT * ROWS_PAD;
-  uint64_t* full = reinterpret_cast<uint64_t*>(lbuf + WT * ROWS_PAD);
-  uint64_t* empty = full + p.num_stages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(lbuf + WT * ROWS_PAD);  // 2S barriers
+  uint64_t* empty = full + 2 * p.num_stages;                           // S barriers
   Schedule* sch = reinterpret_cast<Schedule*>(empty + p.num_stages);
 
   const int warp = threadIdx.x >> 5;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < p.num_stages; ++i) {
-      mbar_init(smem_u32(full + i), 1);
-      mbar_init(smem_u32(empty + i), WR);
-    }
+    for (int i = 0; i < 2 * p.num_stages; ++i) mbar_init(smem_u32(full + i), 1);
+    for (int i = 0; i < p.num_stages; ++i) mbar_init(smem_u32(empty + i), WR);
     fence_mbar_init();
   }
   if (warp == kConsumerWarps && (threadIdx.x & 31) == 0) {
@@ -525,7 +578,7 @@ int split_kv_smem_bytes(const WarpShape& ws, int num_stages) {
          + num_stages * kStageBytes             // K/V ring
          + rows * kCombineStride * 4            // combine buffer
          + 2 * rows * 4                         // m, l
-         + 2 * num_stages * 8                   // full / empty barriers
+         + 3 * num_stages * 8                   // 2S full + S empty barriers
          + 64;                                  // schedule
 }
 

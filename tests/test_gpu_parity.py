@@ -268,3 +268,22 @@ def test_repeated_calls_are_deterministic(sqa):
     a = run(sqa, c)
     for _ in range(3):
         assert torch.equal(a, run(sqa, c))
+
+
+@pytest.mark.parametrize("q_len", [2, 4, 8])
+def test_pipeline_stress_large_pool(sqa, q_len):
+    """16 sequences of 8192 tokens from an 8192-page pool: under this much DRAM
+    traffic the page loads of the shared-memory ring complete out of order.
+    Repeated calls must leave the device status clean, agree bit for bit and
+    match the oracle on sampled sequences."""
+    from small_q_attention_b200.workloads import make_case
+
+    c = make_case(16, q_len, [8192] * 16, hkv=8, pool_factor=1.0, seed=77, device="cuda")
+    first = run(sqa, c, max_seq_len=8192)
+    for _ in range(6):
+        assert torch.equal(first, run(sqa, c, max_seq_len=8192))
+    kc, vc = c["key_cache"].cpu(), c["value_cache"].cpu()
+    for b in (0, 7, 15):
+        ref = paged_mtp_attention_reference(c["query"][b:b + 1], kc, vc, c["block_tables"][b:b + 1],
+                                            c["seq_lens"][b:b + 1], 16, 8)
+        assert_close(first[b:b + 1], ref)
