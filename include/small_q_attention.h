@@ -142,7 +142,7 @@ SQA_API int sqa_merge_partials(const float* parts_o, const float* parts_lse, int
  * SQA_DEV_* bits; returns SQA_ERR_DEVICE when any bit is set. */
 SQA_API int sqa_read_device_status(void* workspace, uint32_t* device_bits, int clear, void* stream);
 
-/* Zero a freshly allocated workspace's status word (asynchronous). */
+/* Zero a workspace before its first use (asynchronous). */
 SQA_API int sqa_workspace_init(void* workspace, size_t workspace_bytes, void* stream);
 
 /* Size of the scratch array built into the library for sqa_forward_noalloc. */

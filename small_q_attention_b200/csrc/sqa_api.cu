@@ -98,7 +98,7 @@ struct Plan {
   int smem;
   int segments;
   int pieces;
-  size_t off_seg, off_lse, off_o, bytes;
+  size_t off_seg, off_lse, off_o, off_timeline = 0, bytes;
 };
 
 int validate(const sqa_args* a) {
@@ -160,6 +160,11 @@ int make_plan(const sqa_args* a, int device, Plan* plan) {
   pl.off_lse = align_up(pl.off_seg + (size_t)pl.segments * sizeof(int2));
   pl.off_o = align_up(pl.off_lse + (size_t)pl.pieces * pl.shape.rows_pad * sizeof(float));
   pl.bytes = align_up(pl.off_o + (size_t)pl.pieces * pl.shape.rows_pad * kHeadDim * sizeof(float));
+#ifdef SQA_DEBUG_TIMELINE
+  // trace buffer at the end: 8 stamps per split CTA, 4 per merge CTA
+  pl.off_timeline = pl.bytes;
+  pl.bytes = align_up(pl.bytes + ((size_t)pl.grid * 8 + (size_t)pl.segments * 16 * 4) * 8);
+#endif
   *plan = pl;
   return SQA_OK;
 }
@@ -205,7 +210,7 @@ size_t sqa_workspace_bytes(const sqa_args* args, int device, int* status) {
 
 int sqa_workspace_init(void* workspace, size_t workspace_bytes, void* stream) {
   if (!workspace || workspace_bytes < kAlign) return SQA_ERR_INVALID_ARGUMENT;
-  return cudaMemsetAsync(workspace, 0, kAlign, reinterpret_cast<cudaStream_t>(stream)) == cudaSuccess
+  return cudaMemsetAsync(workspace, 0, workspace_bytes, reinterpret_cast<cudaStream_t>(stream)) == cudaSuccess
              ? SQA_OK
              : SQA_ERR_CUDA;
 }
@@ -252,6 +257,7 @@ int forward_impl(const sqa_args* a, void* workspace, size_t workspace_bytes, voi
   p.num_pages = a->num_pages;
   p.num_stages = pl.stages;
   p.num_pieces = pl.pieces;
+  p.timeline = pl.off_timeline ? reinterpret_cast<unsigned long long*>(ws + pl.off_timeline) : nullptr;
   p.scale_log2 = 1.4426950408889634f / sqrtf((float)kHeadDim);
 
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_ptr);
@@ -271,6 +277,7 @@ int forward_impl(const sqa_args* a, void* workspace, size_t workspace_bytes, voi
   m.out_o = p.out_o;
   m.out_lse = p.out_lse;
   m.status = p.status;
+  m.timeline = p.timeline ? p.timeline + (size_t)pl.grid * 8 : nullptr;
   m.rows = 0;
   m.num_parts = pl.pieces;
   m.piece_rows = pl.shape.rows_pad;

@@ -50,6 +50,7 @@ struct SplitKvParams {
   int batch, q_len, hq, hkv, max_pages, num_pages;
   int num_stages;
   int num_pieces;               // workspace partial slots
+  unsigned long long* timeline; // -DSQA_DEBUG_TIMELINE: 8 stamps per CTA, else nullptr
   float scale_log2;             // head_dim^-0.5 * log2(e)
 };
 
@@ -59,6 +60,7 @@ struct MergeParams {
   const int2* seg_info;         // nullptr: every segment has pieces [0, num_parts)
   const int32_t* seq_lens;      // per-call merge: empty sequences are written as 0 / -inf
   unsigned int* status;         // per-call merge: device status word
+  unsigned long long* timeline; // -DSQA_DEBUG_TIMELINE: 4 stamps per merge CTA, else nullptr
   __half* out;
   float* out_o;
   float* out_lse;

@@ -8,60 +8,20 @@
 // (csrc/small_q_attention_ext.cu:339-366: global max, rescale, sum, divide,
 // 0 when the denominator is 0) on normalised partials.
 #include "sqa_internal.h"
+#include "sqa_merge_row.cuh"
 #include "sqa_ptx.cuh"
 
 namespace sqa {
 namespace {
 
-constexpr float kLog2e = 1.4426950408889634f;
-constexpr float kLn2 = 0.6931471805599453f;
-
-// Merge `cnt` parts of one row; part i's row is at o + i * o_stride and
-// lse + i * lse_stride.  Writes to whichever of out / out_o / out_lse is set.
-__device__ __forceinline__ void merge_row(const float* o, size_t o_stride, const float* lse,
-                                          size_t lse_stride, int cnt, __half* out, float* out_o,
-                                          float* out_lse) {
-  const int lane = threadIdx.x & 31;
-  float mmax = -INFINITY;
-  for (int i = lane; i < cnt; i += 32) mmax = fmaxf(mmax, __ldg(lse + i * lse_stride));
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) mmax = fmaxf(mmax, __shfl_xor_sync(0xffffffffu, mmax, off));
-  const float base = (mmax == -INFINITY) ? 0.f : mmax;
-
-  float total = 0.f;
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int i0 = 0; i0 < cnt; i0 += 32) {
-    const int i = i0 + lane;
-    const float wl = (i < cnt) ? ex2((__ldg(lse + i * lse_stride) - base) * kLog2e) : 0.f;
-    const int m = min(32, cnt - i0);
-    for (int j = 0; j < m; ++j) {
-      const float wgt = __shfl_sync(0xffffffffu, wl, j);
-      total += wgt;
-      const float4 v = __ldg(reinterpret_cast<const float4*>(o + (i0 + j) * o_stride) + lane);
-      acc.x += wgt * v.x;
-      acc.y += wgt * v.y;
-      acc.z += wgt * v.z;
-      acc.w += wgt * v.w;
-    }
-  }
-  const float inv = (total > 0.f) ? 1.f / total : 0.f;
-  acc.x *= inv;
-  acc.y *= inv;
-  acc.z *= inv;
-  acc.w *= inv;
-  if (out != nullptr) {
-    uint2 h;
-    h.x = pack_half2(acc.x, acc.y);
-    h.y = pack_half2(acc.z, acc.w);
-    reinterpret_cast<uint2*>(out)[lane] = h;
-  }
-  if (out_o != nullptr) reinterpret_cast<float4*>(out_o)[lane] = acc;
-  if (out_lse != nullptr && lane == 0) *out_lse = (total > 0.f) ? base + __logf(total) : -INFINITY;
-  (void)kLn2;
-}
-
 // Per-call merge: grid (B * Hkv, ceil(4 * q_len / 4)), 4 warps = 4 rows per CTA.
 __global__ void __launch_bounds__(128) sqa_segment_merge_kernel(const MergeParams p) {
+  unsigned long long* tl =
+      p.timeline ? p.timeline + ((size_t)blockIdx.y * gridDim.x + blockIdx.x) * 4 : nullptr;
+  if (threadIdx.x == 0) SQA_STAMP(tl, 0);
+  grid_dependency_wait();    // the split-KV grid has finished writing the partials
+  allow_dependent_launch();  // the next call's split-KV kernel may start its prologue
+  if (threadIdx.x == 0) SQA_STAMP(tl, 1);
   const int s = blockIdx.x;
   const int b = s / p.hkv;
   const int h = s - b * p.hkv;
@@ -85,17 +45,38 @@ __global__ void __launch_bounds__(128) sqa_segment_merge_kernel(const MergeParam
   if (info.y <= 1) return;  // written directly by the split-KV kernel
   if (!SQA_CHECK(info.x >= 0 && info.x + info.y <= p.num_parts, p.status, 8, s)) return;
   const size_t first = (size_t)info.x * p.piece_rows + row;
-  merge_row(p.parts_o + first * kHeadDim, (size_t)p.piece_rows * kHeadDim, p.parts_lse + first,
+  merge_row<false>(p.parts_o + first * kHeadDim, (size_t)p.piece_rows * kHeadDim, p.parts_lse + first,
             (size_t)p.piece_rows, info.y, out, out_o, out_lse);
+  if (threadIdx.x == 0) SQA_STAMP(tl, 2);
 }
 
 // Cross-device merge: rows given explicitly, 4 rows per CTA.
 __global__ void __launch_bounds__(128) sqa_partials_merge_kernel(const MergeParams p) {
+  grid_dependency_wait();
+  allow_dependent_launch();
   const long long row = (long long)blockIdx.x * 4 + (threadIdx.x >> 5);
   if (row >= p.rows) return;
-  merge_row(p.parts_o + row * kHeadDim, (size_t)p.rows * kHeadDim, p.parts_lse + row, (size_t)p.rows,
+  merge_row<false>(p.parts_o + row * kHeadDim, (size_t)p.rows * kHeadDim, p.parts_lse + row, (size_t)p.rows,
             p.num_parts, p.out ? p.out + row * kHeadDim : nullptr,
             p.out_o ? p.out_o + row * kHeadDim : nullptr, p.out_lse ? p.out_lse + row : nullptr);
+}
+
+// 128-thread launch that may overlap the previous kernel's tail (programmatic
+// dependent launch); the kernel waits for it before touching memory.
+cudaError_t launch_pdl(void (*kernel)(const MergeParams), dim3 grid, const MergeParams& p, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, p);
+  if (err != cudaSuccess) return err;
+  return cudaGetLastError();
 }
 
 }  // namespace
@@ -103,15 +84,11 @@ __global__ void __launch_bounds__(128) sqa_partials_merge_kernel(const MergePara
 cudaError_t launch_segment_merge(const MergeParams& p, int rows_pad, cudaStream_t stream) {
   (void)rows_pad;
   const int rows = kGroup * p.q_len;
-  const dim3 grid(p.batch * p.hkv, (rows + 3) / 4);
-  sqa_segment_merge_kernel<<<grid, 128, 0, stream>>>(p);
-  return cudaGetLastError();
+  return launch_pdl(sqa_segment_merge_kernel, dim3(p.batch * p.hkv, (rows + 3) / 4), p, stream);
 }
 
 cudaError_t launch_partials_merge(const MergeParams& p, cudaStream_t stream) {
-  const long long blocks = (p.rows + 3) / 4;
-  sqa_partials_merge_kernel<<<(unsigned)blocks, 128, 0, stream>>>(p);
-  return cudaGetLastError();
+  return launch_pdl(sqa_partials_merge_kernel, dim3((unsigned)((p.rows + 3) / 4)), p, stream);
 }
 
 }  // namespace sqa

@@ -1,0 +1,74 @@
+// sqa_merge_row.cuh -- log-sum-exp merge of one output row (one warp).
+//
+// Used by the separate merge kernels (sqa_merge.cu) and by the split-KV
+// kernel's in-kernel merge (sqa_split_kv.cu).  Arithmetic of the upstream
+// split-KV merge (csrc/small_q_attention_ext.cu:339-366: global max, rescale
+// by exp(stat - max), sum, divide; 0 when the total weight is 0) applied to
+// normalised partials with natural-log LSEs.
+#pragma once
+
+#include "sqa_internal.h"
+#include "sqa_ptx.cuh"
+
+namespace sqa {
+
+constexpr float kMergeLog2e = 1.4426950408889634f;
+
+// Merge `cnt` parts of one row; part i's row is at o + i * o_stride and
+// lse + i * lse_stride.  Writes to whichever of out / out_o / out_lse is set.
+// Parts are taken 8 at a time with all their loads issued before use, so a
+// row costs one memory round trip per 8 parts rather than one per part.
+// kCoherent reads through L2 (ld.global.cg): required when the parts were
+// written by other CTAs of the same kernel; otherwise the read-only path.
+template <bool kCoherent>
+__device__ __forceinline__ void merge_row(const float* o, size_t o_stride, const float* lse,
+                                          size_t lse_stride, int cnt, __half* out, float* out_o,
+                                          float* out_lse) {
+  constexpr int kBatch = 8;
+  const int lane = threadIdx.x & 31;
+  auto load_f = [](const float* ptr) { return kCoherent ? __ldcg(ptr) : __ldg(ptr); };
+  auto load_f4 = [](const float4* ptr) { return kCoherent ? __ldcg(ptr) : __ldg(ptr); };
+  float mmax = -INFINITY;
+  for (int i = lane; i < cnt; i += 32) mmax = fmaxf(mmax, load_f(lse + i * lse_stride));
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) mmax = fmaxf(mmax, __shfl_xor_sync(0xffffffffu, mmax, off));
+  const float base = (mmax == -INFINITY) ? 0.f : mmax;
+
+  float total = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int i0 = 0; i0 < cnt; i0 += kBatch) {
+    float4 v[kBatch];
+    float l[kBatch];
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      const bool ok = i0 + j < cnt;
+      v[j] = ok ? load_f4(reinterpret_cast<const float4*>(o + (i0 + j) * o_stride) + lane)
+                : make_float4(0.f, 0.f, 0.f, 0.f);
+      l[j] = ok ? load_f(lse + (i0 + j) * lse_stride) : -INFINITY;
+    }
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      const float wgt = ex2((l[j] - base) * kMergeLog2e);  // -inf -> 0
+      total += wgt;
+      acc.x += wgt * v[j].x;
+      acc.y += wgt * v[j].y;
+      acc.z += wgt * v[j].z;
+      acc.w += wgt * v[j].w;
+    }
+  }
+  const float inv = (total > 0.f) ? 1.f / total : 0.f;
+  acc.x *= inv;
+  acc.y *= inv;
+  acc.z *= inv;
+  acc.w *= inv;
+  if (out != nullptr) {
+    uint2 h;
+    h.x = pack_half2(acc.x, acc.y);
+    h.y = pack_half2(acc.z, acc.w);
+    reinterpret_cast<uint2*>(out)[lane] = h;
+  }
+  if (out_o != nullptr) reinterpret_cast<float4*>(out_o)[lane] = acc;
+  if (out_lse != nullptr && lane == 0) *out_lse = (total > 0.f) ? base + __logf(total) : -INFINITY;
+}
+
+}  // namespace sqa

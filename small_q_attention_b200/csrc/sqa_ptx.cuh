@@ -44,6 +44,18 @@ __device__ __forceinline__ bool debug_check(bool ok, unsigned int* status, unsig
 #define SQA_CHECK(ok, status, check, index) true
 #endif
 
+// Timeline tracing (-DSQA_DEBUG_TIMELINE): %globaltimer stamps per CTA.
+#ifdef SQA_DEBUG_TIMELINE
+#define SQA_STAMP(tl, idx) \
+  do {                     \
+    if (tl) (tl)[idx] = global_timer_ns(); \
+  } while (0)
+#else
+#define SQA_STAMP(tl, idx) \
+  do {                     \
+  } while (0)
+#endif
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
@@ -194,6 +206,14 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
 }
+
+// Programmatic dependent launch.  grid_dependency_wait() blocks until the
+// preceding kernel in the stream has completed and its memory is visible (a
+// no-op when the launch had no programmatic dependency); every global read of
+// inputs and every workspace write comes after it.  allow_dependent_launch()
+// lets the next kernel in the stream start its own prologue early.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void allow_dependent_launch() { asm volatile("griddepcontrol.launch_dependents;" :::); }
 
 // Named barrier over `count` threads (the consumer warps only).
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {

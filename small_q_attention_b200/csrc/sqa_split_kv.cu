@@ -228,9 +228,9 @@ __device__ void producer_loop(const SplitKvParams& p, const Schedule& sch, const
   }
   if (__any_sync(0xffffffffu, bad_page) && lane == 0) atomicOr(p.status, 8u);  // SQA_DEV_BAD_PAGE
   // No bulk copy may still be landing in this CTA's shared memory when it
-  // exits.  On the normal path the consumers have already waited for every
-  // page, so this returns at once; after an abort it bounds the wait.
-  if (lane == 0) {
+  // exits.  On the normal path the consumers wait for every page, so only an
+  // abort (a timed-out wait) needs this bounded drain.
+  if (lane == 0 && *abort) {
     const int bars = min(issued, 2 * S);
     for (int k = 0; k < bars; ++k) {
       const int last = k + 2 * S * ((issued - 1 - k) / (2 * S));  // last page on barrier k
@@ -243,8 +243,8 @@ __device__ void producer_loop(const SplitKvParams& p, const Schedule& sch, const
 // ------------------------------------------------------------------ consumers
 template <int NT, int WR>
 __device__ void consumer_loop(const SplitKvParams& p, const Schedule& sch, uint8_t* stages,
-                              uint64_t* full, uint64_t* empty, float* cbuf, float* mbuf,
-                              float* lbuf, volatile int* abort) {
+                              uint64_t* full, uint64_t* empty, float* cbuf, float* mbuf, float* lbuf,
+                              volatile int* abort) {
   constexpr int WT = kConsumerWarps / WR;  // token groups
   constexpr int ROWS_W = 8 * NT;           // rows per warp
   constexpr int ROWS_PAD = ROWS_W * WR;
@@ -328,6 +328,9 @@ __device__ void consumer_loop(const SplitKvParams& p, const Schedule& sch, uint8
       if (lane == 0) debug_progress[warp] = gi;
 #endif
       mbar_wait_bounded(smem_u32(full + my_fslot), my_fphase, abort, p.status, 3, gi);
+#ifdef SQA_DEBUG_TIMELINE
+      if (gi == 0 && lane == 0 && p.timeline) p.timeline[(size_t)blockIdx.x * 8 + 3] = global_timer_ns();
+#endif
       uint8_t* st = stages + (size_t)my_slot * kStageBytes;
       const uint32_t k_base = smem_u32(st);
       const uint32_t v_base = k_base + 4096;
@@ -530,7 +533,9 @@ __global__ void __launch_bounds__(kThreads, 2)
   Schedule* sch = reinterpret_cast<Schedule*>(empty + p.num_stages);
 
   const int warp = threadIdx.x >> 5;
+  unsigned long long* tl = p.timeline ? p.timeline + (size_t)blockIdx.x * 8 : nullptr;
   if (threadIdx.x == 0) {
+    SQA_STAMP(tl, 0);  // entry
     for (int i = 0; i < 2 * p.num_stages; ++i) mbar_init(smem_u32(full + i), 1);
     for (int i = 0; i < p.num_stages; ++i) mbar_init(smem_u32(empty + i), WR);
     fence_mbar_init();
@@ -539,15 +544,32 @@ __global__ void __launch_bounds__(kThreads, 2)
     prefetch_tensormap(&tm_k);
     prefetch_tensormap(&tm_v);
   }
+  // Everything above touches only shared memory and kernel parameters; the
+  // inputs and the workspace may still be in use by the previous kernel.
+  grid_dependency_wait();
+  allow_dependent_launch();  // the merge kernel may be scheduled now; it waits for this grid
+  if (threadIdx.x == 0) SQA_STAMP(tl, 1);  // after the dependency wait
   if (warp == 0) build_schedule(p, sch);
   __syncthreads();
+  if (threadIdx.x == 0) {
+    SQA_STAMP(tl, 2);  // schedule ready
+#ifdef SQA_DEBUG_TIMELINE
+    if (tl) {
+      unsigned int smid;
+      asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+      tl[7] = smid;
+    }
+#endif
+  }
 
   const Schedule s = *sch;
   volatile int* abort = &sch->abort;
   if (warp == kConsumerWarps) {
     producer_loop(p, s, &tm_k, &tm_v, stages, full, empty, abort);
+    if ((threadIdx.x & 31) == 0) SQA_STAMP(tl, 5);  // producer done (all loads issued and landed)
   } else {
     consumer_loop<NT, WR>(p, s, stages, full, empty, cbuf, mbuf, lbuf, abort);
+    if (threadIdx.x == 0) SQA_STAMP(tl, 4);  // consumers done (last epilogue written)
   }
 }
 
@@ -566,7 +588,18 @@ cudaError_t launch_shape(const SplitKvParams& p, const CUtensorMap& tm_k, const 
     if (err != cudaSuccess) return err;
     if (dev >= 0 && dev < 64) configured[dev] = smem_bytes;
   }
-  kernel<<<grid, kThreads, smem_bytes, stream>>>(p, tm_k, tm_v);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem_bytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  err = cudaLaunchKernelEx(&cfg, kernel, p, tm_k, tm_v);
+  if (err != cudaSuccess) return err;
   return cudaGetLastError();
 }
 

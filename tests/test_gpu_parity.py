@@ -102,10 +102,22 @@ def test_parity_vs_oracle(sqa, q_len, lens, hkv, page_mode):
 
 @pytest.mark.parametrize("num_ctas", [1, 2, 3, 7, 64, 148, 296, 1000])
 def test_forced_splits_merge(sqa, num_ctas):
-    """Every CTA count splits segments differently; all must give the same answer."""
+    """Every CTA count splits segments differently; all must give the oracle's answer."""
     c = case(4, [40, 700, 16, 1500, 4], hkv=2, seed=7)
     ref = oracle(c)
     assert_close(run(sqa, c, num_ctas=num_ctas, min_pages_per_cta=1), ref)
+
+
+def test_back_to_back_calls_are_identical(sqa):
+    """Back-to-back calls (overlapping launches) reuse one workspace: results stay identical."""
+    c = case(8, [5000, 4096, 33, 12000], hkv=8, seed=19)
+    a = run(sqa, c)
+    outs = [sqa.small_q_attention(c["query"], c["key_cache"], c["value_cache"], c["block_tables"],
+                                  c["seq_lens"], 16) for _ in range(4)]
+    torch.cuda.synchronize()
+    for o in outs:
+        assert torch.equal(a, o)
+    assert_close(a, oracle(c))
 
 
 def test_outlier_keys_softmax_range(sqa):
