@@ -208,13 +208,65 @@ def time_oracle(c, budget_s: float, max_calls: int = 50):
 
 
 # ------------------------------------------------------------------ arms
+WORKLOADS = {
+    "cfg2": "cfg2 batch-sharded, weak: B=4 per GPU, q_len=4, kv_len=8192, random pages, pool 1.5x",
+    "cfg3": "cfg3 KV-head-sharded, strong: B=16, q_len=8, kv_len=32768, 8/N KV heads per GPU",
+    "cfg4": "cfg4 batch-sharded (LPT by tokens), strong: B=64, q_len=4, kv_len U[512,32768], K x4 on 1%",
+    "cfg5": "cfg5 long-context, strong: B=1, q_len=16, kv_len=262144 split over N GPUs, (O, LSE) all-gather + merge",
+}
+
+
+def _rank_cases(name, world, rank, device, n_rep):
+    """This rank's input replicas for a workload, with its algorithmic bytes per
+    step and the whole job's bytes per step."""
+    import torch
+
+    from small_q_attention_b200.sharding import kv_head_range, lpt_batch_shards, page_split, shard_lengths
+    from small_q_attention_b200.workloads import CONFIGS, algorithmic_bytes, config_lens, make_case, make_config
+
+    if name == "cfg2":
+        reps = [make_config("cfg2", seed=1000 * rank + r, device=device) for r in range(n_rep)]
+        mine = _case_bytes(reps[0])
+        return reps, mine, mine * world
+    if name == "cfg3":
+        lo, hi = kv_head_range(8, world, rank)
+        lens = [32768] * 16
+        reps = [make_case(16, 8, lens, hkv=hi - lo, pool_factor=1.0, seed=1000 * rank + r, device=device)
+                for r in range(n_rep)]
+        return reps, _case_bytes(reps[0]), algorithmic_bytes(16, 8, lens)
+    if name == "cfg4":
+        lens = config_lens("cfg4")
+        mine_idx = lpt_batch_shards(lens, world)[rank]
+        my_lens = [lens[i] for i in mine_idx]
+        reps = [make_case(len(my_lens), 4, my_lens, pool_factor=1.25, k_outlier_frac=0.01,
+                          seed=1000 * rank + r, device=device) for r in range(n_rep)]
+        return reps, _case_bytes(reps[0]), algorithmic_bytes(64, 4, lens)
+    if name == "cfg5":
+        total = CONFIGS["cfg5"]["kv_len"]
+        lo, hi = page_split(total // 16, world, rank)
+        held, mlen = shard_lengths(total, lo, hi)
+        g = torch.Generator(device=device).manual_seed(5)  # the same query on every rank
+        q = torch.randn(1, 16, 32, 128, generator=g, device=device, dtype=torch.float16)
+        reps = []
+        for r in range(n_rep):
+            c = make_case(1, 16, [held], pool_factor=1.0, seed=1000 * rank + r, device=device)
+            c["query"] = q
+            c["mask_lens"] = torch.tensor([mlen], dtype=torch.int32, device=device)
+            reps.append(c)
+        mine = algorithmic_bytes(1, 16, [held]) - 2 * 16 * 32 * 128 * 2  # K/V + table; Q/O counted once below
+        return reps, mine, algorithmic_bytes(1, 16, [total])
+    raise ValueError(name)
+
+
 def run_ours(args):
+    import ctypes
+
     import torch
 
     import small_q_attention_b200 as sqa
     from small_q_attention_b200 import _native
     from small_q_attention_b200.attention import _fill_args
-    from small_q_attention_b200.workloads import CONFIGS, make_config
+    from small_q_attention_b200.sharding import gather_partials, long_context_attention
 
     world, rank, local = _dist()
     torch.cuda.set_device(local)
@@ -222,22 +274,31 @@ def run_ours(args):
     dist = _init_pg(world, "nccl")
     lib = _native.library()
     peak_gbs, peak_src = _peaks()
+    name = args.workload
+    longctx = name == "cfg5"
 
-    # --- inputs: REPLICAS independent copies of this rank's batch
-    reps = [make_config(WORKLOAD, seed=1000 * rank + r, device=device) for r in range(REPLICAS)]
-    bytes_per_call = _case_bytes(reps[0])
-    cfg = CONFIGS[WORKLOAD]
-    outs = [torch.empty_like(r["query"]) for r in reps]
-    ws_bytes = sqa.workspace_bytes(reps[0]["query"], reps[0]["key_cache"], reps[0]["value_cache"],
-                                   reps[0]["block_tables"], reps[0]["seq_lens"], 16, cfg["kv_len"])
-    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=device)
-    cargs = []
-    for r, o in zip(reps, outs):
-        a = _fill_args(r["query"], r["key_cache"], r["value_cache"], r["block_tables"], r["seq_lens"], None,
-                       cfg["kv_len"], 0, 0)
-        a.out = o.data_ptr()
+    reps, bytes_rank, bytes_job = _rank_cases(name, world, rank, device, REPLICAS)
+    max_len = max(max(r["lens"]) for r in reps)
+    ws_bytes = 0
+    cargs, outs, lses = [], [], []
+    for r in reps:
+        a = _fill_args(r["query"], r["key_cache"], r["value_cache"], r["block_tables"], r["seq_lens"],
+                       r.get("mask_lens"), max_len, 0, 0)
+        if longctx:
+            o = torch.empty(r["query"].shape, dtype=torch.float32, device=device)
+            l = torch.empty(r["query"].shape[:3], dtype=torch.float32, device=device)
+            a.out_partial, a.out_lse = o.data_ptr(), l.data_ptr()
+            lses.append(l)
+        else:
+            o = torch.empty_like(r["query"])
+            a.out = o.data_ptr()
+        outs.append(o)
         cargs.append(a)
-    import ctypes
+        st = ctypes.c_int(0)
+        ws_bytes = max(ws_bytes, lib.sqa_workspace_bytes(ctypes.byref(a), local, ctypes.byref(st)))
+        _native.check(st.value, "sqa_workspace_bytes")
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=device)
+    merged = torch.empty(reps[0]["query"].shape, dtype=torch.float16, device=device)
 
     def call(i, stream, ev0=None, ev1=None):
         a = cargs[i % REPLICAS]
@@ -249,6 +310,13 @@ def run_ours(args):
                                          ctypes.c_size_t(ws_bytes), ctypes.c_void_p(stream),
                                          ctypes.c_void_p(ev0), ctypes.c_void_p(ev1))
         _native.check(code, "sqa_forward")
+        if longctx:  # the exchange step: gather every rank's (O, LSE), merge on every rank
+            j = i % REPLICAS
+            if dist is not None:
+                parts_o, parts_lse = gather_partials(outs[j], lses[j])
+            else:
+                parts_o, parts_lse = outs[j][None], lses[j][None]
+            sqa.merge_partials(parts_o, parts_lse, out=merged)
 
     stream = torch.cuda.Stream(device)
     sh = stream.cuda_stream
@@ -264,8 +332,7 @@ def run_ours(args):
         for i in range(K):
             call(i, torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
-    for _ in range(max(1, W // K + 1)):  # warm the graph itself
-        graph.replay()
+    graph.replay()  # warm the graph itself
     torch.cuda.synchronize()
 
     # --- timed region: K steps, barrier + synchronize on both sides
@@ -282,10 +349,10 @@ def run_ours(args):
         if dist is not None:
             dist.barrier()
     t_ms = _max_over_ranks(start.elapsed_time(end), dist, device)
-    value_tbs = world * K * bytes_per_call / (t_ms * 1e-3) / 1e12
-    del graph
+    value_tbs = K * bytes_job / (t_ms * 1e-3) / 1e12
+    del graph  # holds NCCL work in the long-context mode: release before the group
 
-    # --- roofline: the split-KV kernel alone, one event pair per launch
+    # --- roofline: the split-KV kernel alone, one event pair per launch (this rank)
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
     for e0, e1 in evs:  # create the underlying CUDA events
         e0.record(stream)
@@ -296,23 +363,31 @@ def run_ours(args):
             call(i, sh, e0.cuda_event, e1.cuda_event)
     torch.cuda.synchronize()
     kern_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs)
-    achieved_gbs = bytes_per_call / (kern_ms * 1e-3) / 1e9
+    kern_bytes = bytes_rank + (2 * 16 * 32 * 128 * 2 if longctx else 0)
+    achieved_gbs = kern_bytes / (kern_ms * 1e-3) / 1e9
 
     # --- e2e through the public API with host buffers
-    host_in = [{k: r[k].cpu().pin_memory() for k in ("query", "block_tables", "seq_lens")} for r in reps]
-    dev_in = [{k: torch.empty_like(r[k]) for k in ("query", "block_tables", "seq_lens")} for r in reps]
-    host_out = [torch.empty(o.shape, dtype=o.dtype, pin_memory=True) for o in outs]
+    small = ("query", "block_tables", "seq_lens") + (("mask_lens",) if longctx else ())
+    host_in = [{k: r[k].cpu().pin_memory() for k in small} for r in reps]
+    dev_in = [{k: torch.empty_like(r[k]) for k in small} for r in reps]
+    host_out = torch.empty(reps[0]["query"].shape, dtype=torch.float16, pin_memory=True)
     h2d = sum(t.numel() * t.element_size() for t in host_in[0].values())
-    d2h = host_out[0].numel() * host_out[0].element_size()
+    d2h = host_out.numel() * host_out.element_size()
+    e2e_out = [torch.empty_like(r["query"]) for r in reps]
 
     def e2e_step(i):
         j = i % REPLICAS
-        for k in ("query", "block_tables", "seq_lens"):
+        for k in small:
             dev_in[j][k].copy_(host_in[j][k], non_blocking=True)
-        o = sqa.small_q_attention(dev_in[j]["query"], reps[j]["key_cache"], reps[j]["value_cache"],
-                                  dev_in[j]["block_tables"], dev_in[j]["seq_lens"], 16, cfg["kv_len"],
-                                  out=outs[j], workspace=ws)
-        host_out[j].copy_(o, non_blocking=True)
+        d = dev_in[j]
+        if longctx:
+            o = long_context_attention(d["query"], reps[j]["key_cache"], reps[j]["value_cache"],
+                                       d["block_tables"], d["seq_lens"], d["mask_lens"], 16, out=e2e_out[j],
+                                       workspace=ws)
+        else:
+            o = sqa.small_q_attention(d["query"], reps[j]["key_cache"], reps[j]["value_cache"],
+                                      d["block_tables"], d["seq_lens"], 16, max_len, out=e2e_out[j], workspace=ws)
+        host_out.copy_(o, non_blocking=True)
 
     with torch.cuda.stream(stream):
         for i in range(W):
@@ -328,46 +403,50 @@ def run_ours(args):
         e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = _max_over_ranks(e0.elapsed_time(e1), dist, device)
-    e2e_tbs = world * K * bytes_per_call / (e2e_ms * 1e-3) / 1e12
+    e2e_tbs = K * bytes_job / (e2e_ms * 1e-3) / 1e12
 
-    # --- CPU baseline: the oracle on a bounded sample (rank 0, N=1 only)
+    # --- CPU baseline: the oracle on a bounded sample (rank 0, N=1, the cfg2 line only)
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and name == "cfg2" and not args.no_cpu_baseline:
         times = time_oracle(reps[0], args.cpu_seconds)
         t = statistics.median(times)
-        cpu = {"value": bytes_per_call / t / 1e12, "unit": "TB/s", "cores": _cpu_cores(), "kind": "port",
-               "sample": f"{len(times)} whole {WORKLOAD} calls (B=4,q=4,kv=8192) of the numpy oracle, "
+        cpu = {"value": bytes_rank / t / 1e12, "unit": "TB/s", "cores": _cpu_cores(), "kind": "port",
+               "sample": f"{len(times)} whole cfg2 calls (B=4,q=4,kv=8192) of the numpy oracle, "
                          f"median {t * 1e3:.1f} ms/call, {_cpu_model()}"}
 
     if dist is not None:
         dist.barrier()
     if rank == 0:
-        traffic = _traffic(WORKLOAD)
+        q = reps[0]["query"]
         line = {
             "metric": METRIC, "value": round(value_tbs, 4), "unit": "TB/s", "n_gpus": world, "steps": K,
-            "warmup": W, "ms_per_step": round(t_ms / K, 6), "higher_is_better": True, "scaling": "weak",
+            "warmup": W, "ms_per_step": round(t_ms / K, 6), "higher_is_better": True,
+            "scaling": "weak" if name == "cfg2" else "strong",
             "vs_baseline": None, "dtype": "f16 in, f32 accumulate", "data": "synthetic (seeded N(0,1) fp16)",
-            "config": {"workload": f"{WORKLOAD}: B={cfg['batch']} per GPU, q_len={cfg['q_len']}, "
-                                   f"kv_len={cfg['kv_len']}, Hq/Hkv=32/8, d=128, page 16, random pages, "
-                                   f"pool 1.5x",
-                       "global_batch": cfg["batch"] * world, "seq_len": cfg["kv_len"], "q_len": cfg["q_len"],
-                       "parallelism": f"batch-shard x{world}",
-                       "l2": f"inputs rotated over {REPLICAS} replicas "
+            "config": {"workload": WORKLOADS[name],
+                       "global_batch": (q.shape[0] * world if name == "cfg2" else
+                                        {"cfg3": 16, "cfg4": 64, "cfg5": 1}[name]),
+                       "seq_len": max_len if name != "cfg5" else 262144, "q_len": int(q.shape[1]),
+                       "parallelism": {"cfg2": f"batch-shard x{world}", "cfg3": f"kv-head-shard x{world}",
+                                       "cfg4": f"batch-shard (LPT) x{world}",
+                                       "cfg5": f"kv-range split x{world} + NCCL all-gather"}[name],
+                       "l2": f"inputs rotated over {REPLICAS} replicas per GPU "
                              f"({REPLICAS * reps[0]['key_cache'].numel() * 4 / 1e6:.0f} MB > 126 MB L2)",
                        "us_per_call": round(t_ms / K * 1e3, 3),
-                       "algorithmic_bytes_per_call": bytes_per_call},
+                       "algorithmic_bytes_per_call": bytes_job},
             "roofline": {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": peak_gbs, "unit": "GB/s",
                          "frac": round(achieved_gbs / peak_gbs, 4), "peak_source": f"{peak_src} hbm_gbs (burst)",
-                         "traffic": traffic, "kernel": "sqa_split_kv_kernel",
-                         "kernel_us": round(kern_ms * 1e3, 3)},
+                         "traffic": _traffic(name) if world == 1 else None, "kernel": "sqa_split_kv_kernel",
+                         "kernel_us": round(kern_ms * 1e3, 3), "rank": 0},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_tbs, 4), "unit": "TB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "us_per_step": round(e2e_ms / K * 1e3, 3)},
             "clocks": clocks.summary(),
-            "gpu_launches": 2 * K,
+            "gpu_launches": (3 if longctx else 2) * K,
         }
         print(json.dumps(line), flush=True)
     if dist is not None:
+        dist.barrier()
         dist.destroy_process_group()
 
 
@@ -525,6 +604,8 @@ def main():
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--workload", choices=tuple(WORKLOADS), default="cfg2",
+                    help="cfg2 (default, the driver's line) or a sharded configuration")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--reference-budget-s", type=float, default=150.0)
