@@ -532,8 +532,11 @@ def run_matrix(args):
     # one explicit workspace, large enough for every case (16 KV-head segments x 64 rows worst case)
     ws = torch.zeros(64 << 20, dtype=torch.uint8, device="cuda")
     cases = [("matrix", c) for c in matrix_cases()] + [(n, None) for n in CONFIGS]
-    if args.only:
-        cases = [(n, c) for n, c in cases if n in args.only or (c and f"q{c['q_len']}" in args.only)]
+    if args.only:  # config names, "q<N>" for a q_len, or case labels like q16_kv8192_b16
+        def label_of(n, c):
+            return n if c is None else f"q{c['q_len']}_kv{c['kv_len']}_b{c['batch']}"
+        cases = [(n, c) for n, c in cases
+                 if label_of(n, c) in args.only or (c and f"q{c['q_len']}" in args.only)]
     for name, c in cases:
         if c is None:
             first = make_config(name, seed=0)
