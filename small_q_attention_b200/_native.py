@@ -67,6 +67,7 @@ class SqaArgs(ctypes.Structure):
         ("max_seq_len", ctypes.c_int32),
         ("num_ctas", ctypes.c_int32),
         ("min_pages_per_cta", ctypes.c_int32),
+        ("kernel", ctypes.c_int32),
     ]
 
 

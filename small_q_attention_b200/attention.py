@@ -73,7 +73,7 @@ def _check_inputs(query, key_cache, value_cache, block_tables, seq_lens, page_si
 
 
 def _fill_args(query, key_cache, value_cache, block_tables, seq_lens, mask_lens, max_seq_len,
-               num_ctas, min_pages_per_cta) -> _native.SqaArgs:
+               num_ctas, min_pages_per_cta, kernel: int = 0) -> _native.SqaArgs:
     a = _native.SqaArgs()
     a.query = query.data_ptr()
     a.key_cache = key_cache.data_ptr()
@@ -87,6 +87,7 @@ def _fill_args(query, key_cache, value_cache, block_tables, seq_lens, mask_lens,
     a.max_seq_len = int(max_seq_len)
     a.num_ctas = int(num_ctas)
     a.min_pages_per_cta = int(min_pages_per_cta)
+    a.kernel = int(kernel)
     return a
 
 
@@ -162,7 +163,7 @@ def _run(args, device, workspace, check):
 
 def small_q_attention(query, key_cache, value_cache, block_tables, seq_lens, page_size: int,
                       max_seq_len: int = 0, *, out=None, workspace=None, num_ctas: int = 0,
-                      min_pages_per_cta: int = 0, check: bool = False):
+                      min_pages_per_cta: int = 0, kernel: int = 0, check: bool = False):
     """Causal paged MTP attention; returns fp16 ``[batch, q_len, Hq, 128]``.
 
     ``seq_lens[b]`` is the KV length including the ``q_len`` draft tokens and
@@ -172,7 +173,9 @@ def small_q_attention(query, key_cache, value_cache, block_tables, seq_lens, pag
     page-table width); unlike the upstream (``ext.cu:1173-1176``) it is never
     measured with a device-to-host copy.  ``check=True`` synchronises and
     raises the exception the upstream CPU reference would raise for bad
-    metadata (``seq_lens < q_len``, page ids outside the pool).
+    metadata (``seq_lens < q_len``, page ids outside the pool).  ``kernel``
+    selects the implementation: 0 auto, 1 warp-level mma.sync, 2 tcgen05 with
+    tensor memory (same operator).
     """
     _check_inputs(query, key_cache, value_cache, block_tables, seq_lens, page_size)
     if out is None:
@@ -180,7 +183,7 @@ def small_q_attention(query, key_cache, value_cache, block_tables, seq_lens, pag
     elif out.shape != query.shape or out.dtype != torch.float16 or not out.is_contiguous() or out.device != query.device:
         raise ValueError("out must be a contiguous fp16 tensor shaped like query")
     args = _fill_args(query, key_cache, value_cache, block_tables, seq_lens, None, max_seq_len,
-                      num_ctas, min_pages_per_cta)
+                      num_ctas, min_pages_per_cta, kernel)
     args.out = out.data_ptr()
     _run(args, query.device, workspace, check)
     return out
@@ -189,7 +192,7 @@ def small_q_attention(query, key_cache, value_cache, block_tables, seq_lens, pag
 def small_q_attention_partial(query, key_cache, value_cache, block_tables, seq_lens, page_size: int,
                               mask_lens=None, max_seq_len: int = 0, *, out=None, out_lse=None,
                               workspace=None, num_ctas: int = 0, min_pages_per_cta: int = 0,
-                              check: bool = False):
+                              kernel: int = 0, check: bool = False):
     """Attention over the tokens this call holds; returns ``(O fp32, LSE fp32)``.
 
     The shard form of the operator for splitting one sequence's KV range:
@@ -209,7 +212,7 @@ def small_q_attention_partial(query, key_cache, value_cache, block_tables, seq_l
     if out_lse.dtype != torch.float32 or out_lse.shape != query.shape[:3] or not out_lse.is_contiguous():
         raise ValueError("out_lse must be a contiguous fp32 tensor [batch, q_len, Hq]")
     args = _fill_args(query, key_cache, value_cache, block_tables, seq_lens, mask_lens, max_seq_len,
-                      num_ctas, min_pages_per_cta)
+                      num_ctas, min_pages_per_cta, kernel)
     args.out_partial = out.data_ptr()
     args.out_lse = out_lse.data_ptr()
     _run(args, query.device, workspace, check)

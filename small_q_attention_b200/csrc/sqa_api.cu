@@ -13,7 +13,7 @@
 namespace sqa {
 namespace {
 
-constexpr int kAbiVersion = 100;
+constexpr int kAbiVersion = 101;
 constexpr size_t kAlign = 256;
 constexpr int kMaxDevices = 64;
 constexpr int kCtasPerSm = 2;
@@ -93,6 +93,7 @@ inline bool debug_sync(cudaStream_t, const char*, int, int, const sqa_args*) { r
 
 struct Plan {
   WarpShape shape;
+  bool tc;  // tcgen05 kernel
   int grid;
   int stages;
   int smem;
@@ -109,6 +110,7 @@ int validate(const sqa_args* a) {
   if (a->num_q_heads != kGroup * a->num_kv_heads) return SQA_ERR_UNSUPPORTED;
   if (a->q_len > SQA_MAX_Q_LEN) return SQA_ERR_UNSUPPORTED;
   if (a->max_seq_len < 0 || a->num_ctas < 0 || a->min_pages_per_cta < 0) return SQA_ERR_INVALID_ARGUMENT;
+  if (a->kernel < 0 || a->kernel > 2) return SQA_ERR_INVALID_ARGUMENT;
   // unit indices are 32-bit on the device
   if ((long long)a->batch * a->num_kv_heads * a->max_pages >= (1ll << 31)) return SQA_ERR_UNSUPPORTED;
   if ((long long)a->num_pages * kPageSize >= (1ll << 31)) return SQA_ERR_UNSUPPORTED;
@@ -134,10 +136,18 @@ int make_plan(const sqa_args* a, int device, Plan* plan) {
   if (sms <= 0) return SQA_ERR_CUDA;
   Plan pl;
   pl.shape = warp_shape_for(a->q_len);
-  const int fixed = split_kv_smem_bytes(pl.shape, 0);
-  pl.stages = (kSmemPerCta - fixed) / (kStageBytes + 24);
-  if (pl.stages > kMaxStages) pl.stages = kMaxStages;
-  pl.smem = split_kv_smem_bytes(pl.shape, pl.stages);
+  pl.tc = a->kernel == 2;
+  if (pl.tc) {
+    const int fixed = split_kv_tc_smem_bytes(0);
+    pl.stages = (kSmemPerCta - fixed) / (kStageBytes + 16);
+    if (pl.stages > kMaxStages) pl.stages = kMaxStages;
+    pl.smem = split_kv_tc_smem_bytes(pl.stages);
+  } else {
+    const int fixed = split_kv_smem_bytes(pl.shape, 0);
+    pl.stages = (kSmemPerCta - fixed) / (kStageBytes + 24);
+    if (pl.stages > kMaxStages) pl.stages = kMaxStages;
+    pl.smem = split_kv_smem_bytes(pl.shape, pl.stages);
+  }
   pl.segments = a->batch * a->num_kv_heads;
 
   long long pages_upper = a->max_pages;
@@ -257,13 +267,16 @@ int forward_impl(const sqa_args* a, void* workspace, size_t workspace_bytes, voi
   p.num_pages = a->num_pages;
   p.num_stages = pl.stages;
   p.num_pieces = pl.pieces;
+  p.rows_pad = pl.shape.rows_pad;
   p.timeline = pl.off_timeline ? reinterpret_cast<unsigned long long*>(ws + pl.off_timeline) : nullptr;
   p.scale_log2 = 1.4426950408889634f / sqrtf((float)kHeadDim);
 
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_ptr);
   if (ev_before && cudaEventRecord(reinterpret_cast<cudaEvent_t>(ev_before), stream) != cudaSuccess)
     return SQA_ERR_CUDA;
-  if (launch_split_kv(p, tm_k, tm_v, pl.grid, pl.smem, stream) != cudaSuccess) return SQA_ERR_CUDA;
+  const cudaError_t launched = pl.tc ? launch_split_kv_tc(p, tm_k, tm_v, pl.grid, pl.smem, stream)
+                                    : launch_split_kv(p, tm_k, tm_v, pl.grid, pl.smem, stream);
+  if (launched != cudaSuccess) return SQA_ERR_CUDA;
   if (!debug_sync(stream, "split-KV kernel", pl.grid, pl.smem, a)) return SQA_ERR_CUDA;
   if (ev_after && cudaEventRecord(reinterpret_cast<cudaEvent_t>(ev_after), stream) != cudaSuccess)
     return SQA_ERR_CUDA;

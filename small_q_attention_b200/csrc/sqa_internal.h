@@ -50,6 +50,7 @@ struct SplitKvParams {
   int batch, q_len, hq, hkv, max_pages, num_pages;
   int num_stages;
   int num_pieces;               // workspace partial slots
+  int rows_pad;                 // workspace rows per piece
   unsigned long long* timeline; // -DSQA_DEBUG_TIMELINE: 8 stamps per CTA, else nullptr
   float scale_log2;             // head_dim^-0.5 * log2(e)
 };
@@ -78,5 +79,10 @@ cudaError_t launch_partials_merge(const MergeParams& p, cudaStream_t stream);
 
 // Dynamic shared memory of the split-KV kernel for a warp shape and stage count.
 int split_kv_smem_bytes(const WarpShape& ws, int num_stages);
+
+// The tcgen05 / tensor-memory variant of the split-KV kernel (any q_len <= 16).
+cudaError_t launch_split_kv_tc(const SplitKvParams& p, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
+                               int grid, int smem_bytes, cudaStream_t stream);
+int split_kv_tc_smem_bytes(int num_stages);
 
 }  // namespace sqa

@@ -42,7 +42,7 @@ def test_every_declared_symbol_is_exported(lib):
 
 
 def test_abi_version_and_status_strings(lib):
-    assert lib.sqa_abi_version() == 100
+    assert lib.sqa_abi_version() == 101
     for code in range(6):
         assert lib.sqa_status_string(code).decode()
     assert lib.sqa_status_string(99).decode() == "unknown status"
@@ -61,6 +61,7 @@ def good_args():
 @pytest.mark.parametrize("field,value,code", [
     ("head_dim", 64, 2), ("page_size", 32, 2), ("num_q_heads", 16, 2), ("q_len", 17, 2),
     ("q_len", 0, 1), ("num_pages", 0, 1), ("max_pages", 0, 1), ("batch", -1, 1), ("num_ctas", -1, 1),
+    ("kernel", 3, 1),
 ])
 def test_forward_rejects_bad_shapes(lib, field, value, code):
     a = good_args()
