@@ -283,7 +283,7 @@ def run_ours(args):
     cargs, outs, lses = [], [], []
     for r in reps:
         a = _fill_args(r["query"], r["key_cache"], r["value_cache"], r["block_tables"], r["seq_lens"],
-                       r.get("mask_lens"), max_len, 0, 0)
+                       r.get("mask_lens"), max_len, 0, 0, args.kernel)
         if longctx:
             o = torch.empty(r["query"].shape, dtype=torch.float32, device=device)
             l = torch.empty(r["query"].shape[:3], dtype=torch.float32, device=device)
@@ -386,7 +386,8 @@ def run_ours(args):
                                        workspace=ws)
         else:
             o = sqa.small_q_attention(d["query"], reps[j]["key_cache"], reps[j]["value_cache"],
-                                      d["block_tables"], d["seq_lens"], 16, max_len, out=e2e_out[j], workspace=ws)
+                                      d["block_tables"], d["seq_lens"], 16, max_len, out=e2e_out[j], workspace=ws,
+                                      kernel=args.kernel)
         host_out.copy_(o, non_blocking=True)
 
     with torch.cuda.stream(stream):
@@ -560,7 +561,7 @@ def run_matrix(args):
         outs = [torch.empty_like(x["query"]) for x in inst]
         fn = lambda i: sqa.small_q_attention(  # noqa: E731
             inst[i]["query"], inst[i]["key_cache"], inst[i]["value_cache"], inst[i]["block_tables"],
-            inst[i]["seq_lens"], 16, max(inst[i]["lens"]), out=outs[i], workspace=ws)
+            inst[i]["seq_lens"], 16, max(inst[i]["lens"]), out=outs[i], workspace=ws, kernel=args.kernel)
         for i in range(5):
             fn(i % len(inst))
         torch.cuda.synchronize()
@@ -590,7 +591,7 @@ def run_matrix(args):
                "p50_us": round(us, 3), "min_us": round(min(samples), 3), "alg_bytes": nb,
                "tb_s": round(nb / (us * 1e-6) / 1e12, 4),
                "roofline_frac": round(nb / (us * 1e-6) / 1e9 / peak_gbs, 4), "peak_gbs": peak_gbs,
-               "peak_source": peak_src, "n_gpus": 1, "replicas": n_rep,
+               "peak_source": peak_src, "n_gpus": 1, "replicas": n_rep, "kernel": args.kernel,
                "timing": f"CUDA graph of {reps} back-to-back calls over rotating replicas, median of 5"}
         rows.append(row)
         print(json.dumps(row), flush=True)
@@ -616,6 +617,8 @@ def main():
     ap.add_argument("--matrix-only", action="store_true", help="run only the matrix sweep")
     ap.add_argument("--only", nargs="*", default=None)
     ap.add_argument("--page-mode", default="random", choices=("random", "unique", "shared"))
+    ap.add_argument("--kernel", type=int, default=0, choices=(0, 1, 2),
+                    help="0 auto, 1 warp-level mma.sync kernel, 2 tcgen05 kernel")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -173,7 +173,7 @@ int make_plan(const sqa_args* a, int device, Plan* plan) {
 #ifdef SQA_DEBUG_TIMELINE
   // trace buffer at the end: 8 stamps per split CTA, 4 per merge CTA
   pl.off_timeline = pl.bytes;
-  pl.bytes = align_up(pl.bytes + ((size_t)pl.grid * 8 + (size_t)pl.segments * 16 * 4) * 8);
+  pl.bytes = align_up(pl.bytes + ((size_t)pl.grid * 32 + (size_t)pl.segments * 16 * 4) * 8);
 #endif
   *plan = pl;
   return SQA_OK;
@@ -290,7 +290,7 @@ int forward_impl(const sqa_args* a, void* workspace, size_t workspace_bytes, voi
   m.out_o = p.out_o;
   m.out_lse = p.out_lse;
   m.status = p.status;
-  m.timeline = p.timeline ? p.timeline + (size_t)pl.grid * 8 : nullptr;
+  m.timeline = p.timeline ? p.timeline + (size_t)pl.grid * 32 : nullptr;
   m.rows = 0;
   m.num_parts = pl.pieces;
   m.piece_rows = pl.shape.rows_pad;

@@ -100,6 +100,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // Bounded wait for the phase with the given parity.  `abort` is a CTA-shared
 // flag: once any thread has timed out, every later wait returns at once so
 // that all warps still reach the same named barriers and the kernel ends.
+#ifdef SQA_DEBUG_TIMELINE
+// Per-CTA nanoseconds spent blocked in bounded waits, by wait kind.
+static __shared__ unsigned long long sqa_wait_ns[16];
+#define SQA_WAIT_ACCOUNT(kind, t0)                                                      \
+  do {                                                                                  \
+    if ((threadIdx.x & 31) == 0) atomicAdd(&sqa_wait_ns[(kind) & 15], global_timer_ns() - (t0)); \
+  } while (0)
+#else
+#define SQA_WAIT_ACCOUNT(kind, t0) \
+  do {                             \
+  } while (0)
+#endif
+
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
                                                   volatile int* abort, unsigned int* status,
                                                   unsigned int debug_kind = 0, unsigned int debug_index = 0) {
@@ -107,7 +120,10 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
   const uint64_t t0 = global_timer_ns();
   for (uint32_t it = 1;; ++it) {
     if (*abort) return false;
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait(bar, parity)) {
+      SQA_WAIT_ACCOUNT(debug_kind, t0);
+      return true;
+    }
     if ((it & 63u) == 0u && global_timer_ns() - t0 > kWaitLimitNs) {
       *abort = 1;
       atomicOr(status, 1u /* SQA_DEV_TIMEOUT */);

@@ -431,7 +431,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   Schedule* sch = reinterpret_cast<Schedule*>(empty + p.num_stages);
 
   const int warp = threadIdx.x >> 5;
-  unsigned long long* tl = p.timeline ? p.timeline + (size_t)blockIdx.x * 8 : nullptr;
+  unsigned long long* tl = p.timeline ? p.timeline + (size_t)blockIdx.x * 32 : nullptr;
   if (threadIdx.x == 0) {
     SQA_STAMP(tl, 0);  // entry
     for (int i = 0; i < 2 * p.num_stages; ++i) mbar_init(smem_u32(full + i), 1);

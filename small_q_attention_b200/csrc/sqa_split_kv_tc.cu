@@ -23,8 +23,9 @@
 //   P slots   p_full[NS]            softmax -> MMA (PV)
 //   pv_done[NS]                     MMA (PV commit) -> softmax (P slot reuse, O rescale, epilogue)
 //   q_ready                         softmax (Q tile written for the piece) -> MMA
-// The MMA thread issues QK for page i before PV for page i - kLag, so the
-// softmax of page i - kLag + 1.. overlaps the tensor core.
+// The MMA thread keeps QK kNS pages ahead of the softmax: after PV(i) it
+// issues QK(i + kNS) into the slot the softmax has just released, so the
+// softmax never waits for a QK product in the steady state.
 #include "sqa_internal.h"
 #include "sqa_ptx.cuh"
 #include "sqa_schedule.cuh"
@@ -32,8 +33,7 @@
 namespace sqa {
 namespace {
 
-constexpr int kNS = 4;          // S/P slots in TMEM
-constexpr int kLag = 2;         // PV(i - kLag) is issued after QK(i)
+constexpr int kNS = 5;          // S/P slots in TMEM: QK runs up to kNS pages ahead of the softmax
 constexpr int kTmemCols = 256;  // O | S slots | P slots
 constexpr int kColO = 0;
 constexpr int kColS = 128;
@@ -143,34 +143,34 @@ __device__ void tc_mma(const SplitKvParams& p, const Schedule& sch, const TcSmem
     const int n = min(sch.end, seg_end) - unit;
     mbar_wait_bounded(smem_u32(sm.q_ready), (uint32_t)(pc & 1), abort, p.status, 4, pc);
     tc_fence_after();
-    for (int j = 0; j < n + kLag; ++j) {
-      if (j < n) {  // S(g) = Q K_g^T into slot g % kNS
-        const int g = i0 + j;
-        const int st = g % S;
-        mbar_wait_bounded(smem_u32(sm.full + st), (uint32_t)(g / S) & 1u, abort, p.status, 5, g);
-        tc_fence_after();
-        const uint32_t k_base = smem_u32(sm.stages + (size_t)st * kStageBytes);
-        const uint32_t d = tmem + kColS + (g % kNS) * 16;
+    // S(g) = Q K_g^T into slot g % kNS
+    auto issue_qk = [&](int g) {
+      const int st = g % S;
+      mbar_wait_bounded(smem_u32(sm.full + st), (uint32_t)(g / S) & 1u, abort, p.status, 5, g);
+      tc_fence_after();
+      const uint32_t k_base = smem_u32(sm.stages + (size_t)st * kStageBytes);
+      const uint32_t d = tmem + kColS + (g % kNS) * 16;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t off = (kk >> 2) * 0u + (kk & 3) * 32u;
-          const uint64_t a = smem_desc_sw128(q_base + (kk >> 2) * (kQBytes / 2) + off, 16, 1024);
-          const uint64_t b = smem_desc_sw128(k_base + (kk >> 2) * 2048 + off, 16, 1024);
-          tc_mma_ss(d, a, b, kIdescQK, kk > 0 ? 1u : 0u);
-        }
-        tc_commit(smem_u32(sm.s_full + (g % kNS)));
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t off = (kk & 3) * 32u;
+        const uint64_t a = smem_desc_sw128(q_base + (kk >> 2) * (kQBytes / 2) + off, 16, 1024);
+        const uint64_t b = smem_desc_sw128(k_base + (kk >> 2) * 2048 + off, 16, 1024);
+        tc_mma_ss(d, a, b, kIdescQK, kk > 0 ? 1u : 0u);
       }
-      if (j >= kLag) {  // O += P(g) V_g
-        const int g = i0 + j - kLag;
-        const int st = g % S;
-        mbar_wait_bounded(smem_u32(sm.p_full + (g % kNS)), (uint32_t)(g / kNS) & 1u, abort, p.status, 6, g);
-        tc_fence_after();
-        const uint32_t v_base = smem_u32(sm.stages + (size_t)st * kStageBytes + 4096);
-        const uint64_t b = smem_desc_sw128(v_base, 2048, 1024);  // MN atoms: V lo -> V hi; K atoms: 8 tokens
-        tc_mma_ts(tmem + kColO, tmem + kColP + (g % kNS) * 8, b, kIdescPV, (j - kLag) > 0 ? 1u : 0u);
-        tc_commit(smem_u32(sm.empty + st));             // the page's stage may be refilled
-        tc_commit(smem_u32(sm.pv_done + (g % kNS)));    // P slot free, O up to date
-      }
+      tc_commit(smem_u32(sm.s_full + (g % kNS)));
+    };
+    for (int j = 0; j < min(n, kNS); ++j) issue_qk(i0 + j);
+    for (int j = 0; j < n; ++j) {  // O += P(g) V_g, then refill the freed slot
+      const int g = i0 + j;
+      const int st = g % S;
+      mbar_wait_bounded(smem_u32(sm.p_full + (g % kNS)), (uint32_t)(g / kNS) & 1u, abort, p.status, 6, g);
+      tc_fence_after();
+      const uint32_t v_base = smem_u32(sm.stages + (size_t)st * kStageBytes + 4096);
+      const uint64_t b = smem_desc_sw128(v_base, 2048, 1024);  // MN atoms: V lo -> V hi; K atoms: 8 tokens
+      tc_mma_ts(tmem + kColO, tmem + kColP + (g % kNS) * 8, b, kIdescPV, j > 0 ? 1u : 0u);
+      tc_commit(smem_u32(sm.empty + st));           // the page's stage may be refilled
+      tc_commit(smem_u32(sm.pv_done + (g % kNS)));  // P slot free, O up to date
+      if (j + kNS < n) issue_qk(g + kNS);           // the softmax has read S(g): reuse its slot
     }
     i0 += n;
     ++pc;
@@ -361,8 +361,13 @@ __global__ void __launch_bounds__((SW + 2) * 32, 2)
   const int warp = threadIdx.x >> 5;
   constexpr int kMmaWarp = SW;
   constexpr int kProducerWarp = SW + 1;
+  unsigned long long* tl = p.timeline ? p.timeline + (size_t)blockIdx.x * 32 : nullptr;
+#ifdef SQA_DEBUG_TIMELINE
+  if (threadIdx.x < 16) sqa_wait_ns[threadIdx.x] = 0;
+#endif
 
   if (threadIdx.x == 0) {
+    SQA_STAMP(tl, 0);
     for (int i = 0; i < p.num_stages; ++i) {
       mbar_init(smem_u32(sm.full + i), 1);
       mbar_init(smem_u32(sm.empty + i), 1);
@@ -413,6 +418,12 @@ __global__ void __launch_bounds__((SW + 2) * 32, 2)
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
+#ifdef SQA_DEBUG_TIMELINE
+  if (tl && threadIdx.x == 0) {
+    tl[4] = global_timer_ns();
+    for (int k = 0; k < 16; ++k) tl[16 + k] = sqa_wait_ns[k];
+  }
+#endif
 }
 
 template <int SW>
