@@ -117,11 +117,12 @@ def workspace_for(args: _native.SqaArgs, device: torch.device, workspace: torch.
 
 
 def workspace_bytes(query, key_cache, value_cache, block_tables, seq_lens, page_size,
-                    max_seq_len: int = 0, *, num_ctas: int = 0, min_pages_per_cta: int = 0) -> int:
+                    max_seq_len: int = 0, *, num_ctas: int = 0, min_pages_per_cta: int = 0,
+                    kernel: int = 0) -> int:
     """Bytes of workspace ``small_q_attention`` needs for these shapes."""
     _check_inputs(query, key_cache, value_cache, block_tables, seq_lens, page_size)
     args = _fill_args(query, key_cache, value_cache, block_tables, seq_lens, None, max_seq_len,
-                      num_ctas, min_pages_per_cta)
+                      num_ctas, min_pages_per_cta, kernel)
     st = ctypes.c_int(0)
     need = _native.library().sqa_workspace_bytes(ctypes.byref(args), query.device.index, ctypes.byref(st))
     _native.check(st.value, "sqa_workspace_bytes")

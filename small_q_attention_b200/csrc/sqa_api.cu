@@ -21,6 +21,7 @@ constexpr int kCtasPerSm = 2;
 // (228 KB per SM on sm_100, 1 KB reserved per CTA).
 constexpr int kSmemPerSm = 228 * 1024;
 constexpr int kSmemPerCta = kSmemPerSm / kCtasPerSm - 1024;
+constexpr int kMaxSmemPerCta = 227 * 1024;  // dynamic shared memory limit of one CTA on sm_100
 constexpr int kDefaultMinPagesPerCta = 4;
 
 size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
@@ -136,10 +137,14 @@ int make_plan(const sqa_args* a, int device, Plan* plan) {
   if (sms <= 0) return SQA_ERR_CUDA;
   Plan pl;
   pl.shape = warp_shape_for(a->q_len);
-  pl.tc = a->kernel == 2;
-  if (pl.tc) {
+  // Auto: the tcgen05 kernel for q_len >= 9 (the 64-row tiles keep the warp-level
+  // kernel shared-memory- and issue-bound there), the warp-level kernel below.
+  pl.tc = a->kernel == 2 || (a->kernel == 0 && a->q_len >= 9);
+  int ctas_per_sm = kCtasPerSm;
+  if (pl.tc) {  // one CTA per SM: a ring of 4-page blocks in up to 227 KB of shared memory
+    ctas_per_sm = 1;
     const int fixed = split_kv_tc_smem_bytes(0);
-    pl.stages = (kSmemPerCta - fixed) / (kStageBytes + 16);
+    pl.stages = (kMaxSmemPerCta - fixed) / (split_kv_tc_block_bytes() + 16);
     if (pl.stages > kMaxStages) pl.stages = kMaxStages;
     pl.smem = split_kv_tc_smem_bytes(pl.stages);
   } else {
@@ -157,7 +162,7 @@ int make_plan(const sqa_args* a, int device, Plan* plan) {
   }
   const long long units_upper = (long long)pl.segments * pages_upper;
   const int min_pages = a->min_pages_per_cta > 0 ? a->min_pages_per_cta : kDefaultMinPagesPerCta;
-  long long grid = a->num_ctas > 0 ? a->num_ctas : (long long)sms * kCtasPerSm;
+  long long grid = a->num_ctas > 0 ? a->num_ctas : (long long)sms * ctas_per_sm;
   if (a->num_ctas <= 0) {
     const long long by_work = (units_upper + min_pages - 1) / min_pages;
     if (by_work < grid) grid = by_work;

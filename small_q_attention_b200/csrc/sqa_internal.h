@@ -83,6 +83,7 @@ int split_kv_smem_bytes(const WarpShape& ws, int num_stages);
 // The tcgen05 / tensor-memory variant of the split-KV kernel (any q_len <= 16).
 cudaError_t launch_split_kv_tc(const SplitKvParams& p, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
                                int grid, int smem_bytes, cudaStream_t stream);
-int split_kv_tc_smem_bytes(int num_stages);
+int split_kv_tc_smem_bytes(int num_blocks);
+int split_kv_tc_block_bytes();
 
 }  // namespace sqa

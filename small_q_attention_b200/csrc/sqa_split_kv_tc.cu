@@ -1,31 +1,32 @@
 // sqa_split_kv_tc.cu -- split-KV paged attention on the 5th-generation tensor
-// cores (tcgen05 + tensor memory), for the larger draft lengths.
+// cores (tcgen05 + tensor memory).
 //
-// Same schedule, TMA page staging, partial/merge outputs and status handling
-// as sqa_split_kv.cu; what changes is who does the math:
+// Same schedule, page table walk, TMA page loads, partial/merge outputs and
+// status handling as sqa_split_kv.cu.  The difference is the math engine:
 //
-// * one thread (the MMA warp) issues, per page, eight tcgen05.mma
-//   M128 x N16 x K16 for S = Q K_page^T into a TMEM slot, and later one
-//   M128 x N128 x K16 for O += P V_page with P read from TMEM.  Q (the 4 * q_len
-//   packed rows, zero-padded to 128) is a 128-byte-swizzled K-major tile in
-//   shared memory; K pages are K-major and V pages MN-major operands, both
-//   straight from the TMA ring.  O (128 fp32 columns) lives in TMEM for a
-//   whole piece;
-// * 32 * SW softmax threads each own one packed query row = one TMEM lane:
-//   the row max and sum need no shuffles.  The running max used for the
-//   exponentials is only raised when a page's max exceeds it by more than
-//   2^8, so O in TMEM is rescaled on few pages (the final 1/l keeps the
-//   result exact); probabilities go back to TMEM as fp16 for the PV product.
+// * Pages are staged in blocks of kBP = 4: a ring slot holds the K low/high
+//   and V low/high 64-dim halves of 4 pages, each half-region contiguous, so
+//   the 64 tokens of a block form one K-major operand (rows 128 B apart, 8-row
+//   groups 1 KB apart) and one MN-major operand for V.
+// * One thread (the MMA warp) issues, per block, eight tcgen05.mma
+//   M128 x N64 x K16 for S = Q K_block^T into a TMEM slot, and kBP
+//   M128 x N128 x K16 for O += P V_block with P read back from TMEM.  Q (the
+//   4 * q_len packed query rows of one KV head, zero-padded to 128) is a
+//   128-byte-swizzled K-major tile in shared memory.  O (128 fp32 columns)
+//   stays in TMEM for a whole piece.  Per-page MMAs (N = 16) were measured
+//   first and were issue-bound at ~100 cycles per instruction.
+// * 32 * SW softmax threads each own one packed query row = one TMEM lane, so
+//   row max and sum need no shuffles.  The max used for the exponentials is
+//   raised only when a block's max exceeds it by more than 2^8; then this
+//   warp's O rows are rescaled in TMEM (rare after the first blocks; the final
+//   1/l keeps the result exact).  P is written as fp16 over the block's S.
 //
-// Pipelines (all mbarriers, all waits bounded):
-//   TMA ring  full[S]/empty[S]      producer -> MMA, released by the MMA commit after PV
-//   S slots   s_full[NS]            MMA (QK commit) -> softmax
-//   P slots   p_full[NS]            softmax -> MMA (PV)
-//   pv_done[NS]                     MMA (PV commit) -> softmax (P slot reuse, O rescale, epilogue)
-//   q_ready                         softmax (Q tile written for the piece) -> MMA
-// The MMA thread keeps QK kNS pages ahead of the softmax: after PV(i) it
-// issues QK(i + kNS) into the slot the softmax has just released, so the
-// softmax never waits for a QK product in the steady state.
+// Pipelines (mbarriers; every wait bounded):
+//   ring   full[NB] / empty[NB]   producer -> MMA; released by the commit after PV
+//   S/P    s_full[2] / p_full[2]  MMA (QK commit) -> softmax -> MMA (PV)
+//   pv_done[2]                    MMA (PV commit) -> S/P slot reuse, O rescale, epilogue
+//   q_ready                       softmax (Q tile of the piece written) -> MMA
+// QK of block g+1 is issued before PV of block g.
 #include "sqa_internal.h"
 #include "sqa_ptx.cuh"
 #include "sqa_schedule.cuh"
@@ -33,81 +34,94 @@
 namespace sqa {
 namespace {
 
-constexpr int kNS = 5;          // S/P slots in TMEM: QK runs up to kNS pages ahead of the softmax
-constexpr int kTmemCols = 256;  // O | S slots | P slots
+constexpr int kBP = 4;                          // pages per block
+constexpr int kBlockTokens = kBP * kPageSize;   // 64
+constexpr int kRegionBytes = kBP * 2048;        // one 64-dim half of K or V for a block
+constexpr int kBlockBytes = 4 * kRegionBytes;   // K lo | K hi | V lo | V hi
+constexpr int kTmemCols = 256;                  // O | S/P slot 0 | S/P slot 1
 constexpr int kColO = 0;
 constexpr int kColS = 128;
-constexpr int kColP = kColS + 16 * kNS;
-constexpr int kQBytes = 128 * 128 * 2;  // Q tile: 128 rows x 128 dims fp16, two 64-dim halves
+constexpr int kSlotCols = kBlockTokens;         // fp32 S of a block; its fp16 P takes the first half
+constexpr int kQBytes = 128 * 128 * 2;          // Q tile: 128 rows x 128 dims fp16, two 64-dim halves
 constexpr float kRescaleLog2 = 8.f;
 constexpr float kLn2 = 0.6931471805599453f;
 
 struct TcSmem {
   uint8_t* q;
-  uint8_t* stages;
+  uint8_t* ring;
   uint64_t *full, *empty, *s_full, *p_full, *pv_done, *q_ready, *mma_done;
   uint32_t* tmem_base;
   Schedule* sch;
 };
 
-__device__ __forceinline__ TcSmem carve(uint8_t* smem, int S) {
+__device__ __forceinline__ TcSmem carve(uint8_t* smem, int nb) {
   TcSmem t;
   t.q = smem;
-  t.stages = smem + kQBytes;
-  uint64_t* b = reinterpret_cast<uint64_t*>(t.stages + (size_t)S * kStageBytes);
+  t.ring = smem + kQBytes;
+  uint64_t* b = reinterpret_cast<uint64_t*>(t.ring + (size_t)nb * kBlockBytes);
   t.full = b;
-  t.empty = t.full + S;
-  t.s_full = t.empty + S;
-  t.p_full = t.s_full + kNS;
-  t.pv_done = t.p_full + kNS;
-  t.q_ready = t.pv_done + kNS;
+  t.empty = t.full + nb;
+  t.s_full = t.empty + nb;
+  t.p_full = t.s_full + 2;
+  t.pv_done = t.p_full + 2;
+  t.q_ready = t.pv_done + 2;
   t.mma_done = t.q_ready + 1;
   t.tmem_base = reinterpret_cast<uint32_t*>(t.mma_done + 1);
   t.sch = reinterpret_cast<Schedule*>(t.tmem_base + 2);
   return t;
 }
 
-// ------------------------------------------------------------------ producer (in-order ring)
+__device__ __forceinline__ int blocks_of(int n) { return (n + kBP - 1) / kBP; }
+
+// ------------------------------------------------------------------ producer
 __device__ void tc_producer(const SplitKvParams& p, const Schedule& sch, const CUtensorMap* tm_k,
                             const CUtensorMap* tm_v, const TcSmem& sm, volatile int* abort) {
   const int lane = threadIdx.x & 31;
   const uint64_t policy = l2_policy_evict_first();
-  const int S = p.num_stages;
+  const int NB = p.num_stages;
   SegWalk w = first_segment(p, sch);
   int slot = 0;
   uint32_t phase = 0;
   unsigned int bad_page = 0;
-  int issued = 0;
+  int issued = 0;  // blocks whose loads were issued (a prefix)
   int unit = sch.start;
   while (unit < sch.end) {
     const int seg_end = w.seg_start + w.pages;
     const int n = min(sch.end, seg_end) - unit;
     const int32_t* row = p.block_tables + (size_t)w.b * p.max_pages + w.pg;
     int ids = (lane < n) ? __ldg(row + lane) : 0;
-    for (int c0 = 0; c0 < n; c0 += 32) {
+    for (int c0 = 0; c0 < n; c0 += 32) {  // 32 is a multiple of kBP: blocks never straddle chunks
       const int cnt = min(32, n - c0);
       const int nxt = c0 + 32 + lane;
       const int ids_next = (nxt < n) ? __ldg(row + nxt) : 0;
-      for (int j = 0; j < cnt; ++j) {
-        int page = __shfl_sync(0xffffffffu, ids, j);
-        if (page < 0 || page >= p.num_pages) {
-          bad_page = 1;
-          page = 0;
+      for (int jb = 0; jb < cnt; jb += kBP) {
+        const int np = min(kBP, cnt - jb);
+        int pages[kBP];
+#pragma unroll
+        for (int j = 0; j < kBP; ++j) {
+          pages[j] = __shfl_sync(0xffffffffu, ids, min(jb + j, 31));
+          if (j < np && (pages[j] < 0 || pages[j] >= p.num_pages)) {
+            bad_page = 1;
+            pages[j] = 0;
+          }
         }
         if (lane == 0) {
           if (mbar_wait_bounded(smem_u32(sm.empty + slot), phase ^ 1u, abort, p.status, 1, issued)) {
             const uint32_t f = smem_u32(sm.full + slot);
-            mbar_arrive_expect_tx(f, kStageBytes);
-            const uint32_t dst = smem_u32(sm.stages + (size_t)slot * kStageBytes);
-            const int tok = page * kPageSize;
-            tma_load_3d(dst, tm_k, f, 0, w.h, tok, policy);
-            tma_load_3d(dst + 2048, tm_k, f, 64, w.h, tok, policy);
-            tma_load_3d(dst + 4096, tm_v, f, 0, w.h, tok, policy);
-            tma_load_3d(dst + 6144, tm_v, f, 64, w.h, tok, policy);
+            mbar_arrive_expect_tx(f, np * kStageBytes);
+            const uint32_t base = smem_u32(sm.ring + (size_t)slot * kBlockBytes);
+            for (int j = 0; j < np; ++j) {
+              const int tok = pages[j] * kPageSize;
+              const uint32_t dst = base + j * 2048;
+              tma_load_3d(dst, tm_k, f, 0, w.h, tok, policy);
+              tma_load_3d(dst + kRegionBytes, tm_k, f, 64, w.h, tok, policy);
+              tma_load_3d(dst + 2 * kRegionBytes, tm_v, f, 0, w.h, tok, policy);
+              tma_load_3d(dst + 3 * kRegionBytes, tm_v, f, 64, w.h, tok, policy);
+            }
             ++issued;
           }
         }
-        if (++slot == S) {
+        if (++slot == NB) {
           slot = 0;
           phase ^= 1u;
         }
@@ -120,9 +134,9 @@ __device__ void tc_producer(const SplitKvParams& p, const Schedule& sch, const C
   }
   if (__any_sync(0xffffffffu, bad_page) && lane == 0) atomicOr(p.status, 8u);  // SQA_DEV_BAD_PAGE
   if (lane == 0 && *abort) {  // only an abort can leave loads in flight
-    for (int k = 0; k < min(issued, S); ++k) {
-      const int last = k + S * ((issued - 1 - k) / S);
-      if (!mbar_drain(smem_u32(sm.full + k), (uint32_t)(last / S) & 1u, 100000000ull)) atomicOr(p.status, 1u);
+    for (int k = 0; k < min(issued, NB); ++k) {
+      const int last = k + NB * ((issued - 1 - k) / NB);
+      if (!mbar_drain(smem_u32(sm.full + k), (uint32_t)(last / NB) & 1u, 100000000ull)) atomicOr(p.status, 1u);
     }
   }
 }
@@ -130,49 +144,59 @@ __device__ void tc_producer(const SplitKvParams& p, const Schedule& sch, const C
 // ------------------------------------------------------------------ MMA issuer (one thread)
 __device__ void tc_mma(const SplitKvParams& p, const Schedule& sch, const TcSmem& sm, uint32_t tmem,
                        volatile int* abort) {
-  constexpr uint32_t kIdescQK = mma_idesc_f16(128, 16, false, false);  // Q (K-major) x K page (K-major)
-  constexpr uint32_t kIdescPV = mma_idesc_f16(128, 128, false, true);  // P (TMEM) x V page (MN-major)
-  const int S = p.num_stages;
+  constexpr uint32_t kIdescQK = mma_idesc_f16(128, kBlockTokens, false, false);  // Q x K_block, both K-major
+  constexpr uint32_t kIdescPV = mma_idesc_f16(128, 128, false, true);           // P (TMEM) x V (MN-major)
+  const int NB = p.num_stages;
   const uint32_t q_base = smem_u32(sm.q);
   SegWalk w = first_segment(p, sch);
-  int i0 = 0;  // CTA page counter at the start of the piece
-  int pc = 0;  // piece counter
+  int gb0 = 0;  // CTA block counter at the start of the piece
+  int pc = 0;   // piece counter
   int unit = sch.start;
+
+  // S(h) = Q K_h^T into slot h & 1, once PV(h - 2) has released that slot.
+  auto issue_qk = [&](int h) {
+    if (h >= 2)
+      mbar_wait_bounded(smem_u32(sm.pv_done + (h & 1)), (uint32_t)((h - 2) >> 1) & 1u, abort, p.status, 11, h);
+    const int slot = h % NB;
+    mbar_wait_bounded(smem_u32(sm.full + slot), (uint32_t)(h / NB) & 1u, abort, p.status, 5, h);
+    tc_fence_after();
+    const uint32_t k_base = smem_u32(sm.ring + (size_t)slot * kBlockBytes);
+    const uint32_t d = tmem + kColS + (h & 1) * kSlotCols;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      const uint32_t off = (kk & 3) * 32u;
+      const uint64_t a = smem_desc_sw128(q_base + (kk >> 2) * (kQBytes / 2) + off, 16, 1024);
+      const uint64_t b = smem_desc_sw128(k_base + (kk >> 2) * kRegionBytes + off, 16, 1024);
+      tc_mma_ss(d, a, b, kIdescQK, kk > 0 ? 1u : 0u);
+    }
+    tc_commit(smem_u32(sm.s_full + (h & 1)));
+  };
+
   while (unit < sch.end) {
     const int seg_end = w.seg_start + w.pages;
     const int n = min(sch.end, seg_end) - unit;
+    const int nblk = blocks_of(n);
     mbar_wait_bounded(smem_u32(sm.q_ready), (uint32_t)(pc & 1), abort, p.status, 4, pc);
     tc_fence_after();
-    // S(g) = Q K_g^T into slot g % kNS
-    auto issue_qk = [&](int g) {
-      const int st = g % S;
-      mbar_wait_bounded(smem_u32(sm.full + st), (uint32_t)(g / S) & 1u, abort, p.status, 5, g);
+    issue_qk(gb0);
+    for (int k = 0; k < nblk; ++k) {
+      const int g = gb0 + k;
+      if (k + 1 < nblk) issue_qk(g + 1);
+      const int slot = g % NB;
+      const int np = min(kBP, n - k * kBP);
+      mbar_wait_bounded(smem_u32(sm.p_full + (g & 1)), (uint32_t)(g >> 1) & 1u, abort, p.status, 6, g);
       tc_fence_after();
-      const uint32_t k_base = smem_u32(sm.stages + (size_t)st * kStageBytes);
-      const uint32_t d = tmem + kColS + (g % kNS) * 16;
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const uint32_t off = (kk & 3) * 32u;
-        const uint64_t a = smem_desc_sw128(q_base + (kk >> 2) * (kQBytes / 2) + off, 16, 1024);
-        const uint64_t b = smem_desc_sw128(k_base + (kk >> 2) * 2048 + off, 16, 1024);
-        tc_mma_ss(d, a, b, kIdescQK, kk > 0 ? 1u : 0u);
+      const uint32_t v_base = smem_u32(sm.ring + (size_t)slot * kBlockBytes + 2 * kRegionBytes);
+      const uint32_t p_col = tmem + kColS + (g & 1) * kSlotCols;
+      for (int kk = 0; kk < np; ++kk) {  // 16 tokens (one page) per step
+        // MN atoms (64 dims) kRegionBytes apart: V lo -> V hi; K atoms (8 tokens) 1 KB apart
+        const uint64_t b = smem_desc_sw128(v_base + kk * 2048, kRegionBytes, 1024);
+        tc_mma_ts(tmem + kColO, p_col + kk * 8, b, kIdescPV, (k > 0 || kk > 0) ? 1u : 0u);
       }
-      tc_commit(smem_u32(sm.s_full + (g % kNS)));
-    };
-    for (int j = 0; j < min(n, kNS); ++j) issue_qk(i0 + j);
-    for (int j = 0; j < n; ++j) {  // O += P(g) V_g, then refill the freed slot
-      const int g = i0 + j;
-      const int st = g % S;
-      mbar_wait_bounded(smem_u32(sm.p_full + (g % kNS)), (uint32_t)(g / kNS) & 1u, abort, p.status, 6, g);
-      tc_fence_after();
-      const uint32_t v_base = smem_u32(sm.stages + (size_t)st * kStageBytes + 4096);
-      const uint64_t b = smem_desc_sw128(v_base, 2048, 1024);  // MN atoms: V lo -> V hi; K atoms: 8 tokens
-      tc_mma_ts(tmem + kColO, tmem + kColP + (g % kNS) * 8, b, kIdescPV, j > 0 ? 1u : 0u);
-      tc_commit(smem_u32(sm.empty + st));           // the page's stage may be refilled
-      tc_commit(smem_u32(sm.pv_done + (g % kNS)));  // P slot free, O up to date
-      if (j + kNS < n) issue_qk(g + kNS);           // the softmax has read S(g): reuse its slot
+      tc_commit(smem_u32(sm.empty + slot));       // the block's ring slot may be refilled
+      tc_commit(smem_u32(sm.pv_done + (g & 1)));  // S/P slot free, O up to date
     }
-    i0 += n;
+    gb0 += nblk;
     ++pc;
     unit += n;
     if (unit >= seg_end) next_segment(p, w);
@@ -194,14 +218,16 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
   const int row = warp * 32 + lane;  // = TMEM lane
   const bool active = row < rows;
   const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
+  const int NB = p.num_stages;
 
   SegWalk w = first_segment(p, sch);
-  int i0 = 0;
+  int gb0 = 0;
   int unit = sch.start;
   while (unit < sch.end) {
     const int s = w.b * p.hkv + w.h;
     const int seg_end = w.seg_start + w.pages;
     const int n = min(sch.end, seg_end) - unit;
+    const int nblk = blocks_of(n);
     const bool whole = (unit == w.seg_start) && (seg_end <= sch.end);
     if (tid == 0 && unit == w.seg_start) {
       const int last_cta = (seg_end - 1) / sch.per_cta;
@@ -210,11 +236,11 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
     const int len_raw = __ldg(p.seq_lens + w.b);
     const int len = min(len_raw, w.pages * kPageSize);
     const int mlen = p.mask_lens ? __ldg(p.mask_lens + w.b) : len_raw;
-    const int thr_min = min(len, mlen - p.q_len + 1);
     const int thr = min(len, mlen - p.q_len + (row >> 2) + 1);
+    const int thr_min = min(len, mlen - p.q_len + 1);  // visible tokens of draft row 0
 
     // Q tile of this piece: rows < 4*q_len, 128-byte swizzled, two 64-dim halves.
-    // (All QK products of the previous piece are complete: every S slot was consumed.)
+    // (Every QK product of the previous piece is complete: all its S blocks were consumed.)
     for (int c = tid; c < rows * 16; c += SW * 32) {
       const int r = c >> 4, ch = c & 15;
       const __half* src =
@@ -227,32 +253,39 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
     if (lane == 0) mbar_arrive(smem_u32(sm.q_ready));
 
     float m_used = -INFINITY, l = 0.f;
-    for (int j = 0; j < n; ++j) {
-      const int g = i0 + j;
-      const int sl = g % kNS;
-      const int tok0 = (w.pg + j) * kPageSize;
-      mbar_wait_bounded(smem_u32(sm.s_full + sl), (uint32_t)(g / kNS) & 1u, abort, p.status, 7, g);
+    for (int k = 0; k < nblk; ++k) {
+      const int g = gb0 + k;
+      const int np = min(kBP, n - k * kBP);
+      const int tok0 = (w.pg + k * kBP) * kPageSize;  // first token of the block
+      const int valid_cols = np * kPageSize;
+      mbar_wait_bounded(smem_u32(sm.s_full + (g & 1)), (uint32_t)(g >> 1) & 1u, abort, p.status, 7, g);
       tc_fence_after();
-      uint32_t raw[16];
-      tmem_ld16(tl + kColS + sl * 16, raw);
+      const uint32_t slot_col = tl + kColS + (g & 1) * kSlotCols;
+      uint32_t sraw[kBlockTokens];
+      tmem_ld64(slot_col, sraw);
       tmem_wait_ld();
-      float x[16];
-      const bool masked = tok0 + kPageSize > thr_min;
-      float mx = -INFINITY;
+      // Scores stay unscaled until the exponent: max(c * s) = c * max(s) for c > 0.
+      // mask a block that is partial (pages past the piece hold stale data) or
+      // that reaches the causal tail / the sequence end
+      if (valid_cols < kBlockTokens || tok0 + kBlockTokens > thr_min) {
 #pragma unroll
-      for (int t = 0; t < 16; ++t) {
-        x[t] = __uint_as_float(raw[t]) * p.scale_log2;
-        if (masked && tok0 + t >= thr) x[t] = -INFINITY;
-        mx = fmaxf(mx, x[t]);
+        for (int t = 0; t < kBlockTokens; ++t)
+          if (t >= valid_cols || tok0 + t >= thr) sraw[t] = 0xff800000u;  // -inf
       }
-      const float m_new = fmaxf(m_used, mx);
+      float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+      for (int t = 0; t < kBlockTokens; t += 2) {
+        mx0 = fmaxf(mx0, __uint_as_float(sraw[t]));
+        mx1 = fmaxf(mx1, __uint_as_float(sraw[t + 1]));
+      }
+      const float m_new = fmaxf(m_used, fmaxf(mx0, mx1) * p.scale_log2);
       const bool need = active && (m_new > m_used + kRescaleLog2);
-      if (j == 0) {
+      if (k == 0) {
         m_used = m_new;  // the piece's first PV overwrites O
       } else if (__any_sync(0xffffffffu, need)) {
         // O must be stable: wait for PV(g - 1), then rescale this warp's rows in TMEM
-        mbar_wait_bounded(smem_u32(sm.pv_done + ((g - 1) % kNS)), (uint32_t)((g - 1) / kNS) & 1u, abort,
-                          p.status, 8, g);
+        mbar_wait_bounded(smem_u32(sm.pv_done + ((g - 1) & 1)), (uint32_t)((g - 1) >> 1) & 1u, abort, p.status, 8,
+                          g);
         tc_fence_after();
         const float alpha = need ? ex2(m_used - m_new) : 1.f;
         if (need) {
@@ -270,39 +303,44 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
         }
         tmem_wait_st();
       }
-      const float base = (m_used == -INFINITY) ? 0.f : m_used;
-      uint32_t pk[8];
+      // p = 2^(c*s - m): one FFMA and one ex2 per score; P as fp16 over the
+      // first half of the block's S columns (already read above)
+      const float nbase = active ? -((m_used == -INFINITY) ? 0.f : m_used) : -INFINITY;
+      const float cs = p.scale_log2;
+      uint32_t pk[kBlockTokens / 2];
+      float ls[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int t = 0; t < 8; ++t) {
-        const float p0 = active ? ex2(x[2 * t] - base) : 0.f;
-        const float p1 = active ? ex2(x[2 * t + 1] - base) : 0.f;
-        l += p0 + p1;
+      for (int t = 0; t < kBlockTokens / 2; ++t) {
+        const float p0 = ex2(fmaf(__uint_as_float(sraw[2 * t]), cs, nbase));
+        const float p1 = ex2(fmaf(__uint_as_float(sraw[2 * t + 1]), cs, nbase));
+        ls[t & 3] += p0 + p1;
         pk[t] = pack_half2(p0, p1);
       }
-      if (g >= kNS)  // PV(g - kNS) has read this P slot
-        mbar_wait_bounded(smem_u32(sm.pv_done + sl), (uint32_t)((g - kNS) / kNS) & 1u, abort, p.status, 9, g);
-      tc_fence_after();
-      tmem_st8(tl + kColP + sl * 8, pk);
+      l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+      tmem_st32(slot_col, pk);
       tmem_wait_st();
-      if (tok0 + kPageSize > len && warp == 0) {
+      if (tok0 + valid_cols > len && warp == 0) {
         // tokens at or past the sequence end: zero their V rows (the pool may hold NaN there)
-        uint8_t* vst = sm.stages + (size_t)(g % p.num_stages) * kStageBytes + 4096;
-        const int first = max(len - tok0, 0);
-        for (int c = lane; c < (kPageSize - first) * 16; c += 32) {
-          const int r = first + (c >> 4);
-          *reinterpret_cast<uint4*>(vst + ((c >> 3) & 1) * 2048 + r * 128 + (c & 7) * 16) =
-              make_uint4(0u, 0u, 0u, 0u);
+        uint8_t* vreg = sm.ring + (size_t)(g % NB) * kBlockBytes + 2 * kRegionBytes;
+        for (int j = 0; j < np; ++j) {
+          const int first = max(len - (tok0 + j * kPageSize), 0);
+          if (first >= kPageSize) continue;
+          for (int c = lane; c < (kPageSize - first) * 16; c += 32) {
+            const int r = first + (c >> 4);
+            *reinterpret_cast<uint4*>(vreg + ((c >> 3) & 1) * kRegionBytes + j * 2048 + r * 128 + (c & 7) * 16) =
+                make_uint4(0u, 0u, 0u, 0u);
+          }
         }
         fence_proxy_async_smem();
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(sm.p_full + sl));
+      if (lane == 0) mbar_arrive(smem_u32(sm.p_full + (g & 1)));
     }
 
     // ---- epilogue: O is complete once the piece's last PV has finished
-    const int gl = i0 + n - 1;
-    mbar_wait_bounded(smem_u32(sm.pv_done + (gl % kNS)), (uint32_t)(gl / kNS) & 1u, abort, p.status, 10, gl);
+    const int gl = gb0 + nblk - 1;
+    mbar_wait_bounded(smem_u32(sm.pv_done + (gl & 1)), (uint32_t)(gl >> 1) & 1u, abort, p.status, 10, gl);
     tc_fence_after();
     const float inv = (l > 0.f) ? 1.f / l : 0.f;
     const float lse = (l > 0.f) ? (m_used + __log2f(l)) * kLn2 : -INFINITY;
@@ -344,7 +382,7 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
     }
     tc_fence_before();  // O reads are done before the next piece's first PV overwrites it
 
-    i0 += n;
+    gb0 += nblk;
     unit += n;
     if (unit >= seg_end) next_segment(p, w);
     else w.pg += n;
@@ -352,7 +390,7 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
 }
 
 template <int SW>
-__global__ void __launch_bounds__((SW + 2) * 32, 2)
+__global__ void __launch_bounds__((SW + 2) * 32, 1)
     sqa_split_kv_tc_kernel(const SplitKvParams p, const __grid_constant__ CUtensorMap tm_k,
                            const __grid_constant__ CUtensorMap tm_v) {
   extern __shared__ uint8_t smem_raw[];
@@ -372,7 +410,7 @@ __global__ void __launch_bounds__((SW + 2) * 32, 2)
       mbar_init(smem_u32(sm.full + i), 1);
       mbar_init(smem_u32(sm.empty + i), 1);
     }
-    for (int i = 0; i < kNS; ++i) {
+    for (int i = 0; i < 2; ++i) {
       mbar_init(smem_u32(sm.s_full + i), 1);
       mbar_init(smem_u32(sm.p_full + i), SW);
       mbar_init(smem_u32(sm.pv_done + i), 1);
@@ -456,8 +494,10 @@ cudaError_t launch_tc(const SplitKvParams& p, const CUtensorMap& tm_k, const CUt
 
 }  // namespace
 
-int split_kv_tc_smem_bytes(int num_stages) {
-  return 1024 + kQBytes + num_stages * kStageBytes + (2 * num_stages + 3 * kNS + 2) * 8 + 8 + 64;
+int split_kv_tc_block_bytes() { return kBlockBytes; }
+
+int split_kv_tc_smem_bytes(int num_blocks) {
+  return 1024 + kQBytes + num_blocks * kBlockBytes + (2 * num_blocks + 8) * 8 + 8 + 64;
 }
 
 cudaError_t launch_split_kv_tc(const SplitKvParams& p, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
