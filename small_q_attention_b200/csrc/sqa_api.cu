@@ -137,9 +137,9 @@ int make_plan(const sqa_args* a, int device, Plan* plan) {
   if (sms <= 0) return SQA_ERR_CUDA;
   Plan pl;
   pl.shape = warp_shape_for(a->q_len);
-  // Auto: the tcgen05 kernel for q_len >= 9 (the 64-row tiles keep the warp-level
-  // kernel shared-memory- and issue-bound there), the warp-level kernel below.
-  pl.tc = a->kernel == 2 || (a->kernel == 0 && a->q_len >= 9);
+  // Auto: the tcgen05 kernel for q_len >= 5 (measured faster on B200 at every
+  // batch and length from q_len 8 up), the warp-level kernel below.
+  pl.tc = a->kernel == 2 || (a->kernel == 0 && a->q_len >= 5);
   int ctas_per_sm = kCtasPerSm;
   if (pl.tc) {  // one CTA per SM: a ring of 4-page blocks in up to 227 KB of shared memory
     ctas_per_sm = 1;

@@ -8,25 +8,30 @@
 //   and V low/high 64-dim halves of 4 pages, each half-region contiguous, so
 //   the 64 tokens of a block form one K-major operand (rows 128 B apart, 8-row
 //   groups 1 KB apart) and one MN-major operand for V.
-// * One thread (the MMA warp) issues, per block, eight tcgen05.mma
-//   M128 x N64 x K16 for S = Q K_block^T into a TMEM slot, and kBP
-//   M128 x N128 x K16 for O += P V_block with P read back from TMEM.  Q (the
-//   4 * q_len packed query rows of one KV head, zero-padded to 128) is a
-//   128-byte-swizzled K-major tile in shared memory.  O (128 fp32 columns)
-//   stays in TMEM for a whole piece.  Per-page MMAs (N = 16) were measured
-//   first and were issue-bound at ~100 cycles per instruction.
-// * 32 * SW softmax threads each own one packed query row = one TMEM lane, so
-//   row max and sum need no shuffles.  The max used for the exponentials is
-//   raised only when a block's max exceeds it by more than 2^8; then this
-//   warp's O rows are rescaled in TMEM (rare after the first blocks; the final
-//   1/l keeps the result exact).  P is written as fp16 over the block's S.
+// * Q lives in tensor memory for a whole piece, replicated R times down the
+//   128 lanes (R = 4 for q_len <= 8, 2 for q_len <= 16): lane 128/R * r + i
+//   holds packed query row i (row i = draft token i/4, head i%4 of the group).
+//   Per block the MMA warp issues eight M128 x N64 x K16 MMAs for
+//   S = Q K_block^T (A = Q from TMEM, B = K from shared memory) into one of
+//   four S slots, and kBP M128 x N128 x K16 MMAs for O += P V_page with P read
+//   back from TMEM.  Replica r owns pages [4/R r, 4/R (r+1)) of every block:
+//   the PV MMA of a page writes only the lanes of its replica (the MMA's
+//   output-lane mask), so every replica keeps its own running (O, max, sum)
+//   and the replicas are merged once per piece through shared memory.
+// * Four softmax warps, one per TMEM lane quadrant; each thread owns one row
+//   of one replica and reads only its replica's 64/R S columns of a block, so
+//   the exponentials of a block are spread over all four warps.  The max used
+//   for the exponentials is raised only when a block's max exceeds it by more
+//   than 2^8; then the warp's O rows are rescaled in TMEM.  P (fp16) is written
+//   over the block's S columns.
+// * The MMA warp runs converged and issues through elect.sync.
 //
 // Pipelines (mbarriers; every wait bounded):
 //   ring   full[NB] / empty[NB]   producer -> MMA; released by the commit after PV
-//   S/P    s_full[2] / p_full[2]  MMA (QK commit) -> softmax -> MMA (PV)
-//   pv_done[2]                    MMA (PV commit) -> S/P slot reuse, O rescale, epilogue
-//   q_ready                       softmax (Q tile of the piece written) -> MMA
-// QK of block g+1 is issued before PV of block g.
+//   S/P    s_full[4] / p_full[4]  MMA (QK commit) -> softmax -> MMA (PV)
+//   pv_done[4]                    MMA (PV commit) -> S/P slot reuse, O rescale, epilogue
+//   q_ready                       softmax (Q of the piece in TMEM) -> MMA
+// QK of block g+2 is issued before PV of block g.
 #include "sqa_internal.h"
 #include "sqa_ptx.cuh"
 #include "sqa_schedule.cuh"
@@ -38,17 +43,25 @@ constexpr int kBP = 4;                          // pages per block
 constexpr int kBlockTokens = kBP * kPageSize;   // 64
 constexpr int kRegionBytes = kBP * 2048;        // one 64-dim half of K or V for a block
 constexpr int kBlockBytes = 4 * kRegionBytes;   // K lo | K hi | V lo | V hi
-constexpr int kTmemCols = 256;                  // O | S/P slot 0 | S/P slot 1
+constexpr int kTmemCols = 512;                  // O | Q | S/P slots 0..3
 constexpr int kColO = 0;
-constexpr int kColS = 128;
+constexpr int kColQ = 128;                      // 128 fp16 dims = 64 columns
+constexpr int kColS = 192;
+constexpr int kNumS = 4;
 constexpr int kSlotCols = kBlockTokens;         // fp32 S of a block; its fp16 P takes the first half
-constexpr int kQBytes = 128 * 128 * 2;          // Q tile: 128 rows x 128 dims fp16, two 64-dim halves
+constexpr int kSoftmaxWarps = 4;
+constexpr int kThreadsTc = (kSoftmaxWarps + 2) * 32;
+constexpr int kMergeCols = 64;                  // dims merged per pass
+constexpr int kMergeStride = kMergeCols + 1;    // floats per merge row (conflict-free columns)
+constexpr int kMergeBytes = 128 * kMergeStride * 4;  // one row per TMEM lane
+constexpr int kMlBytes = 128 * 8;               // (max, sum) per lane
 constexpr float kRescaleLog2 = 8.f;
 constexpr float kLn2 = 0.6931471805599453f;
 
 struct TcSmem {
-  uint8_t* q;
   uint8_t* ring;
+  float* merge;
+  float2* ml;
   uint64_t *full, *empty, *s_full, *p_full, *pv_done, *q_ready, *mma_done;
   uint32_t* tmem_base;
   Schedule* sch;
@@ -56,15 +69,16 @@ struct TcSmem {
 
 __device__ __forceinline__ TcSmem carve(uint8_t* smem, int nb) {
   TcSmem t;
-  t.q = smem;
-  t.ring = smem + kQBytes;
-  uint64_t* b = reinterpret_cast<uint64_t*>(t.ring + (size_t)nb * kBlockBytes);
+  t.ring = smem;
+  t.merge = reinterpret_cast<float*>(smem + (size_t)nb * kBlockBytes);
+  t.ml = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(t.merge) + kMergeBytes);
+  uint64_t* b = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(t.ml) + kMlBytes);
   t.full = b;
   t.empty = t.full + nb;
   t.s_full = t.empty + nb;
-  t.p_full = t.s_full + 2;
-  t.pv_done = t.p_full + 2;
-  t.q_ready = t.pv_done + 2;
+  t.p_full = t.s_full + kNumS;
+  t.pv_done = t.p_full + kNumS;
+  t.q_ready = t.pv_done + kNumS;
   t.mma_done = t.q_ready + 1;
   t.tmem_base = reinterpret_cast<uint32_t*>(t.mma_done + 1);
   t.sch = reinterpret_cast<Schedule*>(t.tmem_base + 2);
@@ -73,7 +87,7 @@ __device__ __forceinline__ TcSmem carve(uint8_t* smem, int nb) {
 
 __device__ __forceinline__ int blocks_of(int n) { return (n + kBP - 1) / kBP; }
 
-// ------------------------------------------------------------------ producer
+// ------------------------------------------------------------------ producer (whole warp)
 __device__ void tc_producer(const SplitKvParams& p, const Schedule& sch, const CUtensorMap* tm_k,
                             const CUtensorMap* tm_v, const TcSmem& sm, volatile int* abort) {
   const int lane = threadIdx.x & 31;
@@ -105,8 +119,10 @@ __device__ void tc_producer(const SplitKvParams& p, const Schedule& sch, const C
             pages[j] = 0;
           }
         }
-        if (lane == 0) {
-          if (mbar_wait_bounded(smem_u32(sm.empty + slot), phase ^ 1u, abort, p.status, 1, issued)) {
+        bool ok = mbar_wait_bounded(smem_u32(sm.empty + slot), phase ^ 1u, abort, p.status, 1, issued);
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        if (ok) {
+          if (elect_one()) {
             const uint32_t f = smem_u32(sm.full + slot);
             mbar_arrive_expect_tx(f, np * kStageBytes);
             const uint32_t base = smem_u32(sm.ring + (size_t)slot * kBlockBytes);
@@ -118,8 +134,9 @@ __device__ void tc_producer(const SplitKvParams& p, const Schedule& sch, const C
               tma_load_3d(dst + 2 * kRegionBytes, tm_v, f, 0, w.h, tok, policy);
               tma_load_3d(dst + 3 * kRegionBytes, tm_v, f, 64, w.h, tok, policy);
             }
-            ++issued;
           }
+          __syncwarp();
+          ++issued;
         }
         if (++slot == NB) {
           slot = 0;
@@ -141,35 +158,40 @@ __device__ void tc_producer(const SplitKvParams& p, const Schedule& sch, const C
   }
 }
 
-// ------------------------------------------------------------------ MMA issuer (one thread)
+// ------------------------------------------------------------------ MMA issuer (whole warp, one elected lane)
+template <int R>
 __device__ void tc_mma(const SplitKvParams& p, const Schedule& sch, const TcSmem& sm, uint32_t tmem,
                        volatile int* abort) {
-  constexpr uint32_t kIdescQK = mma_idesc_f16(128, kBlockTokens, false, false);  // Q x K_block, both K-major
+  constexpr uint32_t kIdescQK = mma_idesc_f16(128, kBlockTokens, false, false);  // Q (TMEM) x K_block (K-major)
   constexpr uint32_t kIdescPV = mma_idesc_f16(128, 128, false, true);           // P (TMEM) x V (MN-major)
+  constexpr int kPPR = kBP / R;       // pages of a block per replica
+  constexpr int kLanesPR = 128 / R;   // TMEM lanes per replica
   const int NB = p.num_stages;
-  const uint32_t q_base = smem_u32(sm.q);
   SegWalk w = first_segment(p, sch);
   int gb0 = 0;  // CTA block counter at the start of the piece
   int pc = 0;   // piece counter
   int unit = sch.start;
 
-  // S(h) = Q K_h^T into slot h & 1, once PV(h - 2) has released that slot.
+  // S(h) = Q K_h^T into slot h % 4, once PV(h - 4) has released that slot.
   auto issue_qk = [&](int h) {
-    if (h >= 2)
-      mbar_wait_bounded(smem_u32(sm.pv_done + (h & 1)), (uint32_t)((h - 2) >> 1) & 1u, abort, p.status, 11, h);
+    if (h >= kNumS)
+      mbar_wait_bounded(smem_u32(sm.pv_done + (h % kNumS)), (uint32_t)((h - kNumS) / kNumS) & 1u, abort,
+                        p.status, 11, h);
     const int slot = h % NB;
     mbar_wait_bounded(smem_u32(sm.full + slot), (uint32_t)(h / NB) & 1u, abort, p.status, 5, h);
+    __syncwarp();
     tc_fence_after();
-    const uint32_t k_base = smem_u32(sm.ring + (size_t)slot * kBlockBytes);
-    const uint32_t d = tmem + kColS + (h & 1) * kSlotCols;
+    if (elect_one()) {
+      const uint32_t k_base = smem_u32(sm.ring + (size_t)slot * kBlockBytes);
+      const uint32_t d = tmem + kColS + (h % kNumS) * kSlotCols;
 #pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-      const uint32_t off = (kk & 3) * 32u;
-      const uint64_t a = smem_desc_sw128(q_base + (kk >> 2) * (kQBytes / 2) + off, 16, 1024);
-      const uint64_t b = smem_desc_sw128(k_base + (kk >> 2) * kRegionBytes + off, 16, 1024);
-      tc_mma_ss(d, a, b, kIdescQK, kk > 0 ? 1u : 0u);
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint64_t b = smem_desc_sw128(k_base + (kk >> 2) * kRegionBytes + (kk & 3) * 32u, 16, 1024);
+        tc_mma_ts(d, tmem + kColQ + kk * 8, b, kIdescQK, kk > 0 ? 1u : 0u);
+      }
+      tc_commit(smem_u32(sm.s_full + (h % kNumS)));
     }
-    tc_commit(smem_u32(sm.s_full + (h & 1)));
+    __syncwarp();
   };
 
   while (unit < sch.end) {
@@ -177,24 +199,35 @@ __device__ void tc_mma(const SplitKvParams& p, const Schedule& sch, const TcSmem
     const int n = min(sch.end, seg_end) - unit;
     const int nblk = blocks_of(n);
     mbar_wait_bounded(smem_u32(sm.q_ready), (uint32_t)(pc & 1), abort, p.status, 4, pc);
+    __syncwarp();
     tc_fence_after();
     issue_qk(gb0);
+    if (nblk > 1) issue_qk(gb0 + 1);
     for (int k = 0; k < nblk; ++k) {
       const int g = gb0 + k;
-      if (k + 1 < nblk) issue_qk(g + 1);
+      if (k + 2 < nblk) issue_qk(g + 2);
       const int slot = g % NB;
       const int np = min(kBP, n - k * kBP);
-      mbar_wait_bounded(smem_u32(sm.p_full + (g & 1)), (uint32_t)(g >> 1) & 1u, abort, p.status, 6, g);
+      mbar_wait_bounded(smem_u32(sm.p_full + (g % kNumS)), (uint32_t)(g / kNumS) & 1u, abort, p.status, 6, g);
+      __syncwarp();
       tc_fence_after();
-      const uint32_t v_base = smem_u32(sm.ring + (size_t)slot * kBlockBytes + 2 * kRegionBytes);
-      const uint32_t p_col = tmem + kColS + (g & 1) * kSlotCols;
-      for (int kk = 0; kk < np; ++kk) {  // 16 tokens (one page) per step
-        // MN atoms (64 dims) kRegionBytes apart: V lo -> V hi; K atoms (8 tokens) 1 KB apart
-        const uint64_t b = smem_desc_sw128(v_base + kk * 2048, kRegionBytes, 1024);
-        tc_mma_ts(tmem + kColO, p_col + kk * 8, b, kIdescPV, (k > 0 || kk > 0) ? 1u : 0u);
+      if (elect_one()) {
+        const uint32_t v_base = smem_u32(sm.ring + (size_t)slot * kBlockBytes + 2 * kRegionBytes);
+        const uint32_t p_col = tmem + kColS + (g % kNumS) * kSlotCols;
+        for (int kk = 0; kk < np; ++kk) {  // 16 tokens (one page) per step
+          const int rep = kk / kPPR;
+          uint32_t off[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) off[e] = (e * 32 >= rep * kLanesPR && e * 32 < (rep + 1) * kLanesPR) ? 0u : ~0u;
+          // MN atoms (64 dims) kRegionBytes apart: V lo -> V hi; K atoms (8 tokens) 1 KB apart
+          const uint64_t b = smem_desc_sw128(v_base + kk * 2048, kRegionBytes, 1024);
+          // a replica's first page of the piece overwrites its O rows
+          tc_mma_ts_lanes(tmem + kColO, p_col + kk * 8, b, kIdescPV, (k > 0 || (kk % kPPR) != 0) ? 1u : 0u, off);
+        }
+        tc_commit(smem_u32(sm.empty + slot));              // the block's ring slot may be refilled
+        tc_commit(smem_u32(sm.pv_done + (g % kNumS)));     // S/P slot free, O up to date
       }
-      tc_commit(smem_u32(sm.empty + slot));       // the block's ring slot may be refilled
-      tc_commit(smem_u32(sm.pv_done + (g & 1)));  // S/P slot free, O up to date
+      __syncwarp();
     }
     gb0 += nblk;
     ++pc;
@@ -202,21 +235,26 @@ __device__ void tc_mma(const SplitKvParams& p, const Schedule& sch, const TcSmem
     if (unit >= seg_end) next_segment(p, w);
     else w.pg += n;
   }
-  // every MMA this thread issued must finish before TMEM is released
-  tc_commit(smem_u32(sm.mma_done));
-  if (!mbar_drain(smem_u32(sm.mma_done), 0u, 2000000000ull)) atomicOr(p.status, 1u);
+  // every MMA this warp issued must finish before TMEM is released
+  if (elect_one()) tc_commit(smem_u32(sm.mma_done));
+  __syncwarp();
+  if (!mbar_drain(smem_u32(sm.mma_done), 0u, 2000000000ull) && (threadIdx.x & 31) == 0) atomicOr(p.status, 1u);
 }
 
-// ------------------------------------------------------------------ softmax + epilogue
-template <int SW>
+// ------------------------------------------------------------------ softmax + epilogue (4 warps)
+template <int R>
 __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const TcSmem& sm, uint32_t tmem,
                            volatile int* abort) {
+  constexpr int kLanesPR = 128 / R;          // lanes (rows) per replica
+  constexpr int kTok = kBlockTokens / R;     // tokens of a block per replica
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int tid = threadIdx.x;  // 0 .. 32*SW-1
-  const int rows = kGroup * p.q_len;
-  const int row = warp * 32 + lane;  // = TMEM lane
-  const bool active = row < rows;
+  const int tid = threadIdx.x;               // 0 .. 127
+  const int rows = kGroup * p.q_len;         // <= kLanesPR
+  const int rep = (warp * 32) / kLanesPR;    // replica of this warp
+  const int lrow = warp * 32 + lane - rep * kLanesPR;  // packed query row of this thread
+  const bool active = lrow < rows;
+  const int tok_lo = rep * kTok;             // first block column of this replica
   const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
   const int NB = p.num_stages;
 
@@ -236,19 +274,30 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
     const int len_raw = __ldg(p.seq_lens + w.b);
     const int len = min(len_raw, w.pages * kPageSize);
     const int mlen = p.mask_lens ? __ldg(p.mask_lens + w.b) : len_raw;
-    const int thr = min(len, mlen - p.q_len + (row >> 2) + 1);
+    const int thr = min(len, mlen - p.q_len + (lrow >> 2) + 1);
     const int thr_min = min(len, mlen - p.q_len + 1);  // visible tokens of draft row 0
 
-    // Q tile of this piece: rows < 4*q_len, 128-byte swizzled, two 64-dim halves.
+    // Q of this piece into TMEM: this thread's lane gets packed row lrow (zeros past the rows).
     // (Every QK product of the previous piece is complete: all its S blocks were consumed.)
-    for (int c = tid; c < rows * 16; c += SW * 32) {
-      const int r = c >> 4, ch = c & 15;
+    {
       const __half* src =
-          p.q + ((size_t)(w.b * p.q_len + (r >> 2)) * p.hq + w.h * kGroup + (r & 3)) * kHeadDim + ch * 8;
-      uint8_t* dst = sm.q + (ch >> 3) * (kQBytes / 2) + r * 128 + (((ch & 7) ^ (r & 7)) << 4);
-      *reinterpret_cast<uint4*>(dst) = __ldg(reinterpret_cast<const uint4*>(src));
+          p.q + ((size_t)(w.b * p.q_len + (lrow >> 2)) * p.hq + w.h * kGroup + (lrow & 3)) * kHeadDim;
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t qv[32];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint4 v = active ? __ldg(reinterpret_cast<const uint4*>(src + hh * 64) + c) : make_uint4(0u, 0u, 0u, 0u);
+          qv[4 * c] = v.x;
+          qv[4 * c + 1] = v.y;
+          qv[4 * c + 2] = v.z;
+          qv[4 * c + 3] = v.w;
+        }
+        tmem_st32(tl + kColQ + hh * 32, qv);
+      }
+      tmem_wait_st();
     }
-    fence_proxy_async_smem();  // make the tile visible to the tensor core
+    tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(smem_u32(sm.q_ready));
 
@@ -256,36 +305,36 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
     for (int k = 0; k < nblk; ++k) {
       const int g = gb0 + k;
       const int np = min(kBP, n - k * kBP);
-      const int tok0 = (w.pg + k * kBP) * kPageSize;  // first token of the block
-      const int valid_cols = np * kPageSize;
-      mbar_wait_bounded(smem_u32(sm.s_full + (g & 1)), (uint32_t)(g >> 1) & 1u, abort, p.status, 7, g);
+      const int tok0 = (w.pg + k * kBP) * kPageSize + tok_lo;  // first token of this replica's columns
+      const int valid = np * kPageSize - tok_lo;                 // valid columns of this replica (may be <= 0)
+      mbar_wait_bounded(smem_u32(sm.s_full + (g % kNumS)), (uint32_t)(g / kNumS) & 1u, abort, p.status, 7, g);
       tc_fence_after();
-      const uint32_t slot_col = tl + kColS + (g & 1) * kSlotCols;
-      uint32_t sraw[kBlockTokens];
-      tmem_ld64(slot_col, sraw);
+      const uint32_t slot_col = tl + kColS + (g % kNumS) * kSlotCols;
+      uint32_t sraw[kTok];
+      if constexpr (kTok == 16) tmem_ld16(slot_col + tok_lo, sraw);
+      else tmem_ld32(slot_col + tok_lo, sraw);
       tmem_wait_ld();
       // Scores stay unscaled until the exponent: max(c * s) = c * max(s) for c > 0.
-      // mask a block that is partial (pages past the piece hold stale data) or
-      // that reaches the causal tail / the sequence end
-      if (valid_cols < kBlockTokens || tok0 + kBlockTokens > thr_min) {
+      // mask columns past the piece (stale data), the causal tail and the sequence end
+      if (valid < kTok || tok0 + kTok > thr_min) {
 #pragma unroll
-        for (int t = 0; t < kBlockTokens; ++t)
-          if (t >= valid_cols || tok0 + t >= thr) sraw[t] = 0xff800000u;  // -inf
+        for (int t = 0; t < kTok; ++t)
+          if (t >= valid || tok0 + t >= thr) sraw[t] = 0xff800000u;  // -inf
       }
       float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-      for (int t = 0; t < kBlockTokens; t += 2) {
+      for (int t = 0; t < kTok; t += 2) {
         mx0 = fmaxf(mx0, __uint_as_float(sraw[t]));
         mx1 = fmaxf(mx1, __uint_as_float(sraw[t + 1]));
       }
       const float m_new = fmaxf(m_used, fmaxf(mx0, mx1) * p.scale_log2);
       const bool need = active && (m_new > m_used + kRescaleLog2);
       if (k == 0) {
-        m_used = m_new;  // the piece's first PV overwrites O
+        m_used = m_new;  // the piece's first PV of this replica overwrites its O rows
       } else if (__any_sync(0xffffffffu, need)) {
         // O must be stable: wait for PV(g - 1), then rescale this warp's rows in TMEM
-        mbar_wait_bounded(smem_u32(sm.pv_done + ((g - 1) & 1)), (uint32_t)((g - 1) >> 1) & 1u, abort, p.status, 8,
-                          g);
+        mbar_wait_bounded(smem_u32(sm.pv_done + ((g - 1) % kNumS)), (uint32_t)((g - 1) / kNumS) & 1u, abort,
+                          p.status, 8, g);
         tc_fence_after();
         const float alpha = need ? ex2(m_used - m_new) : 1.f;
         if (need) {
@@ -303,27 +352,29 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
         }
         tmem_wait_st();
       }
-      // p = 2^(c*s - m): one FFMA and one ex2 per score; P as fp16 over the
-      // first half of the block's S columns (already read above)
+      // p = 2^(c*s - m): one FFMA and one ex2 per score; P as fp16 pairs over
+      // this replica's columns in the first half of the block's S slot
       const float nbase = active ? -((m_used == -INFINITY) ? 0.f : m_used) : -INFINITY;
       const float cs = p.scale_log2;
-      uint32_t pk[kBlockTokens / 2];
-      float ls[4] = {0.f, 0.f, 0.f, 0.f};
+      uint32_t pk[kTok / 2];
+      float ls[2] = {0.f, 0.f};
 #pragma unroll
-      for (int t = 0; t < kBlockTokens / 2; ++t) {
+      for (int t = 0; t < kTok / 2; ++t) {
         const float p0 = ex2(fmaf(__uint_as_float(sraw[2 * t]), cs, nbase));
         const float p1 = ex2(fmaf(__uint_as_float(sraw[2 * t + 1]), cs, nbase));
-        ls[t & 3] += p0 + p1;
+        ls[t & 1] += p0 + p1;
         pk[t] = pack_half2(p0, p1);
       }
-      l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
-      tmem_st32(slot_col, pk);
+      l += ls[0] + ls[1];
+      if constexpr (kTok == 16) tmem_st8(slot_col + tok_lo / 2, pk);
+      else tmem_st16(slot_col + tok_lo / 2, pk);
       tmem_wait_st();
-      if (tok0 + valid_cols > len && warp == 0) {
+      const int btok = (w.pg + k * kBP) * kPageSize;
+      if (btok + np * kPageSize > len && warp == 0) {
         // tokens at or past the sequence end: zero their V rows (the pool may hold NaN there)
         uint8_t* vreg = sm.ring + (size_t)(g % NB) * kBlockBytes + 2 * kRegionBytes;
         for (int j = 0; j < np; ++j) {
-          const int first = max(len - (tok0 + j * kPageSize), 0);
+          const int first = max(len - (btok + j * kPageSize), 0);
           if (first >= kPageSize) continue;
           for (int c = lane; c < (kPageSize - first) * 16; c += 32) {
             const int r = first + (c >> 4);
@@ -335,52 +386,81 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(sm.p_full + (g & 1)));
+      if (lane == 0) mbar_arrive(smem_u32(sm.p_full + (g % kNumS)));
     }
 
-    // ---- epilogue: O is complete once the piece's last PV has finished
+    // ---- epilogue: merge the R replicas of every row, then write the piece's rows
     const int gl = gb0 + nblk - 1;
-    mbar_wait_bounded(smem_u32(sm.pv_done + (gl & 1)), (uint32_t)(gl >> 1) & 1u, abort, p.status, 10, gl);
+    sm.ml[rep * kLanesPR + lrow] = make_float2(m_used, l);
+    mbar_wait_bounded(smem_u32(sm.pv_done + (gl % kNumS)), (uint32_t)(gl / kNumS) & 1u, abort, p.status, 10, gl);
     tc_fence_after();
-    const float inv = (l > 0.f) ? 1.f / l : 0.f;
-    const float lse = (l > 0.f) ? (m_used + __log2f(l)) * kLn2 : -INFINITY;
-    const size_t out_row = (size_t)(w.b * p.q_len + (row >> 2)) * p.hq + w.h * kGroup + (row & 3);
-    const int piece = (int)blockIdx.x + s;
-#pragma unroll 1
-    for (int c = 0; c < 128; c += 16) {
-      uint32_t o[16];
-      tmem_ld16(tl + kColO + c, o);
-      tmem_wait_ld();
-      if (!active) continue;
-      float v[16];
+    named_bar_sync(1, kSoftmaxWarps * 32);
+    float mx = -INFINITY;
 #pragma unroll
-      for (int t = 0; t < 16; ++t) v[t] = __uint_as_float(o[t]) * inv;
-      if (whole && p.out != nullptr) {
-        uint4 h0, h1;
-        h0.x = pack_half2(v[0], v[1]);
-        h0.y = pack_half2(v[2], v[3]);
-        h0.z = pack_half2(v[4], v[5]);
-        h0.w = pack_half2(v[6], v[7]);
-        h1.x = pack_half2(v[8], v[9]);
-        h1.y = pack_half2(v[10], v[11]);
-        h1.z = pack_half2(v[12], v[13]);
-        h1.w = pack_half2(v[14], v[15]);
-        uint4* dst = reinterpret_cast<uint4*>(p.out + out_row * kHeadDim + c);
-        dst[0] = h0;
-        dst[1] = h1;
-      } else {
-        float* dst = whole ? p.out_o + out_row * kHeadDim + c
-                           : p.ws_o + ((size_t)piece * p.rows_pad + row) * kHeadDim + c;
-#pragma unroll
-        for (int t = 0; t < 16; t += 4)
-          *reinterpret_cast<float4*>(dst + t) = make_float4(v[t], v[t + 1], v[t + 2], v[t + 3]);
-      }
+    for (int r = 0; r < R; ++r) {
+      const float2 v = sm.ml[r * kLanesPR + lrow];
+      if (v.y > 0.f) mx = fmaxf(mx, v.x);
     }
-    if (active) {
-      if (whole && p.out == nullptr) p.out_lse[out_row] = lse;
-      if (!whole) p.ws_lse[(size_t)piece * p.rows_pad + row] = lse;
+    float L = 0.f;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const float2 v = sm.ml[r * kLanesPR + lrow];
+      if (v.y > 0.f) L += v.y * ex2(v.x - mx);
+    }
+    const float f = (l > 0.f) ? ex2(m_used - mx) / L : 0.f;  // this replica's weight (L > 0 when l > 0)
+    const float lse = (L > 0.f) ? (mx + __log2f(L)) * kLn2 : -INFINITY;
+    // Two chunks of 64 dims: every warp stores its rows' weighted chunk (a
+    // uniform branch: tcgen05.ld needs the whole warp), then the 128 threads sum
+    // the replicas in a fixed order (deterministic) and write coalesced rows.
+    const int piece = (int)blockIdx.x + s;
+    float* mrow = sm.merge + (rep * kLanesPR + lrow) * kMergeStride;
+#pragma unroll 1
+    for (int c0 = 0; c0 < 128; c0 += kMergeCols) {
+#pragma unroll
+      for (int c = 0; c < kMergeCols; c += 16) {
+        uint32_t o[16];
+        tmem_ld16(tl + kColO + c0 + c, o);
+        tmem_wait_ld();
+        // a replica without tokens (f == 0) may hold stale O: never multiply it in
+#pragma unroll
+        for (int t = 0; t < 16; ++t) mrow[c + t] = (f != 0.f) ? __uint_as_float(o[t]) * f : 0.f;
+      }
+      named_bar_sync(1, kSoftmaxWarps * 32);
+      for (int idx = tid; idx < rows * (kMergeCols / 8); idx += kSoftmaxWarps * 32) {
+        const int r = idx / (kMergeCols / 8), ch = idx % (kMergeCols / 8);
+        float v[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) v[t] = 0.f;
+#pragma unroll
+        for (int rr = 0; rr < R; ++rr) {
+          const float* src = sm.merge + (rr * kLanesPR + r) * kMergeStride + ch * 8;
+#pragma unroll
+          for (int t = 0; t < 8; ++t) v[t] += src[t];
+        }
+        const size_t out_row = (size_t)(w.b * p.q_len + (r >> 2)) * p.hq + w.h * kGroup + (r & 3);
+        const int col = c0 + ch * 8;
+        if (whole && p.out != nullptr) {
+          uint4 h;
+          h.x = pack_half2(v[0], v[1]);
+          h.y = pack_half2(v[2], v[3]);
+          h.z = pack_half2(v[4], v[5]);
+          h.w = pack_half2(v[6], v[7]);
+          *reinterpret_cast<uint4*>(p.out + out_row * kHeadDim + col) = h;
+        } else {
+          float* dst = whole ? p.out_o + out_row * kHeadDim + col
+                             : p.ws_o + ((size_t)piece * p.rows_pad + r) * kHeadDim + col;
+          *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+          *reinterpret_cast<float4*>(dst + 4) = make_float4(v[4], v[5], v[6], v[7]);
+        }
+      }
+      named_bar_sync(1, kSoftmaxWarps * 32);
     }
     tc_fence_before();  // O reads are done before the next piece's first PV overwrites it
+    if (rep == 0 && active) {
+      const size_t out_row = (size_t)(w.b * p.q_len + (lrow >> 2)) * p.hq + w.h * kGroup + (lrow & 3);
+      if (whole && p.out == nullptr) p.out_lse[out_row] = lse;
+      if (!whole) p.ws_lse[(size_t)piece * p.rows_pad + lrow] = lse;
+    }
 
     gb0 += nblk;
     unit += n;
@@ -389,16 +469,16 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
   }
 }
 
-template <int SW>
-__global__ void __launch_bounds__((SW + 2) * 32, 1)
+template <int R>
+__global__ void __launch_bounds__(kThreadsTc, 1)
     sqa_split_kv_tc_kernel(const SplitKvParams p, const __grid_constant__ CUtensorMap tm_k,
                            const __grid_constant__ CUtensorMap tm_v) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const TcSmem sm = carve(smem, p.num_stages);
   const int warp = threadIdx.x >> 5;
-  constexpr int kMmaWarp = SW;
-  constexpr int kProducerWarp = SW + 1;
+  constexpr int kMmaWarp = kSoftmaxWarps;
+  constexpr int kProducerWarp = kSoftmaxWarps + 1;
   unsigned long long* tl = p.timeline ? p.timeline + (size_t)blockIdx.x * 32 : nullptr;
 #ifdef SQA_DEBUG_TIMELINE
   if (threadIdx.x < 16) sqa_wait_ns[threadIdx.x] = 0;
@@ -410,19 +490,15 @@ __global__ void __launch_bounds__((SW + 2) * 32, 1)
       mbar_init(smem_u32(sm.full + i), 1);
       mbar_init(smem_u32(sm.empty + i), 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kNumS; ++i) {
       mbar_init(smem_u32(sm.s_full + i), 1);
-      mbar_init(smem_u32(sm.p_full + i), SW);
+      mbar_init(smem_u32(sm.p_full + i), kSoftmaxWarps);
       mbar_init(smem_u32(sm.pv_done + i), 1);
     }
-    mbar_init(smem_u32(sm.q_ready), SW);
+    mbar_init(smem_u32(sm.q_ready), kSoftmaxWarps);
     mbar_init(smem_u32(sm.mma_done), 1);
     fence_mbar_init();
   }
-  // rows of the Q tile past 4 * q_len stay zero for the whole kernel
-  for (int i = threadIdx.x; i < kQBytes / 16; i += blockDim.x)
-    reinterpret_cast<uint4*>(sm.q)[i] = make_uint4(0u, 0u, 0u, 0u);
-  fence_proxy_async_smem();  // these generic writes are read by the tensor core
   if (warp == kProducerWarp && (threadIdx.x & 31) == 0) {
     prefetch_tensormap(&tm_k);
     prefetch_tensormap(&tm_v);
@@ -444,10 +520,9 @@ __global__ void __launch_bounds__((SW + 2) * 32, 1)
   if (warp == kProducerWarp) {
     tc_producer(p, s, &tm_k, &tm_v, sm, abort);
   } else if (warp == kMmaWarp) {
-    if ((threadIdx.x & 31) == 0) tc_mma(p, s, sm, tmem, abort);
-    __syncwarp();
+    tc_mma<R>(p, s, sm, tmem, abort);
   } else {
-    tc_softmax<SW>(p, s, sm, tmem, abort);
+    tc_softmax<R>(p, s, sm, tmem, abort);
   }
 
   tc_fence_before();
@@ -464,10 +539,10 @@ __global__ void __launch_bounds__((SW + 2) * 32, 1)
 #endif
 }
 
-template <int SW>
+template <int R>
 cudaError_t launch_tc(const SplitKvParams& p, const CUtensorMap& tm_k, const CUtensorMap& tm_v, int grid,
                       int smem_bytes, cudaStream_t stream) {
-  auto kernel = sqa_split_kv_tc_kernel<SW>;
+  auto kernel = sqa_split_kv_tc_kernel<R>;
   static int configured[64] = {0};
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
@@ -479,7 +554,7 @@ cudaError_t launch_tc(const SplitKvParams& p, const CUtensorMap& tm_k, const CUt
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3((SW + 2) * 32);
+  cfg.blockDim = dim3(kThreadsTc);
   cfg.dynamicSmemBytes = smem_bytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -497,12 +572,12 @@ cudaError_t launch_tc(const SplitKvParams& p, const CUtensorMap& tm_k, const CUt
 int split_kv_tc_block_bytes() { return kBlockBytes; }
 
 int split_kv_tc_smem_bytes(int num_blocks) {
-  return 1024 + kQBytes + num_blocks * kBlockBytes + (2 * num_blocks + 8) * 8 + 8 + 64;
+  return 1024 + num_blocks * kBlockBytes + kMergeBytes + kMlBytes + (2 * num_blocks + 3 * kNumS + 2) * 8 + 8 + 64;
 }
 
 cudaError_t launch_split_kv_tc(const SplitKvParams& p, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
                                int grid, int smem_bytes, cudaStream_t stream) {
-  if (kGroup * p.q_len <= 32) return launch_tc<1>(p, tm_k, tm_v, grid, smem_bytes, stream);
+  if (kGroup * p.q_len <= 32) return launch_tc<4>(p, tm_k, tm_v, grid, smem_bytes, stream);
   return launch_tc<2>(p, tm_k, tm_v, grid, smem_bytes, stream);
 }
 
