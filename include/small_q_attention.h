@@ -104,7 +104,10 @@ typedef struct sqa_args {
    * work) and the minimum pages one CTA takes (0 = auto). */
   int32_t num_ctas;
   int32_t min_pages_per_cta;
-  /* Kernel choice: 0 = auto (tcgen05 for q_len >= 5, warp-level below),
+  /* Kernel choice: 0 = auto (tcgen05 for q_len >= 9, for q_len 5..8 above 512
+   * page-units and for q_len <= 4 from 32768 page-units, where a page-unit is
+   * one page of one KV head, bounded by max_seq_len or max_pages; warp-level
+   * otherwise),
    * 1 = warp-level mma.sync kernel, 2 = tcgen05 / tensor-memory kernel.
    * Both compute the same operator. */
   int32_t kernel;

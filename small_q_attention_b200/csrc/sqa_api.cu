@@ -22,6 +22,10 @@ constexpr int kCtasPerSm = 2;
 constexpr int kSmemPerSm = 228 * 1024;
 constexpr int kSmemPerCta = kSmemPerSm / kCtasPerSm - 1024;
 constexpr int kMaxSmemPerCta = 227 * 1024;  // dynamic shared memory limit of one CTA on sm_100
+// Auto kernel choice thresholds on the launch's upper bound of units (pages x KV heads):
+// q_len 5..8 takes the tcgen05 kernel above 512 units, q_len <= 4 from 32768 units.
+constexpr long long kAutoTcUnitsQ8 = 512;
+constexpr long long kAutoTcUnitsQ4 = 32768;
 constexpr int kDefaultMinPagesPerCta = 4;
 
 size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
@@ -137,9 +141,23 @@ int make_plan(const sqa_args* a, int device, Plan* plan) {
   if (sms <= 0) return SQA_ERR_CUDA;
   Plan pl;
   pl.shape = warp_shape_for(a->q_len);
-  // Auto: the tcgen05 kernel for q_len >= 5 (measured faster on B200 at every
-  // batch and length from q_len 8 up), the warp-level kernel below.
-  pl.tc = a->kernel == 2 || (a->kernel == 0 && a->q_len >= 5);
+  pl.segments = a->batch * a->num_kv_heads;
+  long long pages_upper = a->max_pages;
+  if (a->max_seq_len > 0) {
+    const long long need = (a->max_seq_len + kPageSize - 1) / kPageSize;
+    if (need < pages_upper) pages_upper = need;
+  }
+  const long long units_upper = (long long)pl.segments * pages_upper;
+  // Auto (measured on B200): the tcgen05 kernel streams at the HBM roofline for
+  // every q_len but has the longer per-CTA latency chain (TMEM, asynchronous MMA
+  // completions, replica merge); the warp-level kernel wins small launches.
+  if (a->kernel == 0) {
+    if (a->q_len >= 9) pl.tc = true;
+    else if (a->q_len >= 5) pl.tc = units_upper > kAutoTcUnitsQ8;
+    else pl.tc = units_upper >= kAutoTcUnitsQ4;
+  } else {
+    pl.tc = a->kernel == 2;
+  }
   int ctas_per_sm = kCtasPerSm;
   if (pl.tc) {  // one CTA per SM: a ring of 4-page blocks in up to 227 KB of shared memory
     ctas_per_sm = 1;
@@ -153,14 +171,6 @@ int make_plan(const sqa_args* a, int device, Plan* plan) {
     if (pl.stages > kMaxStages) pl.stages = kMaxStages;
     pl.smem = split_kv_smem_bytes(pl.shape, pl.stages);
   }
-  pl.segments = a->batch * a->num_kv_heads;
-
-  long long pages_upper = a->max_pages;
-  if (a->max_seq_len > 0) {
-    const long long need = (a->max_seq_len + kPageSize - 1) / kPageSize;
-    if (need < pages_upper) pages_upper = need;
-  }
-  const long long units_upper = (long long)pl.segments * pages_upper;
   const int min_pages = a->min_pages_per_cta > 0 ? a->min_pages_per_cta : kDefaultMinPagesPerCta;
   long long grid = a->num_ctas > 0 ? a->num_ctas : (long long)sms * ctas_per_sm;
   if (a->num_ctas <= 0) {

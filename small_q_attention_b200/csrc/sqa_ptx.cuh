@@ -107,10 +107,12 @@ static __shared__ unsigned long long sqa_wait_ns[16];
   do {                                                                                  \
     if ((threadIdx.x & 31) == 0) atomicAdd(&sqa_wait_ns[(kind) & 15], global_timer_ns() - (t0)); \
   } while (0)
+#define SQA_T0() global_timer_ns()
 #else
 #define SQA_WAIT_ACCOUNT(kind, t0) \
   do {                             \
   } while (0)
+#define SQA_T0() 0ull
 #endif
 
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,

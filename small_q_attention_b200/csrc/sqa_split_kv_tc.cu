@@ -24,14 +24,16 @@
 //   for the exponentials is raised only when a block's max exceeds it by more
 //   than 2^8; then the warp's O rows are rescaled in TMEM.  P (fp16) is written
 //   over the block's S columns.
-// * The MMA warp runs converged and issues through elect.sync.
+// * Two MMA warps, one issuing the QK products and one the PV products, each
+//   converged and issuing through elect.sync: a PV whose P is ready never
+//   waits behind a QK whose pages are still in flight.
 //
 // Pipelines (mbarriers; every wait bounded):
-//   ring   full[NB] / empty[NB]   producer -> MMA; released by the commit after PV
-//   S/P    s_full[4] / p_full[4]  MMA (QK commit) -> softmax -> MMA (PV)
-//   pv_done[4]                    MMA (PV commit) -> S/P slot reuse, O rescale, epilogue
-//   q_ready                       softmax (Q of the piece in TMEM) -> MMA
-// QK of block g+2 is issued before PV of block g.
+//   ring   full[NB] / empty[NB]   producer -> QK issuer; released by the commit after PV
+//   S/P    s_full[4] / p_full[4]  QK issuer (commit) -> softmax -> PV issuer
+//   pv_done[4]                    PV issuer (commit) -> S/P slot reuse, O rescale, epilogue
+//   q_ready                       softmax (Q of the piece in TMEM) -> QK issuer
+// The QK issuer runs up to four blocks ahead of the softmax (one per S slot).
 #include "sqa_internal.h"
 #include "sqa_ptx.cuh"
 #include "sqa_schedule.cuh"
@@ -47,10 +49,14 @@ constexpr int kTmemCols = 512;                  // O | Q | S/P slots 0..3
 constexpr int kColO = 0;
 constexpr int kColQ = 128;                      // 128 fp16 dims = 64 columns
 constexpr int kColS = 192;
-constexpr int kNumS = 4;
+#ifndef SQA_TC_NUM_S
+#define SQA_TC_NUM_S 4
+#endif
+constexpr int kNumS = SQA_TC_NUM_S;             // S/P slots (64 columns each)
+static_assert(kColS + kNumS * 64 <= 512, "S slots must fit in TMEM");
 constexpr int kSlotCols = kBlockTokens;         // fp32 S of a block; its fp16 P takes the first half
 constexpr int kSoftmaxWarps = 4;
-constexpr int kThreadsTc = (kSoftmaxWarps + 2) * 32;
+constexpr int kThreadsTc = (kSoftmaxWarps + 3) * 32;  // softmax x4, QK issuer, PV issuer, producer
 constexpr int kMergeCols = 64;                  // dims merged per pass
 constexpr int kMergeStride = kMergeCols + 1;    // floats per merge row (conflict-free columns)
 constexpr int kMergeBytes = 128 * kMergeStride * 4;  // one row per TMEM lane
@@ -158,59 +164,88 @@ __device__ void tc_producer(const SplitKvParams& p, const Schedule& sch, const C
   }
 }
 
-// ------------------------------------------------------------------ MMA issuer (whole warp, one elected lane)
-template <int R>
-__device__ void tc_mma(const SplitKvParams& p, const Schedule& sch, const TcSmem& sm, uint32_t tmem,
-                       volatile int* abort) {
+// ------------------------------------------------------------------ MMA issuers (whole warps, one elected lane)
+// Two warps issue to the tensor core: one the QK products, one the PV products,
+// so that a PV whose P is ready never waits behind a QK whose pages are still
+// in flight (and the other way round).  Ordering between their MMAs comes only
+// from the barriers: s_full / p_full / pv_done.
+
+// Both issuers: every MMA this warp issued must finish before TMEM is released.
+__device__ __forceinline__ void tc_mma_drain(const SplitKvParams& p, const TcSmem& sm) {
+  if (elect_one()) tc_commit(smem_u32(sm.mma_done));
+  __syncwarp();
+  if (!mbar_drain(smem_u32(sm.mma_done), 0u, 2000000000ull) && (threadIdx.x & 31) == 0) atomicOr(p.status, 1u);
+}
+
+// S(h) = Q K_h^T into slot h % kNumS, once the block's pages are in and PV(h - kNumS)
+// has released the slot; Q of a piece is in TMEM once q_ready completes.
+__device__ void tc_mma_qk(const SplitKvParams& p, const Schedule& sch, const TcSmem& sm, uint32_t tmem,
+                          volatile int* abort) {
   constexpr uint32_t kIdescQK = mma_idesc_f16(128, kBlockTokens, false, false);  // Q (TMEM) x K_block (K-major)
-  constexpr uint32_t kIdescPV = mma_idesc_f16(128, 128, false, true);           // P (TMEM) x V (MN-major)
-  constexpr int kPPR = kBP / R;       // pages of a block per replica
-  constexpr int kLanesPR = 128 / R;   // TMEM lanes per replica
   const int NB = p.num_stages;
   SegWalk w = first_segment(p, sch);
-  int gb0 = 0;  // CTA block counter at the start of the piece
-  int pc = 0;   // piece counter
+  int h = 0;   // CTA block counter
+  int pc = 0;  // piece counter
   int unit = sch.start;
-
-  // S(h) = Q K_h^T into slot h % 4, once PV(h - 4) has released that slot.
-  auto issue_qk = [&](int h) {
-    if (h >= kNumS)
-      mbar_wait_bounded(smem_u32(sm.pv_done + (h % kNumS)), (uint32_t)((h - kNumS) / kNumS) & 1u, abort,
-                        p.status, 11, h);
-    const int slot = h % NB;
-    mbar_wait_bounded(smem_u32(sm.full + slot), (uint32_t)(h / NB) & 1u, abort, p.status, 5, h);
-    __syncwarp();
-    tc_fence_after();
-    if (elect_one()) {
-      const uint32_t k_base = smem_u32(sm.ring + (size_t)slot * kBlockBytes);
-      const uint32_t d = tmem + kColS + (h % kNumS) * kSlotCols;
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const uint64_t b = smem_desc_sw128(k_base + (kk >> 2) * kRegionBytes + (kk & 3) * 32u, 16, 1024);
-        tc_mma_ts(d, tmem + kColQ + kk * 8, b, kIdescQK, kk > 0 ? 1u : 0u);
-      }
-      tc_commit(smem_u32(sm.s_full + (h % kNumS)));
-    }
-    __syncwarp();
-  };
-
   while (unit < sch.end) {
     const int seg_end = w.seg_start + w.pages;
     const int n = min(sch.end, seg_end) - unit;
     const int nblk = blocks_of(n);
     mbar_wait_bounded(smem_u32(sm.q_ready), (uint32_t)(pc & 1), abort, p.status, 4, pc);
-    __syncwarp();
-    tc_fence_after();
-    issue_qk(gb0);
-    if (nblk > 1) issue_qk(gb0 + 1);
-    for (int k = 0; k < nblk; ++k) {
-      const int g = gb0 + k;
-      if (k + 2 < nblk) issue_qk(g + 2);
+    for (int k = 0; k < nblk; ++k, ++h) {
+      if (h >= kNumS)
+        mbar_wait_bounded(smem_u32(sm.pv_done + (h % kNumS)), (uint32_t)((h - kNumS) / kNumS) & 1u, abort,
+                          p.status, 11, h);
+      const int slot = h % NB;
+      mbar_wait_bounded(smem_u32(sm.full + slot), (uint32_t)(h / NB) & 1u, abort, p.status, 5, h);
+      __syncwarp();
+      tc_fence_after();
+      const uint64_t t_qk = SQA_T0();
+      if (elect_one()) {
+        const uint32_t k_base = smem_u32(sm.ring + (size_t)slot * kBlockBytes);
+        const uint32_t d = tmem + kColS + (h % kNumS) * kSlotCols;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t b = smem_desc_sw128(k_base + (kk >> 2) * kRegionBytes + (kk & 3) * 32u, 16, 1024);
+          tc_mma_ts(d, tmem + kColQ + kk * 8, b, kIdescQK, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(smem_u32(sm.s_full + (h % kNumS)));
+      }
+      __syncwarp();
+      SQA_WAIT_ACCOUNT(12, t_qk);
+      (void)t_qk;
+    }
+    ++pc;
+    unit += n;
+    if (unit >= seg_end) next_segment(p, w);
+    else w.pg += n;
+  }
+  tc_mma_drain(p, sm);
+}
+
+// O += P V_g once the softmax has written P(g); then the block's ring slot and
+// S/P slot are released by commits.
+template <int R>
+__device__ void tc_mma_pv(const SplitKvParams& p, const Schedule& sch, const TcSmem& sm, uint32_t tmem,
+                          volatile int* abort) {
+  constexpr uint32_t kIdescPV = mma_idesc_f16(128, 128, false, true);  // P (TMEM) x V (MN-major)
+  constexpr int kPPR = kBP / R;       // pages of a block per replica
+  constexpr int kLanesPR = 128 / R;   // TMEM lanes per replica
+  const int NB = p.num_stages;
+  SegWalk w = first_segment(p, sch);
+  int g = 0;  // CTA block counter
+  int unit = sch.start;
+  while (unit < sch.end) {
+    const int seg_end = w.seg_start + w.pages;
+    const int n = min(sch.end, seg_end) - unit;
+    const int nblk = blocks_of(n);
+    for (int k = 0; k < nblk; ++k, ++g) {
       const int slot = g % NB;
       const int np = min(kBP, n - k * kBP);
       mbar_wait_bounded(smem_u32(sm.p_full + (g % kNumS)), (uint32_t)(g / kNumS) & 1u, abort, p.status, 6, g);
       __syncwarp();
       tc_fence_after();
+      const uint64_t t_pv = SQA_T0();
       if (elect_one()) {
         const uint32_t v_base = smem_u32(sm.ring + (size_t)slot * kBlockBytes + 2 * kRegionBytes);
         const uint32_t p_col = tmem + kColS + (g % kNumS) * kSlotCols;
@@ -228,17 +263,14 @@ __device__ void tc_mma(const SplitKvParams& p, const Schedule& sch, const TcSmem
         tc_commit(smem_u32(sm.pv_done + (g % kNumS)));     // S/P slot free, O up to date
       }
       __syncwarp();
+      SQA_WAIT_ACCOUNT(13, t_pv);
+      (void)t_pv;
     }
-    gb0 += nblk;
-    ++pc;
     unit += n;
     if (unit >= seg_end) next_segment(p, w);
     else w.pg += n;
   }
-  // every MMA this warp issued must finish before TMEM is released
-  if (elect_one()) tc_commit(smem_u32(sm.mma_done));
-  __syncwarp();
-  if (!mbar_drain(smem_u32(sm.mma_done), 0u, 2000000000ull) && (threadIdx.x & 31) == 0) atomicOr(p.status, 1u);
+  tc_mma_drain(p, sm);
 }
 
 // ------------------------------------------------------------------ softmax + epilogue (4 warps)
@@ -309,6 +341,7 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
       const int valid = np * kPageSize - tok_lo;                 // valid columns of this replica (may be <= 0)
       mbar_wait_bounded(smem_u32(sm.s_full + (g % kNumS)), (uint32_t)(g / kNumS) & 1u, abort, p.status, 7, g);
       tc_fence_after();
+      const uint64_t t_sm = SQA_T0();
       const uint32_t slot_col = tl + kColS + (g % kNumS) * kSlotCols;
       uint32_t sraw[kTok];
       if constexpr (kTok == 16) tmem_ld16(slot_col + tok_lo, sraw);
@@ -387,9 +420,12 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(sm.p_full + (g % kNumS)));
+      SQA_WAIT_ACCOUNT(14, t_sm);
+      (void)t_sm;
     }
 
     // ---- epilogue: merge the R replicas of every row, then write the piece's rows
+    const uint64_t t_ep = SQA_T0();
     const int gl = gb0 + nblk - 1;
     sm.ml[rep * kLanesPR + lrow] = make_float2(m_used, l);
     mbar_wait_bounded(smem_u32(sm.pv_done + (gl % kNumS)), (uint32_t)(gl / kNumS) & 1u, abort, p.status, 10, gl);
@@ -456,6 +492,8 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
       named_bar_sync(1, kSoftmaxWarps * 32);
     }
     tc_fence_before();  // O reads are done before the next piece's first PV overwrites it
+    SQA_WAIT_ACCOUNT(15, t_ep);
+    (void)t_ep;
     if (rep == 0 && active) {
       const size_t out_row = (size_t)(w.b * p.q_len + (lrow >> 2)) * p.hq + w.h * kGroup + (lrow & 3);
       if (whole && p.out == nullptr) p.out_lse[out_row] = lse;
@@ -477,8 +515,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const TcSmem sm = carve(smem, p.num_stages);
   const int warp = threadIdx.x >> 5;
-  constexpr int kMmaWarp = kSoftmaxWarps;
-  constexpr int kProducerWarp = kSoftmaxWarps + 1;
+  constexpr int kMmaWarp = kSoftmaxWarps;         // QK issuer; owns the TMEM allocation
+  constexpr int kPvWarp = kSoftmaxWarps + 1;
+  constexpr int kProducerWarp = kSoftmaxWarps + 2;
   unsigned long long* tl = p.timeline ? p.timeline + (size_t)blockIdx.x * 32 : nullptr;
 #ifdef SQA_DEBUG_TIMELINE
   if (threadIdx.x < 16) sqa_wait_ns[threadIdx.x] = 0;
@@ -486,6 +525,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
 
   if (threadIdx.x == 0) {
     SQA_STAMP(tl, 0);
+#ifdef SQA_DEBUG_TIMELINE
+    if (tl) tl[5] = clock64();
+#endif
     for (int i = 0; i < p.num_stages; ++i) {
       mbar_init(smem_u32(sm.full + i), 1);
       mbar_init(smem_u32(sm.empty + i), 1);
@@ -496,7 +538,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
       mbar_init(smem_u32(sm.pv_done + i), 1);
     }
     mbar_init(smem_u32(sm.q_ready), kSoftmaxWarps);
-    mbar_init(smem_u32(sm.mma_done), 1);
+    mbar_init(smem_u32(sm.mma_done), 2);  // one commit from each issuer
     fence_mbar_init();
   }
   if (warp == kProducerWarp && (threadIdx.x & 31) == 0) {
@@ -520,7 +562,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
   if (warp == kProducerWarp) {
     tc_producer(p, s, &tm_k, &tm_v, sm, abort);
   } else if (warp == kMmaWarp) {
-    tc_mma<R>(p, s, sm, tmem, abort);
+    tc_mma_qk(p, s, sm, tmem, abort);
+  } else if (warp == kPvWarp) {
+    tc_mma_pv<R>(p, s, sm, tmem, abort);
   } else {
     tc_softmax<R>(p, s, sm, tmem, abort);
   }
@@ -534,6 +578,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
 #ifdef SQA_DEBUG_TIMELINE
   if (tl && threadIdx.x == 0) {
     tl[4] = global_timer_ns();
+    tl[6] = clock64();
     for (int k = 0; k < 16; ++k) tl[16 + k] = sqa_wait_ns[k];
   }
 #endif
