@@ -468,6 +468,13 @@ __global__ void __launch_bounds__(kThreads, 2)
   } else {
     consumer_loop<NT, WR>(p, s, stages, full, empty, cbuf, mbuf, lbuf, abort);
     if (threadIdx.x == 0) SQA_STAMP(tl, 4);  // consumers done (last epilogue written)
+#ifdef SQA_DEBUG_TIMELINE
+    if (threadIdx.x == 0 && tl) {
+      unsigned int smid;
+      asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+      tl[7] = smid;
+    }
+#endif
   }
 }
 

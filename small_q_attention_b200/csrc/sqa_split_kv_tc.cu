@@ -32,7 +32,7 @@
 //   ring   full[NB] / empty[NB]   producer -> QK issuer; released by the commit after PV
 //   S/P    s_full[4] / p_full[4]  QK issuer (commit) -> softmax -> PV issuer
 //   pv_done[4]                    PV issuer (commit) -> S/P slot reuse, O rescale, epilogue
-//   q_ready                       softmax (Q of the piece in TMEM) -> QK issuer
+//   q_ready[2]                    softmax (Q of a piece in TMEM, one piece ahead) -> QK issuer
 // The QK issuer runs up to four blocks ahead of the softmax (one per S slot).
 #include "sqa_internal.h"
 #include "sqa_ptx.cuh"
@@ -45,10 +45,10 @@ constexpr int kBP = 4;                          // pages per block
 constexpr int kBlockTokens = kBP * kPageSize;   // 64
 constexpr int kRegionBytes = kBP * 2048;        // one 64-dim half of K or V for a block
 constexpr int kBlockBytes = 4 * kRegionBytes;   // K lo | K hi | V lo | V hi
-constexpr int kTmemCols = 512;                  // O | Q | S/P slots 0..3
+constexpr int kTmemCols = 512;                  // O | Q x2 | S/P slots 0..3
 constexpr int kColO = 0;
-constexpr int kColQ = 128;                      // 128 fp16 dims = 64 columns
-constexpr int kColS = 192;
+constexpr int kColQ = 128;                      // two Q slots (pieces alternate), 64 columns each
+constexpr int kColS = 256;
 #ifndef SQA_TC_NUM_S
 #define SQA_TC_NUM_S 4
 #endif
@@ -85,7 +85,7 @@ __device__ __forceinline__ TcSmem carve(uint8_t* smem, int nb) {
   t.p_full = t.s_full + kNumS;
   t.pv_done = t.p_full + kNumS;
   t.q_ready = t.pv_done + kNumS;
-  t.mma_done = t.q_ready + 1;
+  t.mma_done = t.q_ready + 2;
   t.tmem_base = reinterpret_cast<uint32_t*>(t.mma_done + 1);
   t.sch = reinterpret_cast<Schedule*>(t.tmem_base + 2);
   return t;
@@ -191,7 +191,9 @@ __device__ void tc_mma_qk(const SplitKvParams& p, const Schedule& sch, const TcS
     const int seg_end = w.seg_start + w.pages;
     const int n = min(sch.end, seg_end) - unit;
     const int nblk = blocks_of(n);
-    mbar_wait_bounded(smem_u32(sm.q_ready), (uint32_t)(pc & 1), abort, p.status, 4, pc);
+    // Q of piece pc is in Q slot pc % 2 (written one piece ahead by the softmax warps)
+    mbar_wait_bounded(smem_u32(sm.q_ready + (pc & 1)), (uint32_t)(pc >> 1) & 1u, abort, p.status, 4, pc);
+    const uint32_t q_col = tmem + kColQ + (pc & 1) * 64;
     for (int k = 0; k < nblk; ++k, ++h) {
       if (h >= kNumS)
         mbar_wait_bounded(smem_u32(sm.pv_done + (h % kNumS)), (uint32_t)((h - kNumS) / kNumS) & 1u, abort,
@@ -200,6 +202,7 @@ __device__ void tc_mma_qk(const SplitKvParams& p, const Schedule& sch, const TcS
       mbar_wait_bounded(smem_u32(sm.full + slot), (uint32_t)(h / NB) & 1u, abort, p.status, 5, h);
       __syncwarp();
       tc_fence_after();
+      if (h == 0 && (threadIdx.x & 31) == 0 && p.timeline) SQA_STAMP(p.timeline + (size_t)blockIdx.x * 32, 3);
       const uint64_t t_qk = SQA_T0();
       if (elect_one()) {
         const uint32_t k_base = smem_u32(sm.ring + (size_t)slot * kBlockBytes);
@@ -207,7 +210,7 @@ __device__ void tc_mma_qk(const SplitKvParams& p, const Schedule& sch, const TcS
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint64_t b = smem_desc_sw128(k_base + (kk >> 2) * kRegionBytes + (kk & 3) * 32u, 16, 1024);
-          tc_mma_ts(d, tmem + kColQ + kk * 8, b, kIdescQK, kk > 0 ? 1u : 0u);
+          tc_mma_ts(d, q_col + kk * 8, b, kIdescQK, kk > 0 ? 1u : 0u);
         }
         tc_commit(smem_u32(sm.s_full + (h % kNumS)));
       }
@@ -290,8 +293,31 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
   const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
   const int NB = p.num_stages;
 
+  // This thread's lane of Q slot `qs` gets packed row lrow of (b, h) (zeros past the rows).
+  auto write_q = [&](int b, int h, int qs) {
+    const __half* src = p.q + ((size_t)(b * p.q_len + (lrow >> 2)) * p.hq + h * kGroup + (lrow & 3)) * kHeadDim;
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+      uint32_t qv[32];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        uint4 v = active ? __ldg(reinterpret_cast<const uint4*>(src + hh * 64) + c) : make_uint4(0u, 0u, 0u, 0u);
+        qv[4 * c] = v.x;
+        qv[4 * c + 1] = v.y;
+        qv[4 * c + 2] = v.z;
+        qv[4 * c + 3] = v.w;
+      }
+      tmem_st32(tl + kColQ + qs * 64 + hh * 32, qv);
+    }
+    tmem_wait_st();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(sm.q_ready + qs));
+  };
+
   SegWalk w = first_segment(p, sch);
   int gb0 = 0;
+  int pc = 0;  // piece counter
   int unit = sch.start;
   while (unit < sch.end) {
     const int s = w.b * p.hkv + w.h;
@@ -309,29 +335,16 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
     const int thr = min(len, mlen - p.q_len + (lrow >> 2) + 1);
     const int thr_min = min(len, mlen - p.q_len + 1);  // visible tokens of draft row 0
 
-    // Q of this piece into TMEM: this thread's lane gets packed row lrow (zeros past the rows).
-    // (Every QK product of the previous piece is complete: all its S blocks were consumed.)
-    {
-      const __half* src =
-          p.q + ((size_t)(w.b * p.q_len + (lrow >> 2)) * p.hq + w.h * kGroup + (lrow & 3)) * kHeadDim;
-#pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        uint32_t qv[32];
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          uint4 v = active ? __ldg(reinterpret_cast<const uint4*>(src + hh * 64) + c) : make_uint4(0u, 0u, 0u, 0u);
-          qv[4 * c] = v.x;
-          qv[4 * c + 1] = v.y;
-          qv[4 * c + 2] = v.z;
-          qv[4 * c + 3] = v.w;
-        }
-        tmem_st32(tl + kColQ + hh * 32, qv);
-      }
-      tmem_wait_st();
+    // Q into TMEM one piece ahead: piece pc uses Q slot pc % 2, so the QK products
+    // of the next piece can run while this piece's epilogue is still merging.
+    // Slot (pc + 1) % 2 is free: every QK product of piece pc - 1 is complete
+    // (all its S blocks were consumed).
+    if (pc == 0) write_q(w.b, w.h, 0);
+    if (seg_end < sch.end) {  // the next piece starts the next segment
+      SegWalk nw = w;
+      next_segment(p, nw);
+      write_q(nw.b, nw.h, (pc + 1) & 1);
     }
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(smem_u32(sm.q_ready));
 
     float m_used = -INFINITY, l = 0.f;
     for (int k = 0; k < nblk; ++k) {
@@ -501,6 +514,7 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
     }
 
     gb0 += nblk;
+    ++pc;
     unit += n;
     if (unit >= seg_end) next_segment(p, w);
     else w.pg += n;
@@ -538,6 +552,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
       mbar_init(smem_u32(sm.pv_done + i), 1);
     }
     mbar_init(smem_u32(sm.q_ready), kSoftmaxWarps);
+    mbar_init(smem_u32(sm.q_ready + 1), kSoftmaxWarps);
     mbar_init(smem_u32(sm.mma_done), 2);  // one commit from each issuer
     fence_mbar_init();
   }
@@ -547,6 +562,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
   }
   grid_dependency_wait();
   allow_dependent_launch();
+  if (threadIdx.x == 0) SQA_STAMP(tl, 1);
   if (warp == kMmaWarp) {
     tmem_alloc(smem_u32(sm.tmem_base), kTmemCols);
     tmem_relinquish();
@@ -558,6 +574,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
   const uint32_t tmem = *sm.tmem_base;
   const Schedule s = *sm.sch;
   volatile int* abort = &sm.sch->abort;
+  if (threadIdx.x == 0) SQA_STAMP(tl, 2);
 
   if (warp == kProducerWarp) {
     tc_producer(p, s, &tm_k, &tm_v, sm, abort);
@@ -579,6 +596,9 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
   if (tl && threadIdx.x == 0) {
     tl[4] = global_timer_ns();
     tl[6] = clock64();
+    unsigned int smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    tl[7] = smid;
     for (int k = 0; k < 16; ++k) tl[16 + k] = sqa_wait_ns[k];
   }
 #endif
@@ -617,7 +637,7 @@ cudaError_t launch_tc(const SplitKvParams& p, const CUtensorMap& tm_k, const CUt
 int split_kv_tc_block_bytes() { return kBlockBytes; }
 
 int split_kv_tc_smem_bytes(int num_blocks) {
-  return 1024 + num_blocks * kBlockBytes + kMergeBytes + kMlBytes + (2 * num_blocks + 3 * kNumS + 2) * 8 + 8 + 64;
+  return 1024 + num_blocks * kBlockBytes + kMergeBytes + kMlBytes + (2 * num_blocks + 3 * kNumS + 3) * 8 + 8 + 64;
 }
 
 cudaError_t launch_split_kv_tc(const SplitKvParams& p, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
