@@ -58,12 +58,15 @@ def _peaks():
     return FALLBACK_HBM_GBS, "fallback"
 
 
-def _traffic(workload: str):
-    """DRAM bytes per split-KV launch from the committed ncu summary, if any."""
+KERNEL_NAMES = {1: "sqa_split_kv_kernel", 2: "sqa_split_kv_tc_kernel"}
+
+
+def _traffic(workload: str, kernel_id: int):
+    """DRAM bytes per split-KV launch of this kernel from the committed ncu summary, if any."""
     p = ROOT / "profiles" / "traffic.json"
     if not p.exists():
         return None
-    return json.loads(p.read_text()).get(workload)
+    return json.loads(p.read_text()).get(f"{workload}/{KERNEL_NAMES[kernel_id]}")
 
 
 # ------------------------------------------------------------------ clocks
@@ -299,6 +302,9 @@ def run_ours(args):
         _native.check(st.value, "sqa_workspace_bytes")
     ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=device)
     merged = torch.empty(reps[0]["query"].shape, dtype=torch.float16, device=device)
+    kernel_id = lib.sqa_selected_kernel(ctypes.byref(cargs[0]), local)  # what kernel=args.kernel resolves to
+    if kernel_id < 0:
+        _native.check(-kernel_id, "sqa_selected_kernel")
 
     def call(i, stream, ev0=None, ev1=None):
         a = cargs[i % REPLICAS]
@@ -437,7 +443,8 @@ def run_ours(args):
                        "algorithmic_bytes_per_call": bytes_job},
             "roofline": {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": peak_gbs, "unit": "GB/s",
                          "frac": round(achieved_gbs / peak_gbs, 4), "peak_source": f"{peak_src} hbm_gbs (burst)",
-                         "traffic": _traffic(name) if world == 1 else None, "kernel": "sqa_split_kv_kernel",
+                         "traffic": _traffic(name, kernel_id) if world == 1 else None,
+                         "kernel": KERNEL_NAMES[kernel_id],
                          "kernel_us": round(kern_ms * 1e3, 3), "rank": 0},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_tbs, 4), "unit": "TB/s", "h2d_bytes_per_step": h2d,
@@ -573,14 +580,21 @@ def run_matrix(args):
                 fn(i % len(inst))
         g.replay()
         torch.cuda.synchronize()
+        # A burst of heavy cases leaves the SM clock low for up to ~2 s afterwards
+        # (measured: ~1.1 GHz with no throttle reason reported); let it recover so
+        # every case is timed at the same clock, and record the clock per case.
+        time.sleep(args.settle)
+        g.replay()
+        torch.cuda.synchronize()
         samples = []
-        for _ in range(5):
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            g.replay()
-            e1.record()
-            torch.cuda.synchronize()
-            samples.append(e0.elapsed_time(e1) * 1e3 / reps)
+        with ClockSampler(torch.cuda.current_device()) as clocks:
+            for _ in range(5):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                g.replay()
+                e1.record()
+                torch.cuda.synchronize()
+                samples.append(e0.elapsed_time(e1) * 1e3 / reps)
         us = statistics.median(samples)
         bits = sqa.read_device_status(ws.data_ptr(), clear=True)
         if bits:
@@ -592,6 +606,7 @@ def run_matrix(args):
                "tb_s": round(nb / (us * 1e-6) / 1e12, 4),
                "roofline_frac": round(nb / (us * 1e-6) / 1e9 / peak_gbs, 4), "peak_gbs": peak_gbs,
                "peak_source": peak_src, "n_gpus": 1, "replicas": n_rep, "kernel": args.kernel,
+               "sm_mhz": clocks.summary()["sm_mhz"], "clock_reasons": clocks.summary()["reasons"],
                "timing": f"CUDA graph of {reps} back-to-back calls over rotating replicas, median of 5"}
         rows.append(row)
         print(json.dumps(row), flush=True)
@@ -617,6 +632,8 @@ def main():
     ap.add_argument("--matrix-only", action="store_true", help="run only the matrix sweep")
     ap.add_argument("--only", nargs="*", default=None)
     ap.add_argument("--page-mode", default="random", choices=("random", "unique", "shared"))
+    ap.add_argument("--settle", type=float, default=1.0,
+                    help="matrix: seconds of idle before timing each case (clock recovery)")
     ap.add_argument("--kernel", type=int, default=0, choices=(0, 1, 2),
                     help="0 auto, 1 warp-level mma.sync kernel, 2 tcgen05 kernel")
     args = ap.parse_args()

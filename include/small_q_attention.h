@@ -105,9 +105,9 @@ typedef struct sqa_args {
   int32_t num_ctas;
   int32_t min_pages_per_cta;
   /* Kernel choice: 0 = auto (tcgen05 for q_len >= 9, for q_len 5..8 above 512
-   * page-units and for q_len <= 4 from 32768 page-units, where a page-unit is
-   * one page of one KV head, bounded by max_seq_len or max_pages; warp-level
-   * otherwise),
+   * page-units, for q_len 3..4 from 2048 and for q_len <= 2 from 131072
+   * page-units, where a page-unit is one page of one KV head, bounded by
+   * max_seq_len or max_pages; warp-level otherwise),
    * 1 = warp-level mma.sync kernel, 2 = tcgen05 / tensor-memory kernel.
    * Both compute the same operator. */
   int32_t kernel;
@@ -148,6 +148,12 @@ SQA_API int sqa_merge_partials(const float* parts_o, const float* parts_lse, int
  * used by sqa_forward.  Synchronises `stream`.  *device_bits receives the
  * SQA_DEV_* bits; returns SQA_ERR_DEVICE when any bit is set. */
 SQA_API int sqa_read_device_status(void* workspace, uint32_t* device_bits, int clear, void* stream);
+
+/* The kernel sqa_forward would launch for these arguments on `device` (-1 =
+ * the current device): 1 = warp-level mma.sync kernel, 2 = tcgen05 kernel;
+ * minus the SQA_ERR_* code on invalid arguments.  Resolves kernel = 0 (auto).
+ * No upstream counterpart (introspection for measurement and tests). */
+SQA_API int sqa_selected_kernel(const sqa_args* args, int device);
 
 /* Zero a workspace before its first use (asynchronous). */
 SQA_API int sqa_workspace_init(void* workspace, size_t workspace_bytes, void* stream);

@@ -13,6 +13,7 @@ no CPU fallback.
 from .attention import (  # noqa: F401
     merge_partials,
     read_device_status,
+    selected_kernel,
     small_q_attention,
     small_q_attention_partial,
     workspace_bytes,
@@ -24,4 +25,5 @@ __all__ = [
     "merge_partials",
     "workspace_bytes",
     "read_device_status",
+    "selected_kernel",
 ]

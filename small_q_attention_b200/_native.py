@@ -40,6 +40,7 @@ EXPORTED_SYMBOLS = (
     "sqa_workspace_init",
     "sqa_status_string",
     "sqa_abi_version",
+    "sqa_selected_kernel",
 )
 
 
@@ -108,6 +109,8 @@ def library(path: Path | None = None):
         lib.sqa_status_string.restype = ctypes.c_char_p
         lib.sqa_abi_version.argtypes = []
         lib.sqa_abi_version.restype = ctypes.c_int
+        lib.sqa_selected_kernel.argtypes = [ctypes.POINTER(SqaArgs), ctypes.c_int]
+        lib.sqa_selected_kernel.restype = ctypes.c_int
         if path is None:
             _lib = lib
         return lib

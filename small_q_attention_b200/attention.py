@@ -116,6 +116,20 @@ def workspace_for(args: _native.SqaArgs, device: torch.device, workspace: torch.
     return ws.data_ptr(), ws.numel()
 
 
+def selected_kernel(query, key_cache, value_cache, block_tables, seq_lens, page_size,
+                    max_seq_len: int = 0, *, num_ctas: int = 0, min_pages_per_cta: int = 0,
+                    kernel: int = 0) -> int:
+    """The kernel a call with these shapes launches: 1 = warp-level mma.sync,
+    2 = tcgen05 (``kernel=0`` resolved the way ``small_q_attention`` resolves it)."""
+    _check_inputs(query, key_cache, value_cache, block_tables, seq_lens, page_size)
+    args = _fill_args(query, key_cache, value_cache, block_tables, seq_lens, None, max_seq_len,
+                      num_ctas, min_pages_per_cta, kernel)
+    code = _native.library().sqa_selected_kernel(ctypes.byref(args), query.device.index)
+    if code < 0:
+        _native.check(-code, "sqa_selected_kernel")
+    return int(code)
+
+
 def workspace_bytes(query, key_cache, value_cache, block_tables, seq_lens, page_size,
                     max_seq_len: int = 0, *, num_ctas: int = 0, min_pages_per_cta: int = 0,
                     kernel: int = 0) -> int:

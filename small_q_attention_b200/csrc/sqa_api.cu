@@ -13,7 +13,7 @@
 namespace sqa {
 namespace {
 
-constexpr int kAbiVersion = 101;
+constexpr int kAbiVersion = 102;
 constexpr size_t kAlign = 256;
 constexpr int kMaxDevices = 64;
 constexpr int kCtasPerSm = 2;
@@ -22,10 +22,13 @@ constexpr int kCtasPerSm = 2;
 constexpr int kSmemPerSm = 228 * 1024;
 constexpr int kSmemPerCta = kSmemPerSm / kCtasPerSm - 1024;
 constexpr int kMaxSmemPerCta = 227 * 1024;  // dynamic shared memory limit of one CTA on sm_100
-// Auto kernel choice thresholds on the launch's upper bound of units (pages x KV heads):
-// q_len 5..8 takes the tcgen05 kernel above 512 units, q_len <= 4 from 32768 units.
+// Auto kernel choice thresholds on the launch's upper bound of units (pages x KV
+// heads), from the 36-case matrix measured on B200 at 1965 MHz: the tcgen05
+// kernel from 131072 units for q_len <= 2, from 2048 for q_len 3..4, above 512
+// for q_len 5..8, always for q_len >= 9.
+constexpr long long kAutoTcUnitsQ2 = 131072;
+constexpr long long kAutoTcUnitsQ4 = 2048;
 constexpr long long kAutoTcUnitsQ8 = 512;
-constexpr long long kAutoTcUnitsQ4 = 32768;
 constexpr int kDefaultMinPagesPerCta = 4;
 
 size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
@@ -154,7 +157,8 @@ int make_plan(const sqa_args* a, int device, Plan* plan) {
   if (a->kernel == 0) {
     if (a->q_len >= 9) pl.tc = true;
     else if (a->q_len >= 5) pl.tc = units_upper > kAutoTcUnitsQ8;
-    else pl.tc = units_upper >= kAutoTcUnitsQ4;
+    else if (a->q_len >= 3) pl.tc = units_upper >= kAutoTcUnitsQ4;
+    else pl.tc = units_upper >= kAutoTcUnitsQ2;
   } else {
     pl.tc = a->kernel == 2;
   }
@@ -231,6 +235,17 @@ size_t sqa_workspace_bytes(const sqa_args* args, int device, int* status) {
   }
   if (status) *status = st;
   return st == SQA_OK ? pl.bytes : 0;
+}
+
+int sqa_selected_kernel(const sqa_args* args, int device) {
+  int st = validate(args);
+  if (st != SQA_OK) return -st;
+  const int dev = current_device(device);
+  if (dev < 0) return -SQA_ERR_CUDA;
+  Plan pl;
+  st = make_plan(args, dev, &pl);
+  if (st != SQA_OK) return -st;
+  return pl.tc ? 2 : 1;
 }
 
 int sqa_workspace_init(void* workspace, size_t workspace_bytes, void* stream) {
