@@ -1,7 +1,6 @@
 // sqa_merge_row.cuh -- log-sum-exp merge of one output row (one warp).
 //
-// Used by the separate merge kernels (sqa_merge.cu) and by the split-KV
-// kernel's in-kernel merge (sqa_split_kv.cu).  Arithmetic of the upstream
+// Used by the separate merge kernels (sqa_merge.cu).  Arithmetic of the upstream
 // split-KV merge (csrc/small_q_attention_ext.cu:339-366: global max, rescale
 // by exp(stat - max), sum, divide; 0 when the total weight is 0) applied to
 // normalised partials with natural-log LSEs.
