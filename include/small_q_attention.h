@@ -181,6 +181,39 @@ SQA_API int sqa_workspace_init(void* workspace, size_t workspace_bytes, void* st
  * with torch::empty, csrc/small_q_attention_ext.cu:1183-1185). */
 SQA_API int sqa_forward_noalloc(const sqa_args* args, void* stream);
 
+/* ---- Cache append: the step before attention in MTP decoding ----
+ * Writes the K/V of the q_len new tokens of every sequence into their page
+ * slots: token qi of sequence b is position t = seq_lens[b] - q_len + qi
+ * (seq_lens is the length after the append, as the attention takes it,
+ * src/small_q_attention/reference.py:25), stored in page block_tables[b, t/16],
+ * slot t % 16.  The upstream leaves this step to its caller; no upstream
+ * function is replaced.  A sequence with seq_lens < q_len or more pages than
+ * max_pages is skipped whole (SQA_DEV_SEQ_TOO_SHORT / SQA_DEV_SEQ_TOO_LONG), a
+ * token whose page id is outside [0, num_pages) is skipped (SQA_DEV_BAD_PAGE);
+ * the bits are ORed into *status (a device word, e.g. the first word of a
+ * workspace; may be NULL).  Two
+ * tokens mapped to the same slot race.  Asynchronous on `stream`; a pure copy.
+ *   new_keys, new_values  fp16 [batch, q_len, num_kv_heads, 128], 16-byte aligned
+ *   key_cache, value_cache fp16 [num_pages, 16, num_kv_heads, 128], 16-byte aligned */
+typedef struct sqa_append_args {
+  const void* new_keys;
+  const void* new_values;
+  void* key_cache;
+  void* value_cache;
+  const int32_t* block_tables; /* [batch, max_pages] */
+  const int32_t* seq_lens;     /* [batch], lengths after the append */
+  uint32_t* status;            /* device status word or NULL */
+  int32_t batch;
+  int32_t q_len;
+  int32_t num_kv_heads;
+  int32_t head_dim;            /* must be 128 */
+  int32_t page_size;           /* must be 16 */
+  int32_t num_pages;
+  int32_t max_pages;
+} sqa_append_args;
+
+SQA_API int sqa_cache_append(const sqa_append_args* args, void* stream);
+
 /* Static description of a status code. */
 SQA_API const char* sqa_status_string(int status);
 

@@ -4,12 +4,15 @@ Public API:
   small_q_attention(query, key_cache, value_cache, block_tables, seq_lens, page_size, max_seq_len=0)
   small_q_attention_partial(...) -> (O, LSE)   shard form for a split sequence
   merge_partials(parts_o, parts_lse)           log-sum-exp merge of shards
+  cache_append(new_k, new_v, k_cache, v_cache, block_tables, seq_lens)
+                                               write the draft tokens' K/V into their pages
   cuda.forward_v0 ... forward_v5               upstream-compatible entry points
 
 All compute runs in the in-tree C-ABI library ``_lib/libsqa_b200.so``; there is
 no CPU fallback.
 """
 
+from .cache import cache_append  # noqa: F401
 from .attention import (  # noqa: F401
     merge_partials,
     read_device_status,
@@ -26,4 +29,5 @@ __all__ = [
     "workspace_bytes",
     "read_device_status",
     "selected_kernel",
+    "cache_append",
 ]

@@ -41,7 +41,29 @@ EXPORTED_SYMBOLS = (
     "sqa_status_string",
     "sqa_abi_version",
     "sqa_selected_kernel",
+    "sqa_cache_append",
 )
+
+
+class SqaAppendArgs(ctypes.Structure):
+    """Mirror of ``struct sqa_append_args``."""
+
+    _fields_ = [
+        ("new_keys", ctypes.c_void_p),
+        ("new_values", ctypes.c_void_p),
+        ("key_cache", ctypes.c_void_p),
+        ("value_cache", ctypes.c_void_p),
+        ("block_tables", ctypes.c_void_p),
+        ("seq_lens", ctypes.c_void_p),
+        ("status", ctypes.c_void_p),
+        ("batch", ctypes.c_int32),
+        ("q_len", ctypes.c_int32),
+        ("num_kv_heads", ctypes.c_int32),
+        ("head_dim", ctypes.c_int32),
+        ("page_size", ctypes.c_int32),
+        ("num_pages", ctypes.c_int32),
+        ("max_pages", ctypes.c_int32),
+    ]
 
 
 class SqaArgs(ctypes.Structure):
@@ -111,6 +133,8 @@ def library(path: Path | None = None):
         lib.sqa_abi_version.restype = ctypes.c_int
         lib.sqa_selected_kernel.argtypes = [ctypes.POINTER(SqaArgs), ctypes.c_int]
         lib.sqa_selected_kernel.restype = ctypes.c_int
+        lib.sqa_cache_append.argtypes = [ctypes.POINTER(SqaAppendArgs), vp]
+        lib.sqa_cache_append.restype = ctypes.c_int
         if path is None:
             _lib = lib
         return lib

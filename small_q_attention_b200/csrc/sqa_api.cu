@@ -13,7 +13,7 @@
 namespace sqa {
 namespace {
 
-constexpr int kAbiVersion = 102;
+constexpr int kAbiVersion = 103;
 constexpr size_t kAlign = 256;
 constexpr int kMaxDevices = 64;
 constexpr int kCtasPerSm = 2;
