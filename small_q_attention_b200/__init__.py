@@ -6,6 +6,7 @@ Public API:
   merge_partials(parts_o, parts_lse)           log-sum-exp merge of shards
   cache_append(new_k, new_v, k_cache, v_cache, block_tables, seq_lens)
                                                write the draft tokens' K/V into their pages
+  PagedMTPAttention(device).plan(...).run(...)  planned, CUDA-graph-capturable step
   cuda.forward_v0 ... forward_v5               upstream-compatible entry points
 
 All compute runs in the in-tree C-ABI library ``_lib/libsqa_b200.so``; there is
@@ -13,6 +14,7 @@ no CPU fallback.
 """
 
 from .cache import cache_append  # noqa: F401
+from .wrapper import PagedMTPAttention  # noqa: F401
 from .attention import (  # noqa: F401
     merge_partials,
     read_device_status,
@@ -30,4 +32,5 @@ __all__ = [
     "read_device_status",
     "selected_kernel",
     "cache_append",
+    "PagedMTPAttention",
 ]
