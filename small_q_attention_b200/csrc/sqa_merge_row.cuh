@@ -15,8 +15,8 @@ constexpr float kMergeLog2e = 1.4426950408889634f;
 
 // Merge `cnt` parts of one row; part i's row is at o + i * o_stride and
 // lse + i * lse_stride.  Writes to whichever of out / out_o / out_lse is set.
-// Parts are taken 8 at a time with all their loads issued before use, so a
-// row costs one memory round trip per 8 parts rather than one per part.
+// Parts are taken 8 at a time with all loads of a batch issued before use: one
+// memory round trip per 8 parts.
 // kCoherent reads through L2 (ld.global.cg): required when the parts were
 // written by other CTAs of the same kernel; otherwise the read-only path.
 template <bool kCoherent>
@@ -27,13 +27,10 @@ __device__ __forceinline__ void merge_row(const float* o, size_t o_stride, const
   const int lane = threadIdx.x & 31;
   auto load_f = [](const float* ptr) { return kCoherent ? __ldcg(ptr) : __ldg(ptr); };
   auto load_f4 = [](const float4* ptr) { return kCoherent ? __ldcg(ptr) : __ldg(ptr); };
-  float mmax = -INFINITY;
-  for (int i = lane; i < cnt; i += 32) mmax = fmaxf(mmax, load_f(lse + i * lse_stride));
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) mmax = fmaxf(mmax, __shfl_xor_sync(0xffffffffu, mmax, off));
-  const float base = (mmax == -INFINITY) ? 0.f : mmax;
-
-  float total = 0.f;
+  // Batches of 8 parts, every load of a batch in flight at once (one memory
+  // round trip per batch); a running max rescales what earlier batches summed.
+  // With at most 8 parts this is: global max, weights exp(lse_i - max), sum.
+  float base = -INFINITY, total = 0.f;
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int i0 = 0; i0 < cnt; i0 += kBatch) {
     float4 v[kBatch];
@@ -45,6 +42,19 @@ __device__ __forceinline__ void merge_row(const float* o, size_t o_stride, const
                 : make_float4(0.f, 0.f, 0.f, 0.f);
       l[j] = ok ? load_f(lse + (i0 + j) * lse_stride) : -INFINITY;
     }
+    float mx = base;
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) mx = fmaxf(mx, l[j]);
+    if (mx == -INFINITY) continue;  // nothing visible so far
+    if (mx > base && base != -INFINITY) {
+      const float scale = ex2((base - mx) * kMergeLog2e);
+      total *= scale;
+      acc.x *= scale;
+      acc.y *= scale;
+      acc.z *= scale;
+      acc.w *= scale;
+    }
+    base = mx;
 #pragma unroll
     for (int j = 0; j < kBatch; ++j) {
       const float wgt = ex2((l[j] - base) * kMergeLog2e);  // -inf -> 0
