@@ -15,12 +15,12 @@
  * (src/small_q_attention/cuda.py:177-214 -> csrc/small_q_attention_ext.cu:1132-1210).
  *
  * Layout (all row-major, contiguous):
- *   query        fp16  [batch, q_len, num_q_heads, 128]
- *   key_cache    fp16  [num_pages, 16, num_kv_heads, 128]
- *   value_cache  fp16  [num_pages, 16, num_kv_heads, 128]
+ *   query        fp16 or bf16 (sqa_args.dtype)  [batch, q_len, num_q_heads, 128]
+ *   key_cache    same type  [num_pages, 16, num_kv_heads, 128]
+ *   value_cache  same type  [num_pages, 16, num_kv_heads, 128]
  *   block_tables int32 [batch, max_pages]   (row stride max_pages)
  *   seq_lens     int32 [batch]              (total length incl. the q_len drafts)
- *   out          fp16  [batch, q_len, num_q_heads, 128]
+ *   out          same type  [batch, q_len, num_q_heads, 128]
  * Supported: head_dim 128, page_size 16, num_q_heads == 4 * num_kv_heads,
  * 1 <= q_len <= 16.  All pointers are device pointers; query/out/caches must
  * be 16-byte aligned.
@@ -111,7 +111,14 @@ typedef struct sqa_args {
    * 1 = warp-level mma.sync kernel, 2 = tcgen05 / tensor-memory kernel.
    * Both compute the same operator. */
   int32_t kernel;
+  /* Element type of query, key_cache, value_cache and out: SQA_DTYPE_F16 or
+   * SQA_DTYPE_BF16 (all four the same; accumulation is fp32 either way).  The
+   * upstream supports fp16 only (src/small_q_attention/cuda.py:197-211). */
+  int32_t dtype;
 } sqa_args;
+
+#define SQA_DTYPE_F16 0
+#define SQA_DTYPE_BF16 1
 
 /* Workspace bytes sqa_forward needs for these arguments on `device`
  * (-1 = the current device).  Depends only on shapes and tuning fields.

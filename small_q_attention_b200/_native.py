@@ -23,6 +23,10 @@ SQA_ERR_WORKSPACE_TOO_SMALL = 3
 SQA_ERR_CUDA = 4
 SQA_ERR_DEVICE = 5
 
+# element types (SQA_DTYPE_*)
+DTYPE_F16 = 0
+DTYPE_BF16 = 1
+
 # device status bits (SQA_DEV_*)
 DEV_TIMEOUT = 1
 DEV_SEQ_TOO_LONG = 2
@@ -91,6 +95,7 @@ class SqaArgs(ctypes.Structure):
         ("num_ctas", ctypes.c_int32),
         ("min_pages_per_cta", ctypes.c_int32),
         ("kernel", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
     ]
 
 

@@ -46,8 +46,9 @@ def _check_inputs(query, key_cache, value_cache, block_tables, seq_lens, page_si
         raise ValueError("all inputs must be on the same CUDA device")
     if any(not t.is_contiguous() for t in tensors):
         raise ValueError("all inputs must be contiguous")
-    if query.dtype != torch.float16 or key_cache.dtype != torch.float16 or value_cache.dtype != torch.float16:
-        raise ValueError("the kernel requires FP16 Q/K/V")
+    if query.dtype not in (torch.float16, torch.bfloat16) or key_cache.dtype != query.dtype \
+            or value_cache.dtype != query.dtype:
+        raise ValueError("the kernel requires FP16 (or BF16) Q/K/V, all of one type")
     if any(t.dtype != torch.int32 for t in tensors[3:]):
         raise ValueError("block_tables, seq_lens and mask_lens must be int32")
     if query.dim() != 4 or key_cache.dim() != 4:
@@ -88,6 +89,7 @@ def _fill_args(query, key_cache, value_cache, block_tables, seq_lens, mask_lens,
     a.num_ctas = int(num_ctas)
     a.min_pages_per_cta = int(min_pages_per_cta)
     a.kernel = int(kernel)
+    a.dtype = _native.DTYPE_BF16 if query.dtype == torch.bfloat16 else _native.DTYPE_F16
     return a
 
 
@@ -179,7 +181,10 @@ def _run(args, device, workspace, check):
 def small_q_attention(query, key_cache, value_cache, block_tables, seq_lens, page_size: int,
                       max_seq_len: int = 0, *, out=None, workspace=None, num_ctas: int = 0,
                       min_pages_per_cta: int = 0, kernel: int = 0, check: bool = False):
-    """Causal paged MTP attention; returns fp16 ``[batch, q_len, Hq, 128]``.
+    """Causal paged MTP attention; returns ``[batch, q_len, Hq, 128]`` in the input type.
+
+    Q/K/V are FP16 (the upstream contract) or BF16 (all three of one type;
+    accumulation is FP32 either way).
 
     ``seq_lens[b]`` is the KV length including the ``q_len`` draft tokens and
     draft row ``qi`` sees tokens ``< seq_lens[b] - q_len + qi + 1``
@@ -195,8 +200,8 @@ def small_q_attention(query, key_cache, value_cache, block_tables, seq_lens, pag
     _check_inputs(query, key_cache, value_cache, block_tables, seq_lens, page_size)
     if out is None:
         out = torch.empty_like(query)
-    elif out.shape != query.shape or out.dtype != torch.float16 or not out.is_contiguous() or out.device != query.device:
-        raise ValueError("out must be a contiguous fp16 tensor shaped like query")
+    elif out.shape != query.shape or out.dtype != query.dtype or not out.is_contiguous() or out.device != query.device:
+        raise ValueError("out must be a contiguous tensor shaped and typed like query")
     args = _fill_args(query, key_cache, value_cache, block_tables, seq_lens, None, max_seq_len,
                       num_ctas, min_pages_per_cta, kernel)
     args.out = out.data_ptr()
@@ -237,9 +242,10 @@ def small_q_attention_partial(query, key_cache, value_cache, block_tables, seq_l
 def merge_partials(parts_o, parts_lse, *, out=None, out_dtype=torch.float16, return_lse: bool = False):
     """Log-sum-exp merge of stacked partials ``[n, ..., 128]`` / ``[n, ...]``.
 
-    Returns the merged output in ``out_dtype`` (fp16 or fp32) and, with
+    Returns the merged output in ``out_dtype`` (fp16, bf16 or fp32) and, with
     ``return_lse``, the merged LSE.  Same arithmetic as the upstream split-KV
-    merge (``csrc/small_q_attention_ext.cu:339-366``).
+    merge (``csrc/small_q_attention_ext.cu:339-366``).  BF16 output is merged in
+    fp32 and rounded once (``sqa_merge_partials`` writes fp16 or fp32).
     """
     if not (parts_o.is_cuda and parts_lse.is_cuda):
         raise ValueError("partials must be CUDA tensors")
@@ -254,6 +260,13 @@ def merge_partials(parts_o, parts_lse, *, out=None, out_dtype=torch.float16, ret
     shape = parts_o.shape[1:]
     if out is None:
         out = torch.empty(shape, dtype=out_dtype, device=parts_o.device)
+    if out.dtype not in (torch.float16, torch.bfloat16, torch.float32) or out.shape != shape:
+        raise ValueError("out must be fp16, bf16 or fp32 and shaped like one part")
+    if out.dtype == torch.bfloat16:
+        merged = merge_partials(parts_o, parts_lse, out_dtype=torch.float32, return_lse=return_lse)
+        o32, lse = merged if return_lse else (merged, None)
+        out.copy_(o32)
+        return (out, lse) if return_lse else out
     lse = torch.empty(parts_lse.shape[1:], dtype=torch.float32, device=parts_o.device) if return_lse else None
     o16 = out.data_ptr() if out.dtype == torch.float16 else None
     o32 = out.data_ptr() if out.dtype == torch.float32 else None

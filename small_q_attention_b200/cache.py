@@ -53,8 +53,8 @@ def cache_append(new_keys, new_values, key_cache, value_cache, block_tables, seq
         raise ValueError("all inputs must be on the same CUDA device")
     if any(not t.is_contiguous() for t in tensors):
         raise ValueError("all inputs must be contiguous")
-    if any(t.dtype != torch.float16 for t in tensors[:4]):
-        raise ValueError("new K/V and the caches must be FP16")
+    if new_keys.dtype not in (torch.float16, torch.bfloat16) or any(t.dtype != new_keys.dtype for t in tensors[1:4]):
+        raise ValueError("new K/V and the caches must be FP16 (or BF16), all of one type")
     if block_tables.dtype != torch.int32 or seq_lens.dtype != torch.int32:
         raise ValueError("block_tables and seq_lens must be int32")
     if new_keys.dim() != 4 or new_values.shape != new_keys.shape:

@@ -13,7 +13,7 @@
 namespace sqa {
 namespace {
 
-constexpr int kAbiVersion = 103;
+constexpr int kAbiVersion = 104;
 constexpr size_t kAlign = 256;
 constexpr int kMaxDevices = 64;
 constexpr int kCtasPerSm = 2;
@@ -119,6 +119,7 @@ int validate(const sqa_args* a) {
   if (a->q_len > SQA_MAX_Q_LEN) return SQA_ERR_UNSUPPORTED;
   if (a->max_seq_len < 0 || a->num_ctas < 0 || a->min_pages_per_cta < 0) return SQA_ERR_INVALID_ARGUMENT;
   if (a->kernel < 0 || a->kernel > 2) return SQA_ERR_INVALID_ARGUMENT;
+  if (a->dtype != SQA_DTYPE_F16 && a->dtype != SQA_DTYPE_BF16) return SQA_ERR_UNSUPPORTED;
   // unit indices are 32-bit on the device
   if ((long long)a->batch * a->num_kv_heads * a->max_pages >= (1ll << 31)) return SQA_ERR_UNSUPPORTED;
   if ((long long)a->num_pages * kPageSize >= (1ll << 31)) return SQA_ERR_UNSUPPORTED;
@@ -300,6 +301,7 @@ int forward_impl(const sqa_args* a, void* workspace, size_t workspace_bytes, voi
   p.rows_pad = pl.shape.rows_pad;
   p.timeline = pl.off_timeline ? reinterpret_cast<unsigned long long*>(ws + pl.off_timeline) : nullptr;
   p.scale_log2 = 1.4426950408889634f / sqrtf((float)kHeadDim);
+  p.bf16 = a->dtype == SQA_DTYPE_BF16;
 
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_ptr);
   if (ev_before && cudaEventRecord(reinterpret_cast<cudaEvent_t>(ev_before), stream) != cudaSuccess)
@@ -329,6 +331,7 @@ int forward_impl(const sqa_args* a, void* workspace, size_t workspace_bytes, voi
   m.hq = a->num_q_heads;
   m.hkv = a->num_kv_heads;
   m.max_pages = a->max_pages;
+  m.bf16 = p.bf16;
   if (launch_segment_merge(m, pl.shape.rows_pad, stream) != cudaSuccess) return SQA_ERR_CUDA;
   if (!debug_sync(stream, "merge kernel", pl.segments, 0, a)) return SQA_ERR_CUDA;
   return SQA_OK;
@@ -359,6 +362,7 @@ int sqa_merge_partials(const float* parts_o, const float* parts_lse, int32_t num
   m.out_o = out_o;
   m.out_lse = out_lse;
   m.rows = rows;
+  m.bf16 = 0;
   m.num_parts = num_parts;
   return launch_partials_merge(m, reinterpret_cast<cudaStream_t>(stream)) == cudaSuccess ? SQA_OK : SQA_ERR_CUDA;
 }

@@ -36,7 +36,7 @@ inline WarpShape warp_shape_for(int q_len) {
 }
 
 struct SplitKvParams {
-  const __half* q;              // [B, q_len, Hq, 128]
+  const __half* q;              // [B, q_len, Hq, 128] (fp16 or bf16 bits)
   const int32_t* block_tables;  // [B, max_pages]
   const int32_t* seq_lens;      // [B]
   const int32_t* mask_lens;     // [B] or nullptr
@@ -53,6 +53,7 @@ struct SplitKvParams {
   int rows_pad;                 // workspace rows per piece
   unsigned long long* timeline; // -DSQA_DEBUG_TIMELINE: 8 stamps per CTA, else nullptr
   float scale_log2;             // head_dim^-0.5 * log2(e)
+  int bf16;                     // q / caches / out hold bf16 (else fp16) bits
 };
 
 struct MergeParams {
@@ -69,6 +70,7 @@ struct MergeParams {
   int num_parts;                // cross-device merge: parts; per-call merge: workspace partial slots
   int piece_rows;               // rows per piece (rows_pad for the per-call merge)
   int batch, q_len, hq, hkv, max_pages;
+  int bf16;                     // out holds bf16 (else fp16)
 };
 
 // Launchers (stream-ordered, no allocation).  Return cudaGetLastError().

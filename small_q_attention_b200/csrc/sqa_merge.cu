@@ -1,12 +1,12 @@
 // sqa_merge.cu -- log-sum-exp merge of split-KV partials.
 //
-// One warp merges one output row: lanes load the parts' log-sum-exps 32 at a
-// time, take the max, and each lane then accumulates a float4 column of the
-// 128-dim row over the parts with weights exp(lse_i - LSE).  A row whose parts
-// all have lse = -inf (no visible key) is written as 0 (and -inf).  This is
-// the arithmetic of the upstream split-KV merge
-// (csrc/small_q_attention_ext.cu:339-366: global max, rescale, sum, divide,
-// 0 when the denominator is 0) on normalised partials.
+// One warp merges one output row: each lane accumulates a float4 column of
+// the 128-dim row over the parts with weights exp(lse_i - LSE), 8 parts per
+// memory round trip (sqa_merge_row.cuh).  A row whose parts all have
+// lse = -inf (no visible key) is written as 0 (and -inf).  This is the
+// arithmetic of the upstream split-KV merge (csrc/small_q_attention_ext.cu:
+// 339-366: global max, rescale, sum, divide, 0 when the denominator is 0) on
+// normalised partials.
 #include "sqa_internal.h"
 #include "sqa_merge_row.cuh"
 #include "sqa_ptx.cuh"
@@ -36,7 +36,7 @@ __global__ void __launch_bounds__(128) sqa_segment_merge_kernel(const MergeParam
 
   const int len = max(__ldg(p.seq_lens + b), 0);
   if (len == 0) {  // no page was processed for this sequence: nothing is visible
-    if (out) reinterpret_cast<uint2*>(out)[lane] = make_uint2(0u, 0u);
+    if (out) reinterpret_cast<uint2*>(out)[lane] = make_uint2(0u, 0u);  // +0 in fp16 and bf16
     if (out_o) reinterpret_cast<float4*>(out_o)[lane] = make_float4(0.f, 0.f, 0.f, 0.f);
     if (out_lse && lane == 0) *out_lse = -INFINITY;
     return;
@@ -46,7 +46,7 @@ __global__ void __launch_bounds__(128) sqa_segment_merge_kernel(const MergeParam
   if (!SQA_CHECK(info.x >= 0 && info.x + info.y <= p.num_parts, p.status, 8, s)) return;
   const size_t first = (size_t)info.x * p.piece_rows + row;
   merge_row<false>(p.parts_o + first * kHeadDim, (size_t)p.piece_rows * kHeadDim, p.parts_lse + first,
-            (size_t)p.piece_rows, info.y, out, out_o, out_lse);
+            (size_t)p.piece_rows, info.y, out, out_o, out_lse, p.bf16 != 0);
   if (threadIdx.x == 0) SQA_STAMP(tl, 2);
 }
 
@@ -58,7 +58,7 @@ __global__ void __launch_bounds__(128) sqa_partials_merge_kernel(const MergePara
   if (row >= p.rows) return;
   merge_row<false>(p.parts_o + row * kHeadDim, (size_t)p.rows * kHeadDim, p.parts_lse + row, (size_t)p.rows,
             p.num_parts, p.out ? p.out + row * kHeadDim : nullptr,
-            p.out_o ? p.out_o + row * kHeadDim : nullptr, p.out_lse ? p.out_lse + row : nullptr);
+            p.out_o ? p.out_o + row * kHeadDim : nullptr, p.out_lse ? p.out_lse + row : nullptr, p.bf16 != 0);
 }
 
 // 128-thread launch that may overlap the previous kernel's tail (programmatic

@@ -14,7 +14,8 @@ namespace sqa {
 constexpr float kMergeLog2e = 1.4426950408889634f;
 
 // Merge `cnt` parts of one row; part i's row is at o + i * o_stride and
-// lse + i * lse_stride.  Writes to whichever of out / out_o / out_lse is set.
+// lse + i * lse_stride.  Writes to whichever of out (fp16, or bf16 with
+// out_bf16) / out_o / out_lse is set.
 // Parts are taken 8 at a time with all loads of a batch issued before use: one
 // memory round trip per 8 parts.
 // kCoherent reads through L2 (ld.global.cg): required when the parts were
@@ -22,7 +23,7 @@ constexpr float kMergeLog2e = 1.4426950408889634f;
 template <bool kCoherent>
 __device__ __forceinline__ void merge_row(const float* o, size_t o_stride, const float* lse,
                                           size_t lse_stride, int cnt, __half* out, float* out_o,
-                                          float* out_lse) {
+                                          float* out_lse, bool out_bf16 = false) {
   constexpr int kBatch = 8;
   const int lane = threadIdx.x & 31;
   auto load_f = [](const float* ptr) { return kCoherent ? __ldcg(ptr) : __ldg(ptr); };
@@ -72,8 +73,8 @@ __device__ __forceinline__ void merge_row(const float* o, size_t o_stride, const
   acc.w *= inv;
   if (out != nullptr) {
     uint2 h;
-    h.x = pack_half2(acc.x, acc.y);
-    h.y = pack_half2(acc.z, acc.w);
+    h.x = out_bf16 ? pack_bf162(acc.x, acc.y) : pack_half2(acc.x, acc.y);
+    h.y = out_bf16 ? pack_bf162(acc.z, acc.w) : pack_half2(acc.z, acc.w);
     reinterpret_cast<uint2*>(out)[lane] = h;
   }
   if (out_o != nullptr) reinterpret_cast<float4*>(out_o)[lane] = acc;

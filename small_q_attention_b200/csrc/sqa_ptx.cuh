@@ -9,6 +9,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
 
@@ -211,14 +212,23 @@ __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
   return y;
 }
 
-// D = A(16x16, row) * B(16x8, col) + D, fp16 inputs, fp32 accumulate.
+// D = A(16x16, row) * B(16x8, col) + D, fp16 (or, kBf16, bf16) inputs, fp32 accumulate.
+template <bool kBf16 = false>
 __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
                                           uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
-      "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  if constexpr (kBf16) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+        "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
 }
 
 // 2^x with the SFU approximation (ex2.approx.ftz.f32); ex2(-inf) = +0.
@@ -231,6 +241,18 @@ __device__ __forceinline__ float ex2(float x) {
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ uint32_t pack_bf162(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Two floats as the path's 16-bit element type (round to nearest even).
+template <bool kBf16>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  if constexpr (kBf16) return pack_bf162(lo, hi);
+  else return pack_half2(lo, hi);
 }
 
 // Programmatic dependent launch.  grid_dependency_wait() blocks until the
@@ -372,10 +394,12 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo
   return d;
 }
 
-// Instruction descriptor of tcgen05.mma.kind::f16: fp16 A/B, fp32 D.
-__host__ __device__ constexpr uint32_t mma_idesc_f16(int m, int n, bool a_mn_major, bool b_mn_major) {
-  return (1u << 4)                                 // D format: f32
-         | (0u << 7) | (0u << 10)                  // A, B format: f16
+// Instruction descriptor of tcgen05.mma.kind::f16: fp16 (bf16 = false) or bf16
+// A and B (always the same type), fp32 D.
+__host__ __device__ constexpr uint32_t mma_idesc_f16(int m, int n, bool a_mn_major, bool b_mn_major,
+                                                     bool bf16 = false) {
+  return (1u << 4)                                           // D format: f32
+         | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10)  // A, B format: f16 = 0, bf16 = 1
          | ((a_mn_major ? 1u : 0u) << 15) | ((b_mn_major ? 1u : 0u) << 16)
          | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }

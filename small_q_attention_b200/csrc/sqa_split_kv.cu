@@ -139,7 +139,7 @@ __device__ void producer_loop(const SplitKvParams& p, const Schedule& sch, const
 }
 
 // ------------------------------------------------------------------ consumers
-template <int NT, int WR>
+template <int NT, int WR, bool BF>
 __device__ void consumer_loop(const SplitKvParams& p, const Schedule& sch, uint8_t* stages,
                               uint64_t* full, uint64_t* empty, float* cbuf, float* mbuf, float* lbuf,
                               volatile int* abort) {
@@ -260,8 +260,8 @@ __device__ void consumer_loop(const SplitKvParams& p, const Schedule& sch, uint8
         ldsm_x4(a, k_base + (kk >> 2) * 2048 + k_row * 128 + chunk * 16);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-          if (kk & 1) mma_16816(sb[nt], a, qf[nt][kk][0], qf[nt][kk][1]);
-          else mma_16816(sa[nt], a, qf[nt][kk][0], qf[nt][kk][1]);
+          if (kk & 1) mma_16816<BF>(sb[nt], a, qf[nt][kk][0], qf[nt][kk][1]);
+          else mma_16816<BF>(sa[nt], a, qf[nt][kk][0], qf[nt][kk][1]);
         }
       }
 
@@ -295,8 +295,8 @@ __device__ void consumer_loop(const SplitKvParams& p, const Schedule& sch, uint8
         l_run[nt][0] = l_run[nt][0] * alpha[nt][0] + (p0 + p2);
         l_run[nt][1] = l_run[nt][1] * alpha[nt][1] + (p1 + p3);
         // [tok g | tok g+8][rows 2t, 2t+1] -> transpose -> B fragment [tok 2t.., 2t+8..][row g]
-        pb[nt][0] = movmatrix_trans(pack_half2(p0, p1));
-        pb[nt][1] = movmatrix_trans(pack_half2(p2, p3));
+        pb[nt][0] = movmatrix_trans(pack2<BF>(p0, p1));
+        pb[nt][1] = movmatrix_trans(pack2<BF>(p2, p3));
       }
       bool rescale = false;
 #pragma unroll
@@ -320,7 +320,7 @@ __device__ void consumer_loop(const SplitKvParams& p, const Schedule& sch, uint8
         const int chunk = (((md & 3) << 1) | v_cb) ^ (v_row & 7);
         ldsm_x4_trans(a, v_base + (md >> 2) * 2048 + v_row * 128 + chunk * 16);
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) mma_16816(o[md][nt], a, pb[nt][0], pb[nt][1]);
+        for (int nt = 0; nt < NT; ++nt) mma_16816<BF>(o[md][nt], a, pb[nt][0], pb[nt][1]);
       }
 
       if (tail) fence_proxy_async_smem();  // generic writes above vs the next TMA into this stage
@@ -393,8 +393,8 @@ __device__ void consumer_loop(const SplitKvParams& p, const Schedule& sch, uint8
       if (whole) {
         if (p.out != nullptr) {
           uint2 h;
-          h.x = pack_half2(acc.x, acc.y);
-          h.y = pack_half2(acc.z, acc.w);
+          h.x = pack2<BF>(acc.x, acc.y);
+          h.y = pack2<BF>(acc.z, acc.w);
           *reinterpret_cast<uint2*>(p.out + out_row * kHeadDim + c4) = h;
         } else {
           *reinterpret_cast<float4*>(p.out_o + out_row * kHeadDim + c4) = acc;
@@ -413,7 +413,7 @@ __device__ void consumer_loop(const SplitKvParams& p, const Schedule& sch, uint8
   }
 }
 
-template <int NT, int WR>
+template <int NT, int WR, bool BF>
 __global__ void __launch_bounds__(kThreads, 2)
     sqa_split_kv_kernel(const SplitKvParams p, const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v) {
@@ -466,7 +466,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     producer_loop(p, s, &tm_k, &tm_v, stages, full, empty, abort);
     if ((threadIdx.x & 31) == 0) SQA_STAMP(tl, 5);  // producer done (all loads issued and landed)
   } else {
-    consumer_loop<NT, WR>(p, s, stages, full, empty, cbuf, mbuf, lbuf, abort);
+    consumer_loop<NT, WR, BF>(p, s, stages, full, empty, cbuf, mbuf, lbuf, abort);
     if (threadIdx.x == 0) SQA_STAMP(tl, 4);  // consumers done (last epilogue written)
 #ifdef SQA_DEBUG_TIMELINE
     if (threadIdx.x == 0 && tl) {
@@ -478,10 +478,10 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 }
 
-template <int NT, int WR>
+template <int NT, int WR, bool BF>
 cudaError_t launch_shape(const SplitKvParams& p, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
                          int grid, int smem_bytes, cudaStream_t stream) {
-  auto kernel = sqa_split_kv_kernel<NT, WR>;
+  auto kernel = sqa_split_kv_kernel<NT, WR, BF>;
   // Raise the dynamic shared-memory limit once per device (the size is fixed
   // per warp shape), outside any stream capture that may follow.
   static int configured[64] = {0};
@@ -523,10 +523,16 @@ int split_kv_smem_bytes(const WarpShape& ws, int num_stages) {
 cudaError_t launch_split_kv(const SplitKvParams& p, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
                             int grid, int smem_bytes, cudaStream_t stream) {
   const WarpShape ws = warp_shape_for(p.q_len);
-  if (ws.nt == 1) return launch_shape<1, 1>(p, tm_k, tm_v, grid, smem_bytes, stream);
-  if (ws.wr == 1) return launch_shape<2, 1>(p, tm_k, tm_v, grid, smem_bytes, stream);
-  if (ws.wr == 2) return launch_shape<2, 2>(p, tm_k, tm_v, grid, smem_bytes, stream);
-  return launch_shape<2, 4>(p, tm_k, tm_v, grid, smem_bytes, stream);
+  if (p.bf16) {
+    if (ws.nt == 1) return launch_shape<1, 1, true>(p, tm_k, tm_v, grid, smem_bytes, stream);
+    if (ws.wr == 1) return launch_shape<2, 1, true>(p, tm_k, tm_v, grid, smem_bytes, stream);
+    if (ws.wr == 2) return launch_shape<2, 2, true>(p, tm_k, tm_v, grid, smem_bytes, stream);
+    return launch_shape<2, 4, true>(p, tm_k, tm_v, grid, smem_bytes, stream);
+  }
+  if (ws.nt == 1) return launch_shape<1, 1, false>(p, tm_k, tm_v, grid, smem_bytes, stream);
+  if (ws.wr == 1) return launch_shape<2, 1, false>(p, tm_k, tm_v, grid, smem_bytes, stream);
+  if (ws.wr == 2) return launch_shape<2, 2, false>(p, tm_k, tm_v, grid, smem_bytes, stream);
+  return launch_shape<2, 4, false>(p, tm_k, tm_v, grid, smem_bytes, stream);
 }
 
 }  // namespace sqa

@@ -179,9 +179,10 @@ __device__ __forceinline__ void tc_mma_drain(const SplitKvParams& p, const TcSme
 
 // S(h) = Q K_h^T into slot h % kNumS, once the block's pages are in and PV(h - kNumS)
 // has released the slot; Q of a piece is in TMEM once q_ready completes.
+template <bool BF>
 __device__ void tc_mma_qk(const SplitKvParams& p, const Schedule& sch, const TcSmem& sm, uint32_t tmem,
                           volatile int* abort) {
-  constexpr uint32_t kIdescQK = mma_idesc_f16(128, kBlockTokens, false, false);  // Q (TMEM) x K_block (K-major)
+  constexpr uint32_t kIdescQK = mma_idesc_f16(128, kBlockTokens, false, false, BF);  // Q (TMEM) x K_block (K-major)
   const int NB = p.num_stages;
   SegWalk w = first_segment(p, sch);
   int h = 0;   // CTA block counter
@@ -228,10 +229,10 @@ __device__ void tc_mma_qk(const SplitKvParams& p, const Schedule& sch, const TcS
 
 // O += P V_g once the softmax has written P(g); then the block's ring slot and
 // S/P slot are released by commits.
-template <int R>
+template <int R, bool BF>
 __device__ void tc_mma_pv(const SplitKvParams& p, const Schedule& sch, const TcSmem& sm, uint32_t tmem,
                           volatile int* abort) {
-  constexpr uint32_t kIdescPV = mma_idesc_f16(128, 128, false, true);  // P (TMEM) x V (MN-major)
+  constexpr uint32_t kIdescPV = mma_idesc_f16(128, 128, false, true, BF);  // P (TMEM) x V (MN-major)
   constexpr int kPPR = kBP / R;       // pages of a block per replica
   constexpr int kLanesPR = 128 / R;   // TMEM lanes per replica
   const int NB = p.num_stages;
@@ -277,7 +278,7 @@ __device__ void tc_mma_pv(const SplitKvParams& p, const Schedule& sch, const TcS
 }
 
 // ------------------------------------------------------------------ softmax + epilogue (4 warps)
-template <int R>
+template <int R, bool BF>
 __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const TcSmem& sm, uint32_t tmem,
                            volatile int* abort) {
   constexpr int kLanesPR = 128 / R;          // lanes (rows) per replica
@@ -409,7 +410,7 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
         const float p0 = ex2(fmaf(__uint_as_float(sraw[2 * t]), cs, nbase));
         const float p1 = ex2(fmaf(__uint_as_float(sraw[2 * t + 1]), cs, nbase));
         ls[t & 1] += p0 + p1;
-        pk[t] = pack_half2(p0, p1);
+        pk[t] = pack2<BF>(p0, p1);
       }
       l += ls[0] + ls[1];
       if constexpr (kTok == 16) tmem_st8(slot_col + tok_lo / 2, pk);
@@ -490,10 +491,10 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
         const int col = c0 + ch * 8;
         if (whole && p.out != nullptr) {
           uint4 h;
-          h.x = pack_half2(v[0], v[1]);
-          h.y = pack_half2(v[2], v[3]);
-          h.z = pack_half2(v[4], v[5]);
-          h.w = pack_half2(v[6], v[7]);
+          h.x = pack2<BF>(v[0], v[1]);
+          h.y = pack2<BF>(v[2], v[3]);
+          h.z = pack2<BF>(v[4], v[5]);
+          h.w = pack2<BF>(v[6], v[7]);
           *reinterpret_cast<uint4*>(p.out + out_row * kHeadDim + col) = h;
         } else {
           float* dst = whole ? p.out_o + out_row * kHeadDim + col
@@ -521,7 +522,7 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
   }
 }
 
-template <int R>
+template <int R, bool BF>
 __global__ void __launch_bounds__(kThreadsTc, 1)
     sqa_split_kv_tc_kernel(const SplitKvParams p, const __grid_constant__ CUtensorMap tm_k,
                            const __grid_constant__ CUtensorMap tm_v) {
@@ -579,11 +580,11 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
   if (warp == kProducerWarp) {
     tc_producer(p, s, &tm_k, &tm_v, sm, abort);
   } else if (warp == kMmaWarp) {
-    tc_mma_qk(p, s, sm, tmem, abort);
+    tc_mma_qk<BF>(p, s, sm, tmem, abort);
   } else if (warp == kPvWarp) {
-    tc_mma_pv<R>(p, s, sm, tmem, abort);
+    tc_mma_pv<R, BF>(p, s, sm, tmem, abort);
   } else {
-    tc_softmax<R>(p, s, sm, tmem, abort);
+    tc_softmax<R, BF>(p, s, sm, tmem, abort);
   }
 
   tc_fence_before();
@@ -604,10 +605,10 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
 #endif
 }
 
-template <int R>
+template <int R, bool BF>
 cudaError_t launch_tc(const SplitKvParams& p, const CUtensorMap& tm_k, const CUtensorMap& tm_v, int grid,
                       int smem_bytes, cudaStream_t stream) {
-  auto kernel = sqa_split_kv_tc_kernel<R>;
+  auto kernel = sqa_split_kv_tc_kernel<R, BF>;
   static int configured[64] = {0};
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
@@ -642,8 +643,12 @@ int split_kv_tc_smem_bytes(int num_blocks) {
 
 cudaError_t launch_split_kv_tc(const SplitKvParams& p, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
                                int grid, int smem_bytes, cudaStream_t stream) {
-  if (kGroup * p.q_len <= 32) return launch_tc<4>(p, tm_k, tm_v, grid, smem_bytes, stream);
-  return launch_tc<2>(p, tm_k, tm_v, grid, smem_bytes, stream);
+  if (p.bf16) {
+    if (kGroup * p.q_len <= 32) return launch_tc<4, true>(p, tm_k, tm_v, grid, smem_bytes, stream);
+    return launch_tc<2, true>(p, tm_k, tm_v, grid, smem_bytes, stream);
+  }
+  if (kGroup * p.q_len <= 32) return launch_tc<4, false>(p, tm_k, tm_v, grid, smem_bytes, stream);
+  return launch_tc<2, false>(p, tm_k, tm_v, grid, smem_bytes, stream);
 }
 
 }  // namespace sqa

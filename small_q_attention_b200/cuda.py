@@ -33,8 +33,17 @@ def _check_chunk(chunk_keys):
         raise ValueError("chunk_keys must be positive")
 
 
+def _fp16_only(query, key_cache, value_cache):
+    # the upstream wrappers accept FP16 only (cuda.py:197-211); small_q_attention also takes BF16
+    import torch
+
+    if any(isinstance(t, torch.Tensor) and t.dtype != torch.float16 for t in (query, key_cache, value_cache)):
+        raise ValueError("the kernel requires FP16 Q/K/V")
+
+
 def forward_v0(query, key_cache, value_cache, block_tables, seq_lens, page_size: int, verbose: bool = False):
     _load(verbose)
+    _fp16_only(query, key_cache, value_cache)
     return small_q_attention(query, key_cache, value_cache, block_tables, seq_lens, page_size)
 
 
@@ -45,6 +54,7 @@ def forward_v2(query, key_cache, value_cache, block_tables, seq_lens, page_size:
                chunk_keys: int = 512, verbose: bool = False):
     _check_chunk(chunk_keys)
     _load(verbose)
+    _fp16_only(query, key_cache, value_cache)
     return small_q_attention(query, key_cache, value_cache, block_tables, seq_lens, page_size)
 
 
@@ -52,6 +62,7 @@ def forward_v3(query, key_cache, value_cache, block_tables, seq_lens, page_size:
                chunk_keys: int = 512, max_seq_len: int = 0, verbose: bool = False):
     _check_chunk(chunk_keys)
     _load(verbose)
+    _fp16_only(query, key_cache, value_cache)
     return small_q_attention(query, key_cache, value_cache, block_tables, seq_lens, page_size,
                              max_seq_len=max_seq_len)
 

@@ -66,7 +66,7 @@ def algorithmic_bytes(batch: int, q_len: int, lens, hq: int = HQ, hkv: int = HKV
 
 def make_case(batch: int, q_len: int, lens, *, hkv: int = HKV, pool_factor: float = 1.0,
               page_mode: str = "random", seed: int = 0, device="cuda", k_outlier_frac: float = 0.0,
-              gen_device=None, max_pages: int | None = None):
+              gen_device=None, max_pages: int | None = None, dtype=torch.float16):
     """Seeded fp16 Q/K/V caches, int32 page table and lengths on ``device``.
 
     ``gen_device`` is where the random numbers are drawn ("cpu" for
@@ -84,9 +84,10 @@ def make_case(batch: int, q_len: int, lens, *, hkv: int = HKV, pool_factor: floa
         pool = max(needed, int(math.ceil(needed * pool_factor)), 1)
     g = torch.Generator(device=gen_device).manual_seed(seed)
     hq = 4 * hkv
-    query = torch.randn(batch, q_len, hq, HEAD_DIM, generator=g, device=gen_device, dtype=torch.float16)
-    key_cache = torch.randn(pool, PAGE, hkv, HEAD_DIM, generator=g, device=gen_device, dtype=torch.float16)
-    value_cache = torch.randn(pool, PAGE, hkv, HEAD_DIM, generator=g, device=gen_device, dtype=torch.float16)
+    query = torch.randn(batch, q_len, hq, HEAD_DIM, generator=g, device=gen_device, dtype=torch.float16).to(dtype)
+    key_cache = torch.randn(pool, PAGE, hkv, HEAD_DIM, generator=g, device=gen_device, dtype=torch.float16).to(dtype)
+    value_cache = torch.randn(pool, PAGE, hkv, HEAD_DIM, generator=g, device=gen_device,
+                              dtype=torch.float16).to(dtype)
     if k_outlier_frac > 0:
         hit = torch.rand(pool, PAGE, generator=g, device=gen_device) < k_outlier_frac
         key_cache[hit] *= 4

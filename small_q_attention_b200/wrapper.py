@@ -108,8 +108,8 @@ class PagedMTPAttention:
             raise ValueError("inputs are not on the planned device")
         if out is None:
             out = torch.empty_like(query)
-        elif out.shape != query.shape or out.dtype != torch.float16 or not out.is_contiguous() or out.device != query.device:
-            raise ValueError("out must be a contiguous fp16 tensor shaped like query")
+        elif out.shape != query.shape or out.dtype != query.dtype or not out.is_contiguous() or out.device != query.device:
+            raise ValueError("out must be a contiguous tensor shaped and typed like query")
         if (append_keys is None) != (append_values is None):
             raise ValueError("append_keys and append_values go together")
         if append_keys is not None:
