@@ -59,6 +59,17 @@ def _peaks():
 
 
 KERNEL_NAMES = {1: "sqa_split_kv_kernel", 2: "sqa_split_kv_tc_kernel"}
+DTYPES = {}  # filled lazily (torch is imported inside the run functions)
+
+
+def _as_dtype(c, name):
+    """A workload dict with its Q/K/V cast to ``name`` ("f16" leaves it as generated)."""
+    if name == "f16":
+        return c
+    import torch
+
+    t = {"bf16": torch.bfloat16}[name]
+    return dict(c, query=c["query"].to(t), key_cache=c["key_cache"].to(t), value_cache=c["value_cache"].to(t))
 
 
 def _traffic(workload: str, kernel_id: int):
@@ -535,6 +546,7 @@ def run_matrix(args):
     from small_q_attention_b200.workloads import CONFIGS, make_case, make_config, matrix_cases
 
     torch.cuda.set_device(0)
+    DTYPES.update({"f16": torch.float16, "bf16": torch.bfloat16})
     peak_gbs, peak_src = _peaks()
     rows = []
     # one explicit workspace, large enough for every case (16 KV-head segments x 64 rows worst case)
@@ -547,11 +559,11 @@ def run_matrix(args):
                  if label_of(n, c) in args.only or (c and f"q{c['q_len']}" in args.only)]
     for name, c in cases:
         if c is None:
-            first = make_config(name, seed=0)
+            first = _as_dtype(make_config(name, seed=0), args.dtype)
             label = name
         else:
             first = make_case(c["batch"], c["q_len"], [c["kv_len"]] * c["batch"], pool_factor=1.0,
-                              page_mode=args.page_mode, seed=0)
+                              dtype=DTYPES[args.dtype], page_mode=args.page_mode, seed=0)
             label = f"q{c['q_len']}_kv{c['kv_len']}_b{c['batch']}"
         nb = _case_bytes(first)
         # distinct input copies so that consecutive calls never find K/V in L2:
@@ -561,9 +573,10 @@ def run_matrix(args):
         inst = [first]
         for s_ in range(1, n_rep):
             if c is None:
-                inst.append(make_config(name, seed=s_))
+                inst.append(_as_dtype(make_config(name, seed=s_), args.dtype))
             else:
                 inst.append(make_case(c["batch"], c["q_len"], [c["kv_len"]] * c["batch"], pool_factor=1.0,
+                                      dtype=DTYPES[args.dtype],
                                       page_mode=args.page_mode, seed=s_))
         outs = [torch.empty_like(x["query"]) for x in inst]
         fn = lambda i: sqa.small_q_attention(  # noqa: E731
@@ -607,6 +620,7 @@ def run_matrix(args):
                "roofline_frac": round(nb / (us * 1e-6) / 1e9 / peak_gbs, 4), "peak_gbs": peak_gbs,
                "peak_source": peak_src, "n_gpus": 1, "replicas": n_rep, "kernel": args.kernel,
                "sm_mhz": clocks.summary()["sm_mhz"], "clock_reasons": clocks.summary()["reasons"],
+               "dtype": args.dtype,
                "timing": f"CUDA graph of {reps} back-to-back calls over rotating replicas, median of 5"}
         rows.append(row)
         print(json.dumps(row), flush=True)
@@ -632,6 +646,8 @@ def main():
     ap.add_argument("--matrix-only", action="store_true", help="run only the matrix sweep")
     ap.add_argument("--only", nargs="*", default=None)
     ap.add_argument("--page-mode", default="random", choices=("random", "unique", "shared"))
+    ap.add_argument("--dtype", default="f16", choices=("f16", "bf16"),
+                    help="matrix: element type of Q/K/V (the driver line is always f16)")
     ap.add_argument("--settle", type=float, default=1.0,
                     help="matrix: seconds of idle before timing each case (clock recovery)")
     ap.add_argument("--kernel", type=int, default=0, choices=(0, 1, 2),
