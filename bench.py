@@ -383,29 +383,65 @@ def run_ours(args):
     kern_bytes = bytes_rank + (2 * 16 * 32 * 128 * 2 if longctx else 0)
     achieved_gbs = kern_bytes / (kern_ms * 1e-3) / 1e9
 
-    # --- e2e through the public API with host buffers
+    # --- e2e through the public API with host buffers: the step's small inputs
+    # (Q, page table, lengths) go up in one pinned copy, the output comes back
     small = ("query", "block_tables", "seq_lens") + (("mask_lens",) if longctx else ())
-    host_in = [{k: r[k].cpu().pin_memory() for k in small} for r in reps]
-    dev_in = [{k: torch.empty_like(r[k]) for k in small} for r in reps]
+
+    def _packed(r, pin):
+        """One uint8 buffer holding the step's small inputs back to back (256-B aligned) + typed views."""
+        sizes = [r[k].numel() * r[k].element_size() for k in small]
+        offs, total = [], 0
+        for n in sizes:
+            offs.append(total)
+            total += (n + 255) // 256 * 256
+        buf = torch.empty(total, dtype=torch.uint8, pin_memory=pin, device="cpu" if pin else device)
+        views = {k: buf[o:o + n].view(r[k].dtype).view(r[k].shape) for k, o, n in zip(small, offs, sizes)}
+        return buf, views
+
+    host_in, dev_in = [], []
+    for r in reps:
+        hb, hv = _packed(r, True)
+        for k in small:
+            hv[k].copy_(r[k].cpu())
+        db, dv = _packed(r, False)
+        host_in.append(hb)
+        dev_in.append((db, dv))
     host_out = torch.empty(reps[0]["query"].shape, dtype=torch.float16, pin_memory=True)
-    h2d = sum(t.numel() * t.element_size() for t in host_in[0].values())
+    h2d = host_in[0].numel()
     d2h = host_out.numel() * host_out.element_size()
     e2e_out = [torch.empty_like(r["query"]) for r in reps]
 
+    # A serving loop's pipeline: each step's H2D copy runs on a copy stream and may
+    # overlap the previous step's kernel; the step's D2H read runs on a second copy
+    # stream after its kernel.  Every step's copies are inside the timed region.
+    s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    ev_in = [torch.cuda.Event() for _ in range(REPLICAS)]
+    ev_done = [torch.cuda.Event() for _ in range(REPLICAS)]
+    ev_out = [torch.cuda.Event() for _ in range(REPLICAS)]
+
     def e2e_step(i):
         j = i % REPLICAS
-        for k in small:
-            dev_in[j][k].copy_(host_in[j][k], non_blocking=True)
-        d = dev_in[j]
+        s_in.wait_event(ev_done[j])  # the kernel that last read dev_in[j] has finished
+        with torch.cuda.stream(s_in):
+            dev_in[j][0].copy_(host_in[j], non_blocking=True)
+            ev_in[j].record(s_in)
+        stream.wait_event(ev_in[j])
+        stream.wait_event(ev_out[j])  # the D2H that last read e2e_out[j] has finished
+        d = dev_in[j][1]
+        # `stream` is the current stream for the whole loop (set once below)
         if longctx:
             o = long_context_attention(d["query"], reps[j]["key_cache"], reps[j]["value_cache"],
                                        d["block_tables"], d["seq_lens"], d["mask_lens"], 16, out=e2e_out[j],
                                        workspace=ws)
         else:
             o = sqa.small_q_attention(d["query"], reps[j]["key_cache"], reps[j]["value_cache"],
-                                      d["block_tables"], d["seq_lens"], 16, max_len, out=e2e_out[j], workspace=ws,
-                                      kernel=args.kernel)
-        host_out.copy_(o, non_blocking=True)
+                                      d["block_tables"], d["seq_lens"], 16, max_len, out=e2e_out[j],
+                                      workspace=ws, kernel=args.kernel)
+        ev_done[j].record(stream)
+        s_out.wait_event(ev_done[j])
+        with torch.cuda.stream(s_out):
+            host_out.copy_(o, non_blocking=True)
+            ev_out[j].record(s_out)
 
     with torch.cuda.stream(stream):
         for i in range(W):
@@ -416,8 +452,11 @@ def run_ours(args):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
         e0.record(stream)
+        s_in.wait_stream(stream)
         for i in range(K):
             e2e_step(i)
+        for ev in ev_out:
+            stream.wait_event(ev)
         e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = _max_over_ranks(e0.elapsed_time(e1), dist, device)

@@ -26,37 +26,78 @@ PAGE_SIZE = 16
 GQA_GROUP = 4
 MAX_Q_LEN = 16
 
+_DTYPES = (torch.float16, torch.bfloat16)
 _ws_lock = threading.Lock()
 _workspaces: dict[tuple[int, int], torch.Tensor] = {}
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+_cuda_ok: bool | None = None
+
+
 def _stream_handle(device: torch.device) -> int:
+    """cudaStream_t of torch's current stream on ``device`` (the raw handle lookup
+    avoids building a Stream object on every call)."""
+    if _raw_stream is not None:
+        return _raw_stream(device.index)
     return torch.cuda.current_stream(device).cuda_stream
 
 
+def _cuda_available() -> bool:
+    global _cuda_ok
+    if _cuda_ok is None:
+        _cuda_ok = torch.cuda.is_available()
+    return _cuda_ok
+
+
+class _on_device:
+    """``torch.cuda.device(device)`` only when it is not already current (the
+    context manager costs several microseconds per call)."""
+
+    __slots__ = ("index", "prev")
+
+    def __init__(self, device: torch.device):
+        self.index = device.index
+
+    def __enter__(self):
+        self.prev = torch.cuda.current_device()
+        if self.prev != self.index:
+            torch.cuda.set_device(self.index)
+        return self
+
+    def __exit__(self, *exc):
+        if self.prev != self.index:
+            torch.cuda.set_device(self.prev)
+        return False
+
+
 def _check_inputs(query, key_cache, value_cache, block_tables, seq_lens, page_size, mask_lens=None):
-    if not torch.cuda.is_available():
+    if not _cuda_available():
         raise RuntimeError("CUDA is required for the small-q attention kernel")
-    tensors = [query, key_cache, value_cache, block_tables, seq_lens]
-    if mask_lens is not None:
-        tensors.append(mask_lens)
-    if any(not isinstance(t, torch.Tensor) or not t.is_cuda for t in tensors):
+    tensors = (query, key_cache, value_cache, block_tables, seq_lens) + ((mask_lens,) if mask_lens is not None else ())
+    if not all(isinstance(t, torch.Tensor) for t in tensors):
         raise ValueError("all inputs must be CUDA tensors")
-    if any(t.device != query.device for t in tensors):
-        raise ValueError("all inputs must be on the same CUDA device")
-    if any(not t.is_contiguous() for t in tensors):
-        raise ValueError("all inputs must be contiguous")
-    if query.dtype not in (torch.float16, torch.bfloat16) or key_cache.dtype != query.dtype \
-            or value_cache.dtype != query.dtype:
+    dev = query.device
+    if dev.type != "cuda":
+        raise ValueError("all inputs must be CUDA tensors")
+    for t in tensors:
+        if t.device != dev:
+            raise ValueError("all inputs must be CUDA tensors on the same device")
+        if not t.is_contiguous():
+            raise ValueError("all inputs must be contiguous")
+    qd = query.dtype
+    if qd not in _DTYPES or key_cache.dtype != qd or value_cache.dtype != qd:
         raise ValueError("the kernel requires FP16 (or BF16) Q/K/V, all of one type")
-    if any(t.dtype != torch.int32 for t in tensors[3:]):
-        raise ValueError("block_tables, seq_lens and mask_lens must be int32")
+    for t in tensors[3:]:
+        if t.dtype != torch.int32:
+            raise ValueError("block_tables, seq_lens and mask_lens must be int32")
     if query.dim() != 4 or key_cache.dim() != 4:
         raise ValueError("query and key_cache must be 4-D")
-    if value_cache.shape != key_cache.shape:
+    kshape = key_cache.shape
+    if value_cache.shape != kshape:
         raise ValueError("value_cache shape mismatch")
     batch, q_len, hq, head_dim = query.shape
-    _, cache_page, hkv, cache_dim = key_cache.shape
+    _, cache_page, hkv, cache_dim = kshape
     if not (1 <= q_len <= MAX_Q_LEN):
         raise ValueError(f"q_len must be in [1, {MAX_Q_LEN}]")
     if head_dim != HEAD_DIM or cache_dim != HEAD_DIM:
@@ -69,46 +110,49 @@ def _check_inputs(query, key_cache, value_cache, block_tables, seq_lens, page_si
         raise ValueError("invalid metadata: block_tables must be [batch, max_pages], seq_lens [batch]")
     if mask_lens is not None and mask_lens.numel() != batch:
         raise ValueError("mask_lens must have one entry per sequence")
-    if key_cache.shape[0] == 0 or block_tables.shape[1] == 0:
+    if kshape[0] == 0 or block_tables.shape[1] == 0:
         raise ValueError("empty KV cache is not supported")
 
 
 def _fill_args(query, key_cache, value_cache, block_tables, seq_lens, mask_lens, max_seq_len,
                num_ctas, min_pages_per_cta, kernel: int = 0) -> _native.SqaArgs:
-    a = _native.SqaArgs()
-    a.query = query.data_ptr()
-    a.key_cache = key_cache.data_ptr()
-    a.value_cache = value_cache.data_ptr()
-    a.block_tables = block_tables.data_ptr()
-    a.seq_lens = seq_lens.data_ptr()
-    a.mask_lens = mask_lens.data_ptr() if mask_lens is not None else None
-    a.batch, a.q_len, a.num_q_heads, a.head_dim = (int(x) for x in query.shape)
-    a.num_pages, a.page_size, a.num_kv_heads = (int(x) for x in key_cache.shape[:3])
-    a.max_pages = int(block_tables.shape[1])
-    a.max_seq_len = int(max_seq_len)
-    a.num_ctas = int(num_ctas)
-    a.min_pages_per_cta = int(min_pages_per_cta)
-    a.kernel = int(kernel)
-    a.dtype = _native.DTYPE_BF16 if query.dtype == torch.bfloat16 else _native.DTYPE_F16
-    return a
+    batch, q_len, hq, head_dim = query.shape
+    num_pages, page_size, hkv, _ = key_cache.shape
+    return _native.SqaArgs(
+        query.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(), block_tables.data_ptr(),
+        seq_lens.data_ptr(), mask_lens.data_ptr() if mask_lens is not None else None, None, None, None,
+        batch, q_len, hq, hkv, head_dim, page_size, num_pages, block_tables.shape[1], int(max_seq_len),
+        int(num_ctas), int(min_pages_per_cta), int(kernel),
+        _native.DTYPE_BF16 if query.dtype == torch.bfloat16 else _native.DTYPE_F16)
+
+
+_need_cache: dict[tuple, int] = {}
+
+
+def _workspace_need(args: _native.SqaArgs, device_index: int) -> int:
+    key = (device_index, args.batch, args.q_len, args.num_kv_heads, args.num_pages, args.max_pages,
+           args.max_seq_len, args.num_ctas, args.min_pages_per_cta, args.kernel)
+    need = _need_cache.get(key)
+    if need is None:
+        st = ctypes.c_int(0)
+        need = int(_native.library().sqa_workspace_bytes(ctypes.byref(args), device_index, ctypes.byref(st)))
+        _native.check(st.value, "sqa_workspace_bytes")
+        _need_cache[key] = need
+    return need
 
 
 def workspace_for(args: _native.SqaArgs, device: torch.device, workspace: torch.Tensor | None = None):
-    """Return (pointer, bytes) of a workspace large enough for ``args``.
+    """Return (pointer, bytes) of the workspace for ``args``.
 
-    With ``workspace=None`` one uint8 buffer per (device, stream) is kept and
-    grown on demand; its status word starts zeroed.
+    A caller's ``workspace`` is used as given (``sqa_forward`` rejects one that
+    is too small).  With ``workspace=None`` one uint8 buffer per (device,
+    stream) is kept and grown on demand; its status word starts zeroed.
     """
-    lib = _native.library()
-    st = ctypes.c_int(0)
-    need = lib.sqa_workspace_bytes(ctypes.byref(args), device.index, ctypes.byref(st))
-    _native.check(st.value, "sqa_workspace_bytes")
     if workspace is not None:
         if workspace.device != device or not workspace.is_contiguous():
             raise ValueError("workspace must be a contiguous tensor on the query's device")
-        if workspace.numel() * workspace.element_size() < need:
-            raise ValueError(f"workspace too small: need {need} bytes")
         return workspace.data_ptr(), workspace.numel() * workspace.element_size()
+    need = _workspace_need(args, device.index)
     key = (device.index, _stream_handle(device))
     with _ws_lock:
         ws = _workspaces.get(key)
@@ -170,9 +214,11 @@ def _raise_device_bits(bits: int) -> None:
 def _run(args, device, workspace, check):
     ws_ptr, ws_bytes = workspace_for(args, device, workspace)
     stream = _stream_handle(device)
-    with torch.cuda.device(device):
+    with _on_device(device):
         code = _native.library().sqa_forward(ctypes.byref(args), ctypes.c_void_p(ws_ptr),
                                             ctypes.c_size_t(ws_bytes), ctypes.c_void_p(stream))
+        if code == _native.SQA_ERR_WORKSPACE_TOO_SMALL and workspace is not None:
+            raise ValueError(f"workspace too small: need {_workspace_need(args, device.index)} bytes")
         _native.check(code, "sqa_forward")
         if check:
             _raise_device_bits(read_device_status(ws_ptr, clear=True, device=device))
@@ -270,7 +316,7 @@ def merge_partials(parts_o, parts_lse, *, out=None, out_dtype=torch.float16, ret
     lse = torch.empty(parts_lse.shape[1:], dtype=torch.float32, device=parts_o.device) if return_lse else None
     o16 = out.data_ptr() if out.dtype == torch.float16 else None
     o32 = out.data_ptr() if out.dtype == torch.float32 else None
-    with torch.cuda.device(parts_o.device):
+    with _on_device(parts_o.device):
         code = _native.library().sqa_merge_partials(
             ctypes.c_void_p(parts_o.data_ptr()), ctypes.c_void_p(parts_lse.data_ptr()), n, rows,
             ctypes.c_void_p(o16), ctypes.c_void_p(o32),

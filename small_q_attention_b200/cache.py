@@ -18,7 +18,8 @@ import threading
 import torch
 
 from . import _native
-from .attention import HEAD_DIM, PAGE_SIZE, _raise_device_bits, _stream_handle, read_device_status
+from .attention import (HEAD_DIM, PAGE_SIZE, _cuda_available, _on_device, _raise_device_bits, _stream_handle,
+                        read_device_status)
 
 _status_lock = threading.Lock()
 _status_words: dict[tuple[int, int], torch.Tensor] = {}
@@ -44,7 +45,7 @@ def cache_append(new_keys, new_values, key_cache, value_cache, block_tables, seq
     ``ValueError`` for ``seq_lens < q_len`` or lengths beyond the page table and
     ``IndexError`` for a page id outside the cache (those tokens are not written).
     """
-    if not torch.cuda.is_available():
+    if not _cuda_available():
         raise RuntimeError("CUDA is required for the cache-append kernel")
     tensors = [new_keys, new_values, key_cache, value_cache, block_tables, seq_lens]
     if any(not isinstance(t, torch.Tensor) or not t.is_cuda for t in tensors):
@@ -87,7 +88,7 @@ def cache_append(new_keys, new_values, key_cache, value_cache, block_tables, seq
     a.batch, a.q_len, a.num_kv_heads = batch, q_len, hkv
     a.head_dim, a.page_size = HEAD_DIM, PAGE_SIZE
     a.num_pages, a.max_pages = int(key_cache.shape[0]), int(block_tables.shape[1])
-    with torch.cuda.device(device):
+    with _on_device(device):
         code = _native.library().sqa_cache_append(ctypes.byref(a), ctypes.c_void_p(_stream_handle(device)))
         _native.check(code, "sqa_cache_append")
         if check:

@@ -66,7 +66,7 @@ EncodeTiledFn encode_fn() {
 
 // [num_pages * 16 tokens, Hkv, 128] fp16 seen as a 3-D tensor; one box is
 // 64 dims x 1 head x 16 tokens (2 KB), 128-byte swizzled.
-bool encode_cache_map(CUtensorMap* map, const void* base, int num_pages, int hkv) {
+bool encode_cache_map_uncached(CUtensorMap* map, const void* base, int num_pages, int hkv) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   const cuuint64_t dims[3] = {(cuuint64_t)kHeadDim, (cuuint64_t)hkv, (cuuint64_t)num_pages * kPageSize};
@@ -76,6 +76,30 @@ bool encode_cache_map(CUtensorMap* map, const void* base, int num_pages, int hkv
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// A serving loop passes the same caches on every call: keep the last few
+// encoded maps per host thread (a map depends only on base, pages and heads;
+// the element type does not matter to a copy of 2-byte elements).
+bool encode_cache_map(CUtensorMap* map, const void* base, int num_pages, int hkv) {
+  struct Entry {
+    const void* base;
+    int num_pages, hkv;
+    CUtensorMap map;
+  };
+  constexpr int kEntries = 8;
+  thread_local Entry cache[kEntries] = {};
+  thread_local int next = 0;
+  for (int i = 0; i < kEntries; ++i) {
+    if (cache[i].base == base && cache[i].num_pages == num_pages && cache[i].hkv == hkv && base != nullptr) {
+      *map = cache[i].map;
+      return true;
+    }
+  }
+  if (!encode_cache_map_uncached(map, base, num_pages, hkv)) return false;
+  cache[next] = Entry{base, num_pages, hkv, *map};
+  next = (next + 1) % kEntries;
+  return true;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }

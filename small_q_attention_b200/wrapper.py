@@ -21,7 +21,7 @@ import ctypes
 import torch
 
 from . import _native
-from .attention import (GQA_GROUP, HEAD_DIM, MAX_Q_LEN, PAGE_SIZE, _check_inputs, _fill_args,
+from .attention import (GQA_GROUP, HEAD_DIM, MAX_Q_LEN, PAGE_SIZE, _check_inputs, _fill_args, _on_device,
                         _raise_device_bits, _stream_handle, read_device_status)
 from .cache import cache_append
 
@@ -118,7 +118,7 @@ class PagedMTPAttention:
                        self._num_ctas, self._min_pages, self._kernel)
         a.out = out.data_ptr()
         ws = self._workspace
-        with torch.cuda.device(self.device):
+        with _on_device(self.device):
             code = _native.library().sqa_forward(ctypes.byref(a), ctypes.c_void_p(ws.data_ptr()),
                                                 ctypes.c_size_t(ws.numel()),
                                                 ctypes.c_void_p(_stream_handle(self.device)))
