@@ -115,10 +115,26 @@ typedef struct sqa_args {
    * SQA_DTYPE_BF16 (all four the same; accumulation is fp32 either way).  The
    * upstream supports fp16 only (src/small_q_attention/cuda.py:197-211). */
   int32_t dtype;
+  /* Cache layout: SQA_KV_NHD = [num_pages, 16, num_kv_heads, 128] (the upstream's,
+   * ext.cu:466) or SQA_KV_HND = [num_pages, num_kv_heads, 16, 128] (one KV head's
+   * page contiguous; the default layout of FlashInfer's paged decode). */
+  int32_t kv_layout;
+  /* Softmax scale applied to q.k (0 = 1/sqrt(128), the upstream's,
+   * src/small_q_attention/reference.py:46) and a factor applied to every output
+   * row (0 = 1); e.g. FlashInfer's bmm1_scale / bmm2_scale. */
+  float sm_scale;
+  float out_scale;
+  /* Elements from one page to the next in key_cache and value_cache (0 = the
+   * caches are contiguous tensors, 16 * num_kv_heads * 128).  Larger values
+   * address one layer of a bigger pool or K and V interleaved per page
+   * ([num_pages, 2, ...]); a multiple of 8 (16-byte aligned pages). */
+  int64_t page_stride;
 } sqa_args;
 
 #define SQA_DTYPE_F16 0
 #define SQA_DTYPE_BF16 1
+#define SQA_KV_NHD 0
+#define SQA_KV_HND 1
 
 /* Workspace bytes sqa_forward needs for these arguments on `device`
  * (-1 = the current device).  Depends only on shapes and tuning fields.
@@ -201,7 +217,9 @@ SQA_API int sqa_forward_noalloc(const sqa_args* args, void* stream);
  * workspace; may be NULL).  Two
  * tokens mapped to the same slot race.  Asynchronous on `stream`; a pure copy.
  *   new_keys, new_values  fp16 [batch, q_len, num_kv_heads, 128], 16-byte aligned
- *   key_cache, value_cache fp16 [num_pages, 16, num_kv_heads, 128], 16-byte aligned */
+ *   key_cache, value_cache [num_pages, 16, num_kv_heads, 128] (NHD) or
+ *                          [num_pages, num_kv_heads, 16, 128] (HND), 16-byte aligned.
+ *   Any 2-byte element type (fp16 or bf16: the append is a copy). */
 typedef struct sqa_append_args {
   const void* new_keys;
   const void* new_values;
@@ -217,6 +235,8 @@ typedef struct sqa_append_args {
   int32_t page_size;           /* must be 16 */
   int32_t num_pages;
   int32_t max_pages;
+  int32_t kv_layout;           /* SQA_KV_NHD or SQA_KV_HND, as in sqa_args */
+  int64_t page_stride;         /* elements from page to page, 0 = contiguous (as in sqa_args) */
 } sqa_append_args;
 
 SQA_API int sqa_cache_append(const sqa_append_args* args, void* stream);

@@ -27,6 +27,10 @@ SQA_ERR_DEVICE = 5
 DTYPE_F16 = 0
 DTYPE_BF16 = 1
 
+# cache layouts (SQA_KV_*)
+KV_NHD = 0
+KV_HND = 1
+
 # device status bits (SQA_DEV_*)
 DEV_TIMEOUT = 1
 DEV_SEQ_TOO_LONG = 2
@@ -67,6 +71,8 @@ class SqaAppendArgs(ctypes.Structure):
         ("page_size", ctypes.c_int32),
         ("num_pages", ctypes.c_int32),
         ("max_pages", ctypes.c_int32),
+        ("kv_layout", ctypes.c_int32),
+        ("page_stride", ctypes.c_int64),
     ]
 
 
@@ -96,6 +102,10 @@ class SqaArgs(ctypes.Structure):
         ("min_pages_per_cta", ctypes.c_int32),
         ("kernel", ctypes.c_int32),
         ("dtype", ctypes.c_int32),
+        ("kv_layout", ctypes.c_int32),
+        ("sm_scale", ctypes.c_float),
+        ("out_scale", ctypes.c_float),
+        ("page_stride", ctypes.c_int64),
     ]
 
 

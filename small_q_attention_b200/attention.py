@@ -71,7 +71,39 @@ class _on_device:
         return False
 
 
-def _check_inputs(query, key_cache, value_cache, block_tables, seq_lens, page_size, mask_lens=None):
+_LAYOUTS = {"NHD": 0, "HND": 1}
+
+
+def _layout_code(kv_layout: str) -> int:
+    code = _LAYOUTS.get(kv_layout)
+    if code is None:
+        raise ValueError('kv_layout must be "NHD" ([pages, 16, Hkv, 128]) or "HND" ([pages, Hkv, 16, 128])')
+    return code
+
+
+def _cache_page_stride(key_cache, value_cache) -> int:
+    """Elements from one page to the next (0 = contiguous caches).
+
+    The caches may be views with a larger page stride, e.g. ``kv[:, 0]`` / ``kv[:, 1]``
+    of a ``[pages, 2, ...]`` pool or one layer of a multi-layer pool: every dim but
+    the page dim must be packed, the page stride a multiple of 8 elements, and K
+    and V must have the same strides.
+    """
+    if key_cache.dim() != 4:
+        raise ValueError("key_cache must be 4-D")
+    if key_cache.is_contiguous() and value_cache.is_contiguous():
+        return 0
+    st = key_cache.stride()
+    inner = key_cache.shape[1] * key_cache.shape[2] * key_cache.shape[3]
+    packed = (key_cache.shape[2] * key_cache.shape[3], key_cache.shape[3], 1)
+    if value_cache.stride() != st or tuple(st[1:]) != packed or st[0] < inner or st[0] % 8:
+        raise ValueError("key_cache / value_cache must be packed within a page, with one page stride "
+                         "(a multiple of 8 elements) shared by K and V")
+    return int(st[0])
+
+
+def _check_inputs(query, key_cache, value_cache, block_tables, seq_lens, page_size, mask_lens=None,
+                  kv_layout: str = "NHD"):
     if not _cuda_available():
         raise RuntimeError("CUDA is required for the small-q attention kernel")
     tensors = (query, key_cache, value_cache, block_tables, seq_lens) + ((mask_lens,) if mask_lens is not None else ())
@@ -80,11 +112,12 @@ def _check_inputs(query, key_cache, value_cache, block_tables, seq_lens, page_si
     dev = query.device
     if dev.type != "cuda":
         raise ValueError("all inputs must be CUDA tensors")
-    for t in tensors:
+    for i, t in enumerate(tensors):
         if t.device != dev:
             raise ValueError("all inputs must be CUDA tensors on the same device")
-        if not t.is_contiguous():
+        if i not in (1, 2) and not t.is_contiguous():
             raise ValueError("all inputs must be contiguous")
+    _cache_page_stride(key_cache, value_cache)
     qd = query.dtype
     if qd not in _DTYPES or key_cache.dtype != qd or value_cache.dtype != qd:
         raise ValueError("the kernel requires FP16 (or BF16) Q/K/V, all of one type")
@@ -97,7 +130,10 @@ def _check_inputs(query, key_cache, value_cache, block_tables, seq_lens, page_si
     if value_cache.shape != kshape:
         raise ValueError("value_cache shape mismatch")
     batch, q_len, hq, head_dim = query.shape
-    _, cache_page, hkv, cache_dim = kshape
+    if _layout_code(kv_layout):
+        _, hkv, cache_page, cache_dim = kshape
+    else:
+        _, cache_page, hkv, cache_dim = kshape
     if not (1 <= q_len <= MAX_Q_LEN):
         raise ValueError(f"q_len must be in [1, {MAX_Q_LEN}]")
     if head_dim != HEAD_DIM or cache_dim != HEAD_DIM:
@@ -105,7 +141,7 @@ def _check_inputs(query, key_cache, value_cache, block_tables, seq_lens, page_si
     if hq % hkv != 0 or hq // hkv != GQA_GROUP:
         raise ValueError("the kernel requires a GQA group size of exactly 4 (Hq/Hkv = 32/8)")
     if int(page_size) != cache_page or cache_page != PAGE_SIZE:
-        raise ValueError("page_size must be 16 and match key_cache.shape[1]")
+        raise ValueError("page_size must be 16 and match the cache's page dimension")
     if block_tables.dim() != 2 or block_tables.shape[0] != batch or seq_lens.numel() != batch:
         raise ValueError("invalid metadata: block_tables must be [batch, max_pages], seq_lens [batch]")
     if mask_lens is not None and mask_lens.numel() != batch:
@@ -115,15 +151,22 @@ def _check_inputs(query, key_cache, value_cache, block_tables, seq_lens, page_si
 
 
 def _fill_args(query, key_cache, value_cache, block_tables, seq_lens, mask_lens, max_seq_len,
-               num_ctas, min_pages_per_cta, kernel: int = 0) -> _native.SqaArgs:
+               num_ctas, min_pages_per_cta, kernel: int = 0, kv_layout: str = "NHD", sm_scale=None,
+               out_scale: float = 1.0) -> _native.SqaArgs:
     batch, q_len, hq, head_dim = query.shape
-    num_pages, page_size, hkv, _ = key_cache.shape
+    layout = _layout_code(kv_layout)
+    if layout:
+        num_pages, hkv, page_size, _ = key_cache.shape
+    else:
+        num_pages, page_size, hkv, _ = key_cache.shape
     return _native.SqaArgs(
         query.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(), block_tables.data_ptr(),
         seq_lens.data_ptr(), mask_lens.data_ptr() if mask_lens is not None else None, None, None, None,
         batch, q_len, hq, hkv, head_dim, page_size, num_pages, block_tables.shape[1], int(max_seq_len),
         int(num_ctas), int(min_pages_per_cta), int(kernel),
-        _native.DTYPE_BF16 if query.dtype == torch.bfloat16 else _native.DTYPE_F16)
+        _native.DTYPE_BF16 if query.dtype == torch.bfloat16 else _native.DTYPE_F16, layout,
+        0.0 if sm_scale is None else float(sm_scale), float(out_scale),
+        _cache_page_stride(key_cache, value_cache))
 
 
 _need_cache: dict[tuple, int] = {}
@@ -164,12 +207,12 @@ def workspace_for(args: _native.SqaArgs, device: torch.device, workspace: torch.
 
 def selected_kernel(query, key_cache, value_cache, block_tables, seq_lens, page_size,
                     max_seq_len: int = 0, *, num_ctas: int = 0, min_pages_per_cta: int = 0,
-                    kernel: int = 0) -> int:
+                    kernel: int = 0, kv_layout: str = "NHD") -> int:
     """The kernel a call with these shapes launches: 1 = warp-level mma.sync,
     2 = tcgen05 (``kernel=0`` resolved the way ``small_q_attention`` resolves it)."""
-    _check_inputs(query, key_cache, value_cache, block_tables, seq_lens, page_size)
+    _check_inputs(query, key_cache, value_cache, block_tables, seq_lens, page_size, kv_layout=kv_layout)
     args = _fill_args(query, key_cache, value_cache, block_tables, seq_lens, None, max_seq_len,
-                      num_ctas, min_pages_per_cta, kernel)
+                      num_ctas, min_pages_per_cta, kernel, kv_layout)
     code = _native.library().sqa_selected_kernel(ctypes.byref(args), query.device.index)
     if code < 0:
         _native.check(-code, "sqa_selected_kernel")
@@ -178,11 +221,11 @@ def selected_kernel(query, key_cache, value_cache, block_tables, seq_lens, page_
 
 def workspace_bytes(query, key_cache, value_cache, block_tables, seq_lens, page_size,
                     max_seq_len: int = 0, *, num_ctas: int = 0, min_pages_per_cta: int = 0,
-                    kernel: int = 0) -> int:
+                    kernel: int = 0, kv_layout: str = "NHD") -> int:
     """Bytes of workspace ``small_q_attention`` needs for these shapes."""
-    _check_inputs(query, key_cache, value_cache, block_tables, seq_lens, page_size)
+    _check_inputs(query, key_cache, value_cache, block_tables, seq_lens, page_size, kv_layout=kv_layout)
     args = _fill_args(query, key_cache, value_cache, block_tables, seq_lens, None, max_seq_len,
-                      num_ctas, min_pages_per_cta, kernel)
+                      num_ctas, min_pages_per_cta, kernel, kv_layout)
     st = ctypes.c_int(0)
     need = _native.library().sqa_workspace_bytes(ctypes.byref(args), query.device.index, ctypes.byref(st))
     _native.check(st.value, "sqa_workspace_bytes")
@@ -226,7 +269,8 @@ def _run(args, device, workspace, check):
 
 def small_q_attention(query, key_cache, value_cache, block_tables, seq_lens, page_size: int,
                       max_seq_len: int = 0, *, out=None, workspace=None, num_ctas: int = 0,
-                      min_pages_per_cta: int = 0, kernel: int = 0, check: bool = False):
+                      min_pages_per_cta: int = 0, kernel: int = 0, check: bool = False,
+                      kv_layout: str = "NHD", sm_scale: float | None = None, out_scale: float = 1.0):
     """Causal paged MTP attention; returns ``[batch, q_len, Hq, 128]`` in the input type.
 
     Q/K/V are FP16 (the upstream contract) or BF16 (all three of one type;
@@ -241,15 +285,17 @@ def small_q_attention(query, key_cache, value_cache, block_tables, seq_lens, pag
     raises the exception the upstream CPU reference would raise for bad
     metadata (``seq_lens < q_len``, page ids outside the pool).  ``kernel``
     selects the implementation: 0 auto, 1 warp-level mma.sync, 2 tcgen05 with
-    tensor memory (same operator).
+    tensor memory (same operator).  ``kv_layout`` "HND" takes caches as
+    ``[pages, Hkv, 16, 128]``; ``sm_scale`` (default ``128**-0.5``) scales q.k and
+    ``out_scale`` every output row (FlashInfer's ``bmm1_scale`` / ``bmm2_scale``).
     """
-    _check_inputs(query, key_cache, value_cache, block_tables, seq_lens, page_size)
+    _check_inputs(query, key_cache, value_cache, block_tables, seq_lens, page_size, kv_layout=kv_layout)
     if out is None:
         out = torch.empty_like(query)
     elif out.shape != query.shape or out.dtype != query.dtype or not out.is_contiguous() or out.device != query.device:
         raise ValueError("out must be a contiguous tensor shaped and typed like query")
     args = _fill_args(query, key_cache, value_cache, block_tables, seq_lens, None, max_seq_len,
-                      num_ctas, min_pages_per_cta, kernel)
+                      num_ctas, min_pages_per_cta, kernel, kv_layout, sm_scale, out_scale)
     args.out = out.data_ptr()
     _run(args, query.device, workspace, check)
     return out
@@ -258,7 +304,8 @@ def small_q_attention(query, key_cache, value_cache, block_tables, seq_lens, pag
 def small_q_attention_partial(query, key_cache, value_cache, block_tables, seq_lens, page_size: int,
                               mask_lens=None, max_seq_len: int = 0, *, out=None, out_lse=None,
                               workspace=None, num_ctas: int = 0, min_pages_per_cta: int = 0,
-                              kernel: int = 0, check: bool = False):
+                              kernel: int = 0, check: bool = False, kv_layout: str = "NHD",
+                              sm_scale: float | None = None, out_scale: float = 1.0):
     """Attention over the tokens this call holds; returns ``(O fp32, LSE fp32)``.
 
     The shard form of the operator for splitting one sequence's KV range:
@@ -268,7 +315,7 @@ def small_q_attention_partial(query, key_cache, value_cache, block_tables, seq_l
     ``LSE`` the natural-log log-sum-exp ``[B, q_len, Hq]`` (-inf for a row
     that sees no key here).  Combine shards with :func:`merge_partials`.
     """
-    _check_inputs(query, key_cache, value_cache, block_tables, seq_lens, page_size, mask_lens)
+    _check_inputs(query, key_cache, value_cache, block_tables, seq_lens, page_size, mask_lens, kv_layout)
     if out is None:
         out = torch.empty(query.shape, dtype=torch.float32, device=query.device)
     if out_lse is None:
@@ -278,7 +325,7 @@ def small_q_attention_partial(query, key_cache, value_cache, block_tables, seq_l
     if out_lse.dtype != torch.float32 or out_lse.shape != query.shape[:3] or not out_lse.is_contiguous():
         raise ValueError("out_lse must be a contiguous fp32 tensor [batch, q_len, Hq]")
     args = _fill_args(query, key_cache, value_cache, block_tables, seq_lens, mask_lens, max_seq_len,
-                      num_ctas, min_pages_per_cta, kernel)
+                      num_ctas, min_pages_per_cta, kernel, kv_layout, sm_scale, out_scale)
     args.out_partial = out.data_ptr()
     args.out_lse = out_lse.data_ptr()
     _run(args, query.device, workspace, check)

@@ -18,8 +18,8 @@ import threading
 import torch
 
 from . import _native
-from .attention import (HEAD_DIM, PAGE_SIZE, _cuda_available, _on_device, _raise_device_bits, _stream_handle,
-                        read_device_status)
+from .attention import (HEAD_DIM, PAGE_SIZE, _cache_page_stride, _cuda_available, _layout_code, _on_device,
+                        _raise_device_bits, _stream_handle, read_device_status)
 
 _status_lock = threading.Lock()
 _status_words: dict[tuple[int, int], torch.Tensor] = {}
@@ -36,9 +36,10 @@ def _status_word(device: torch.device) -> torch.Tensor:
 
 
 def cache_append(new_keys, new_values, key_cache, value_cache, block_tables, seq_lens, *,
-                 check: bool = False):
-    """Write ``new_keys`` / ``new_values`` ``[batch, q_len, Hkv, 128]`` fp16 into
-    the paged caches ``[num_pages, 16, Hkv, 128]`` in place; returns the caches.
+                 check: bool = False, kv_layout: str = "NHD"):
+    """Write ``new_keys`` / ``new_values`` ``[batch, q_len, Hkv, 128]`` into the
+    paged caches ``[num_pages, 16, Hkv, 128]`` (``kv_layout="HND"``:
+    ``[num_pages, Hkv, 16, 128]``) in place; returns the caches.
 
     Errors of the contract (dtype, device, shape, contiguity) raise ``ValueError``
     before launch.  With ``check=True`` the call synchronises and raises
@@ -52,7 +53,7 @@ def cache_append(new_keys, new_values, key_cache, value_cache, block_tables, seq
         raise ValueError("all inputs must be CUDA tensors")
     if any(t.device != key_cache.device for t in tensors):
         raise ValueError("all inputs must be on the same CUDA device")
-    if any(not t.is_contiguous() for t in tensors):
+    if any(not t.is_contiguous() for t in (new_keys, new_values, block_tables, seq_lens)):
         raise ValueError("all inputs must be contiguous")
     if new_keys.dtype not in (torch.float16, torch.bfloat16) or any(t.dtype != new_keys.dtype for t in tensors[1:4]):
         raise ValueError("new K/V and the caches must be FP16 (or BF16), all of one type")
@@ -61,13 +62,15 @@ def cache_append(new_keys, new_values, key_cache, value_cache, block_tables, seq
     if new_keys.dim() != 4 or new_values.shape != new_keys.shape:
         raise ValueError("new_keys / new_values must be [batch, q_len, Hkv, 128]")
     if key_cache.dim() != 4 or value_cache.shape != key_cache.shape:
-        raise ValueError("key_cache / value_cache must be [num_pages, 16, Hkv, 128]")
+        raise ValueError("key_cache / value_cache must be 4-D and of one shape")
+    layout = _layout_code(kv_layout)
     batch, q_len, hkv, dim = new_keys.shape
+    cache_page, cache_heads = (key_cache.shape[2], key_cache.shape[1]) if layout else key_cache.shape[1:3]
     if dim != HEAD_DIM or key_cache.shape[3] != HEAD_DIM:
         raise ValueError("the kernel supports head_dim 128")
-    if key_cache.shape[1] != PAGE_SIZE:
+    if cache_page != PAGE_SIZE:
         raise ValueError("page_size must be 16")
-    if key_cache.shape[2] != hkv:
+    if cache_heads != hkv:
         raise ValueError("new K/V and the caches disagree on the number of KV heads")
     if q_len < 1:
         raise ValueError("q_len must be at least 1")
@@ -88,6 +91,8 @@ def cache_append(new_keys, new_values, key_cache, value_cache, block_tables, seq
     a.batch, a.q_len, a.num_kv_heads = batch, q_len, hkv
     a.head_dim, a.page_size = HEAD_DIM, PAGE_SIZE
     a.num_pages, a.max_pages = int(key_cache.shape[0]), int(block_tables.shape[1])
+    a.kv_layout = layout
+    a.page_stride = _cache_page_stride(key_cache, value_cache)
     with _on_device(device):
         code = _native.library().sqa_cache_append(ctypes.byref(a), ctypes.c_void_p(_stream_handle(device)))
         _native.check(code, "sqa_cache_append")

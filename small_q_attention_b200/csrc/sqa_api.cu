@@ -5,6 +5,7 @@
 // over the paged caches and launches the kernels on the caller's stream.
 // Errors are status codes; no exception leaves this file.
 #include <cstdio>
+#include <cmath>
 #include <mutex>
 
 #include "../../include/small_q_attention.h"
@@ -13,7 +14,7 @@
 namespace sqa {
 namespace {
 
-constexpr int kAbiVersion = 104;
+constexpr int kAbiVersion = 106;
 constexpr size_t kAlign = 256;
 constexpr int kMaxDevices = 64;
 constexpr int kCtasPerSm = 2;
@@ -66,14 +67,22 @@ EncodeTiledFn encode_fn() {
 
 // [num_pages * 16 tokens, Hkv, 128] fp16 seen as a 3-D tensor; one box is
 // 64 dims x 1 head x 16 tokens (2 KB), 128-byte swizzled.
-bool encode_cache_map_uncached(CUtensorMap* map, const void* base, int num_pages, int hkv) {
+// One box = 64 dims x 16 tokens of one KV head (2 KB, 128-byte swizzle) in every
+// layout.  The map is 4-D, (dim, d1, d2, page): NHD has d1 = head (256 B apart),
+// d2 = token (Hkv * 256 B apart); HND has d1 = token (256 B apart), d2 = head
+// (4 KB apart); pages are `page_stride` bytes apart (16 * Hkv * 256 when the
+// cache is one contiguous tensor).
+bool encode_cache_map_uncached(CUtensorMap* map, const void* base, int num_pages, int hkv, bool hnd,
+                               uint64_t page_stride) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
-  const cuuint64_t dims[3] = {(cuuint64_t)kHeadDim, (cuuint64_t)hkv, (cuuint64_t)num_pages * kPageSize};
-  const cuuint64_t strides[2] = {(cuuint64_t)kHeadDim * 2, (cuuint64_t)hkv * kHeadDim * 2};
-  const cuuint32_t box[3] = {64, 1, (cuuint32_t)kPageSize};
-  const cuuint32_t estr[3] = {1, 1, 1};
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+  const cuuint64_t row = (cuuint64_t)kHeadDim * 2;
+  const cuuint64_t dims[4] = {(cuuint64_t)kHeadDim, hnd ? (cuuint64_t)kPageSize : (cuuint64_t)hkv,
+                              hnd ? (cuuint64_t)hkv : (cuuint64_t)kPageSize, (cuuint64_t)num_pages};
+  const cuuint64_t strides[3] = {row, hnd ? row * kPageSize : row * hkv, (cuuint64_t)page_stride};
+  const cuuint32_t box[4] = {64, hnd ? (cuuint32_t)kPageSize : 1u, hnd ? 1u : (cuuint32_t)kPageSize, 1u};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -81,28 +90,36 @@ bool encode_cache_map_uncached(CUtensorMap* map, const void* base, int num_pages
 // A serving loop passes the same caches on every call: keep the last few
 // encoded maps per host thread (a map depends only on base, pages and heads;
 // the element type does not matter to a copy of 2-byte elements).
-bool encode_cache_map(CUtensorMap* map, const void* base, int num_pages, int hkv) {
+bool encode_cache_map(CUtensorMap* map, const void* base, int num_pages, int hkv, bool hnd, uint64_t page_stride) {
   struct Entry {
     const void* base;
     int num_pages, hkv;
+    bool hnd;
+    uint64_t page_stride;
     CUtensorMap map;
   };
   constexpr int kEntries = 8;
   thread_local Entry cache[kEntries] = {};
   thread_local int next = 0;
   for (int i = 0; i < kEntries; ++i) {
-    if (cache[i].base == base && cache[i].num_pages == num_pages && cache[i].hkv == hkv && base != nullptr) {
+    if (cache[i].base == base && cache[i].num_pages == num_pages && cache[i].hkv == hkv && cache[i].hnd == hnd &&
+        cache[i].page_stride == page_stride && base != nullptr) {
       *map = cache[i].map;
       return true;
     }
   }
-  if (!encode_cache_map_uncached(map, base, num_pages, hkv)) return false;
-  cache[next] = Entry{base, num_pages, hkv, *map};
+  if (!encode_cache_map_uncached(map, base, num_pages, hkv, hnd, page_stride)) return false;
+  cache[next] = Entry{base, num_pages, hkv, hnd, page_stride, *map};
   next = (next + 1) % kEntries;
   return true;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Elements between consecutive pages (0 = contiguous cache) -> bytes.
+uint64_t page_stride_bytes(int64_t page_stride, int hkv) {
+  return (uint64_t)(page_stride > 0 ? page_stride : (int64_t)kPageSize * hkv * kHeadDim) * 2;
+}
 
 // Debug builds synchronise after each launch (outside stream capture) and
 // report which kernel failed, so a device fault is tied to one launch.
@@ -144,6 +161,13 @@ int validate(const sqa_args* a) {
   if (a->max_seq_len < 0 || a->num_ctas < 0 || a->min_pages_per_cta < 0) return SQA_ERR_INVALID_ARGUMENT;
   if (a->kernel < 0 || a->kernel > 2) return SQA_ERR_INVALID_ARGUMENT;
   if (a->dtype != SQA_DTYPE_F16 && a->dtype != SQA_DTYPE_BF16) return SQA_ERR_UNSUPPORTED;
+  if (a->kv_layout != SQA_KV_NHD && a->kv_layout != SQA_KV_HND) return SQA_ERR_UNSUPPORTED;
+  // a page must hold 16 x Hkv x 128 elements and start 16-byte aligned (TMA strides)
+  if (a->page_stride < 0 || (a->page_stride > 0 && (a->page_stride < (int64_t)kPageSize * a->num_kv_heads * kHeadDim ||
+                                                    a->page_stride % 8 != 0)))
+    return SQA_ERR_INVALID_ARGUMENT;
+  if (!(a->sm_scale >= 0.f) || !std::isfinite(a->sm_scale) || !std::isfinite(a->out_scale))
+    return SQA_ERR_INVALID_ARGUMENT;
   // unit indices are 32-bit on the device
   if ((long long)a->batch * a->num_kv_heads * a->max_pages >= (1ll << 31)) return SQA_ERR_UNSUPPORTED;
   if ((long long)a->num_pages * kPageSize >= (1ll << 31)) return SQA_ERR_UNSUPPORTED;
@@ -297,8 +321,10 @@ int forward_impl(const sqa_args* a, void* workspace, size_t workspace_bytes, voi
   if (workspace_bytes < pl.bytes) return SQA_ERR_WORKSPACE_TOO_SMALL;
 
   CUtensorMap tm_k, tm_v;
-  if (!encode_cache_map(&tm_k, a->key_cache, a->num_pages, a->num_kv_heads) ||
-      !encode_cache_map(&tm_v, a->value_cache, a->num_pages, a->num_kv_heads))
+  const bool hnd = a->kv_layout == SQA_KV_HND;
+  const uint64_t page_stride = page_stride_bytes(a->page_stride, a->num_kv_heads);
+  if (!encode_cache_map(&tm_k, a->key_cache, a->num_pages, a->num_kv_heads, hnd, page_stride) ||
+      !encode_cache_map(&tm_v, a->value_cache, a->num_pages, a->num_kv_heads, hnd, page_stride))
     return SQA_ERR_CUDA;
 
   uint8_t* ws = static_cast<uint8_t*>(workspace);
@@ -324,8 +350,10 @@ int forward_impl(const sqa_args* a, void* workspace, size_t workspace_bytes, voi
   p.num_pieces = pl.pieces;
   p.rows_pad = pl.shape.rows_pad;
   p.timeline = pl.off_timeline ? reinterpret_cast<unsigned long long*>(ws + pl.off_timeline) : nullptr;
-  p.scale_log2 = 1.4426950408889634f / sqrtf((float)kHeadDim);
+  p.scale_log2 = 1.4426950408889634f * (a->sm_scale > 0.f ? a->sm_scale : 1.f / sqrtf((float)kHeadDim));
   p.bf16 = a->dtype == SQA_DTYPE_BF16;
+  p.hnd = hnd;
+  p.out_scale = a->out_scale != 0.f ? a->out_scale : 1.f;
 
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_ptr);
   if (ev_before && cudaEventRecord(reinterpret_cast<cudaEvent_t>(ev_before), stream) != cudaSuccess)

@@ -31,6 +31,8 @@ struct AppendParams {
   unsigned int* status;     // may be null
   long long items;          // batch * q_len * hkv * 16
   int q_len, hkv, num_pages, max_pages;
+  int hnd;                  // caches are [P, Hkv, 16, 128] (else [P, 16, Hkv, 128])
+  long long page_stride16;  // 16-byte units from one page to the next
 };
 
 __global__ void __launch_bounds__(256) sqa_cache_append_kernel(const AppendParams p) {
@@ -61,7 +63,9 @@ __global__ void __launch_bounds__(256) sqa_cache_append_kernel(const AppendParam
       bad |= err;
       continue;
     }
-    const size_t dst = (((size_t)page * kPageSize + (t % kPageSize)) * p.hkv + h) * 16 + c;
+    const size_t in_page = p.hnd ? ((size_t)h * kPageSize + (t % kPageSize)) * 16 + c
+                                 : ((size_t)(t % kPageSize) * p.hkv + h) * 16 + c;
+    const size_t dst = (size_t)page * p.page_stride16 + in_page;
     p.k_cache[dst] = __ldg(p.new_k + i);
     p.v_cache[dst] = __ldg(p.new_v + i);
   }
@@ -77,6 +81,10 @@ extern "C" SQA_API int sqa_cache_append(const sqa_append_args* a, void* stream) 
   if (a == nullptr) return SQA_ERR_INVALID_ARGUMENT;
   if (a->head_dim != kHeadDim || a->page_size != kPageSize) return SQA_ERR_UNSUPPORTED;
   if (a->batch < 0 || a->q_len <= 0 || a->num_kv_heads <= 0 || a->num_pages <= 0 || a->max_pages <= 0)
+    return SQA_ERR_INVALID_ARGUMENT;
+  if (a->kv_layout != SQA_KV_NHD && a->kv_layout != SQA_KV_HND) return SQA_ERR_UNSUPPORTED;
+  if (a->page_stride < 0 || (a->page_stride > 0 && (a->page_stride < (int64_t)kPageSize * a->num_kv_heads * kHeadDim ||
+                                                    a->page_stride % 8 != 0)))
     return SQA_ERR_INVALID_ARGUMENT;
   if (a->batch == 0) return SQA_OK;
   if (!a->new_keys || !a->new_values || !a->key_cache || !a->value_cache || !a->block_tables || !a->seq_lens)
@@ -100,6 +108,8 @@ extern "C" SQA_API int sqa_cache_append(const sqa_append_args* a, void* stream) 
   p.hkv = a->num_kv_heads;
   p.num_pages = a->num_pages;
   p.max_pages = a->max_pages;
+  p.hnd = a->kv_layout == SQA_KV_HND;
+  p.page_stride16 = (a->page_stride > 0 ? a->page_stride : (int64_t)kPageSize * a->num_kv_heads * kHeadDim) / 8;
 
   int dev = 0, sms = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) !=

@@ -54,6 +54,8 @@ struct SplitKvParams {
   unsigned long long* timeline; // -DSQA_DEBUG_TIMELINE: 8 stamps per CTA, else nullptr
   float scale_log2;             // head_dim^-0.5 * log2(e)
   int bf16;                     // q / caches / out hold bf16 (else fp16) bits
+  int hnd;                      // caches are [P, Hkv, 16, 128] (else [P, 16, Hkv, 128])
+  float out_scale;              // multiplies every output row (1 = plain attention)
 };
 
 struct MergeParams {

@@ -104,11 +104,13 @@ __device__ void producer_loop(const SplitKvParams& p, const Schedule& sch, const
             const uint32_t f = smem_u32(full + fslot);
             mbar_arrive_expect_tx(f, kStageBytes);
             const uint32_t dst = smem_u32(stages + (size_t)slot * kStageBytes);
-            const int tok = page * kPageSize;
-            tma_load_3d(dst, tm_k, f, 0, w.h, tok, policy);
-            tma_load_3d(dst + 2048, tm_k, f, 64, w.h, tok, policy);
-            tma_load_3d(dst + 4096, tm_v, f, 0, w.h, tok, policy);
-            tma_load_3d(dst + 6144, tm_v, f, 64, w.h, tok, policy);
+            // NHD map: (dim, head, token, page); HND map: (dim, token, head, page)
+            const int c1 = p.hnd ? 0 : w.h;
+            const int c2 = p.hnd ? w.h : 0;
+            tma_load_4d(dst, tm_k, f, 0, c1, c2, page, policy);
+            tma_load_4d(dst + 2048, tm_k, f, 64, c1, c2, page, policy);
+            tma_load_4d(dst + 4096, tm_v, f, 0, c1, c2, page, policy);
+            tma_load_4d(dst + 6144, tm_v, f, 64, c1, c2, page, policy);
             ++issued;
           }
         }
@@ -382,7 +384,7 @@ __device__ void consumer_loop(const SplitKvParams& p, const Schedule& sch, uint8
         acc.z += wgt * v.z;
         acc.w += wgt * v.w;
       }
-      const float inv = (L > 0.f) ? 1.f / L : 0.f;
+      const float inv = (L > 0.f) ? p.out_scale / L : 0.f;
       acc.x *= inv;
       acc.y *= inv;
       acc.z *= inv;

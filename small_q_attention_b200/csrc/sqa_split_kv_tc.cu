@@ -133,12 +133,14 @@ __device__ void tc_producer(const SplitKvParams& p, const Schedule& sch, const C
             mbar_arrive_expect_tx(f, np * kStageBytes);
             const uint32_t base = smem_u32(sm.ring + (size_t)slot * kBlockBytes);
             for (int j = 0; j < np; ++j) {
-              const int tok = pages[j] * kPageSize;
+              // NHD map: (dim, head, token, page); HND map: (dim, token, head, page)
+              const int c1 = p.hnd ? 0 : w.h;
+              const int c2 = p.hnd ? w.h : 0;
               const uint32_t dst = base + j * 2048;
-              tma_load_3d(dst, tm_k, f, 0, w.h, tok, policy);
-              tma_load_3d(dst + kRegionBytes, tm_k, f, 64, w.h, tok, policy);
-              tma_load_3d(dst + 2 * kRegionBytes, tm_v, f, 0, w.h, tok, policy);
-              tma_load_3d(dst + 3 * kRegionBytes, tm_v, f, 64, w.h, tok, policy);
+              tma_load_4d(dst, tm_k, f, 0, c1, c2, pages[j], policy);
+              tma_load_4d(dst + kRegionBytes, tm_k, f, 64, c1, c2, pages[j], policy);
+              tma_load_4d(dst + 2 * kRegionBytes, tm_v, f, 0, c1, c2, pages[j], policy);
+              tma_load_4d(dst + 3 * kRegionBytes, tm_v, f, 64, c1, c2, pages[j], policy);
             }
           }
           __syncwarp();
@@ -457,7 +459,8 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
       const float2 v = sm.ml[r * kLanesPR + lrow];
       if (v.y > 0.f) L += v.y * ex2(v.x - mx);
     }
-    const float f = (l > 0.f) ? ex2(m_used - mx) / L : 0.f;  // this replica's weight (L > 0 when l > 0)
+    // this replica's weight (L > 0 when l > 0), with the output scale folded in
+    const float f = (l > 0.f) ? ex2(m_used - mx) * p.out_scale / L : 0.f;
     const float lse = (L > 0.f) ? (mx + __log2f(L)) * kLn2 : -INFINITY;
     // Two chunks of 64 dims: every warp stores its rows' weighted chunk (a
     // uniform branch: tcgen05.ld needs the whole warp), then the 128 threads sum

@@ -21,8 +21,8 @@ import ctypes
 import torch
 
 from . import _native
-from .attention import (GQA_GROUP, HEAD_DIM, MAX_Q_LEN, PAGE_SIZE, _check_inputs, _fill_args, _on_device,
-                        _raise_device_bits, _stream_handle, read_device_status)
+from .attention import (GQA_GROUP, HEAD_DIM, MAX_Q_LEN, PAGE_SIZE, _check_inputs, _fill_args, _layout_code,
+                        _on_device, _raise_device_bits, _stream_handle, read_device_status)
 from .cache import cache_append
 
 
@@ -53,7 +53,8 @@ class PagedMTPAttention:
     # ------------------------------------------------------------------ plan
     def plan(self, batch: int, q_len: int, num_kv_heads: int, num_pages: int, max_pages: int,
              max_seq_len: int = 0, *, page_size: int = PAGE_SIZE, head_dim: int = HEAD_DIM,
-             num_ctas: int = 0, min_pages_per_cta: int = 0) -> "PagedMTPAttention":
+             num_ctas: int = 0, min_pages_per_cta: int = 0, kv_layout: str = "NHD",
+             sm_scale: float | None = None, out_scale: float = 1.0) -> "PagedMTPAttention":
         """Fix the shapes of the following ``run`` calls and size the workspace.
 
         ``max_seq_len`` bounds ``seq_lens`` for the launch size (0: the page-table
@@ -70,6 +71,7 @@ class PagedMTPAttention:
         a.batch, a.q_len, a.num_q_heads, a.head_dim = batch, q_len, GQA_GROUP * num_kv_heads, head_dim
         a.num_kv_heads, a.page_size, a.num_pages, a.max_pages = num_kv_heads, page_size, num_pages, max_pages
         a.max_seq_len, a.num_ctas, a.min_pages_per_cta, a.kernel = max_seq_len, num_ctas, min_pages_per_cta, self._kernel
+        a.kv_layout = _layout_code(kv_layout)
         lib = _native.library()
         st = ctypes.c_int(0)
         need = int(lib.sqa_workspace_bytes(ctypes.byref(a), self.device.index, ctypes.byref(st)))
@@ -81,6 +83,7 @@ class PagedMTPAttention:
             self._workspace = torch.zeros(max(need, 1 << 16), dtype=torch.uint8, device=self.device)
         self._shape = (batch, q_len, num_kv_heads, num_pages, max_pages)
         self._max_seq_len, self._num_ctas, self._min_pages = max_seq_len, num_ctas, min_pages_per_cta
+        self._kv_layout, self._sm_scale, self._out_scale = kv_layout, sm_scale, out_scale
         self.selected_kernel = int(picked)
         return self
 
@@ -98,8 +101,9 @@ class PagedMTPAttention:
         it when capturing a CUDA graph)."""
         if self._shape is None:
             raise RuntimeError("plan() has not been called")
-        _check_inputs(query, key_cache, value_cache, block_tables, seq_lens, PAGE_SIZE)
-        shape = (int(query.shape[0]), int(query.shape[1]), int(key_cache.shape[2]), int(key_cache.shape[0]),
+        _check_inputs(query, key_cache, value_cache, block_tables, seq_lens, PAGE_SIZE, kv_layout=self._kv_layout)
+        hkv = key_cache.shape[1] if self._kv_layout == "HND" else key_cache.shape[2]
+        shape = (int(query.shape[0]), int(query.shape[1]), int(hkv), int(key_cache.shape[0]),
                  int(block_tables.shape[1]))
         if shape != self._shape:
             raise ValueError(f"run() shapes {shape} differ from the planned {self._shape} "
@@ -113,9 +117,11 @@ class PagedMTPAttention:
         if (append_keys is None) != (append_values is None):
             raise ValueError("append_keys and append_values go together")
         if append_keys is not None:
-            cache_append(append_keys, append_values, key_cache, value_cache, block_tables, seq_lens)
+            cache_append(append_keys, append_values, key_cache, value_cache, block_tables, seq_lens,
+                         kv_layout=self._kv_layout)
         a = _fill_args(query, key_cache, value_cache, block_tables, seq_lens, None, self._max_seq_len,
-                       self._num_ctas, self._min_pages, self._kernel)
+                       self._num_ctas, self._min_pages, self._kernel, self._kv_layout, self._sm_scale,
+                       self._out_scale)
         a.out = out.data_ptr()
         ws = self._workspace
         with _on_device(self.device):

@@ -42,7 +42,7 @@ def test_every_declared_symbol_is_exported(lib):
 
 
 def test_abi_version_and_status_strings(lib):
-    assert lib.sqa_abi_version() == 104
+    assert lib.sqa_abi_version() == 106
     for code in range(6):
         assert lib.sqa_status_string(code).decode()
     assert lib.sqa_status_string(99).decode() == "unknown status"
@@ -114,3 +114,33 @@ def test_operator_requires_cuda_without_fallback():
     with pytest.raises(RuntimeError):
         small_q_attention(q, cache, cache, torch.zeros(1, 4, dtype=torch.int32),
                           torch.tensor([32], dtype=torch.int32), 16)
+
+
+def test_struct_layouts_match_the_header(tmp_path):
+    """The ctypes mirrors have the C structs' size and every field offset."""
+    import ctypes
+    import shutil
+    import subprocess
+
+    from small_q_attention_b200._native import SqaAppendArgs, SqaArgs
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    include = Path(__file__).resolve().parents[1] / "include"
+    lines = ["#include <stddef.h>", "#include <stdio.h>", '#include "small_q_attention.h"', "int main(void) {"]
+    for cls, cname in ((SqaArgs, "sqa_args"), (SqaAppendArgs, "sqa_append_args")):
+        lines.append(f'  printf("{cname} size %zu\\n", sizeof({cname}));')
+        for name, _ in cls._fields_:
+            lines.append(f'  printf("{cname} {name} %zu\\n", offsetof({cname}, {name}));')
+    lines.append("  return 0; }")
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    subprocess.run([cc, "-I", str(include), str(src), "-o", str(exe)], check=True)
+    got = dict(((a, b), int(c)) for a, b, c in (ln.split() for ln in subprocess.run(
+        [str(exe)], check=True, capture_output=True, text=True).stdout.splitlines()))
+    for cls, cname in ((SqaArgs, "sqa_args"), (SqaAppendArgs, "sqa_append_args")):
+        assert got[(cname, "size")] == ctypes.sizeof(cls)
+        for name, _ in cls._fields_:
+            assert got[(cname, name)] == getattr(cls, name).offset, (cname, name)
