@@ -68,6 +68,9 @@ def _as_dtype(c, name):
         return c
     import torch
 
+    if name == "fp8":  # fp16 queries, fp8 e4m3 caches
+        f8 = torch.float8_e4m3fn
+        return dict(c, key_cache=c["key_cache"].to(f8), value_cache=c["value_cache"].to(f8))
     t = {"bf16": torch.bfloat16}[name]
     return dict(c, query=c["query"].to(t), key_cache=c["key_cache"].to(t), value_cache=c["value_cache"].to(t))
 
@@ -182,7 +185,8 @@ def _case_bytes(c):
     from small_q_attention_b200.workloads import algorithmic_bytes
 
     q = c["query"]
-    return algorithmic_bytes(q.shape[0], q.shape[1], c["lens"], q.shape[2], c["num_kv_heads"])
+    return algorithmic_bytes(q.shape[0], q.shape[1], c["lens"], q.shape[2], c["num_kv_heads"],
+                             c["key_cache"].element_size())
 
 
 def _cpu_cores():
@@ -601,22 +605,21 @@ def run_matrix(args):
             first = _as_dtype(make_config(name, seed=0), args.dtype)
             label = name
         else:
-            first = make_case(c["batch"], c["q_len"], [c["kv_len"]] * c["batch"], pool_factor=1.0,
-                              dtype=DTYPES[args.dtype], page_mode=args.page_mode, seed=0)
+            first = _as_dtype(make_case(c["batch"], c["q_len"], [c["kv_len"]] * c["batch"], pool_factor=1.0,
+                                        page_mode=args.page_mode, seed=0), args.dtype)
             label = f"q{c['q_len']}_kv{c['kv_len']}_b{c['batch']}"
         nb = _case_bytes(first)
         # distinct input copies so that consecutive calls never find K/V in L2:
         # at least 2 and enough for >= 400 MB of caches in rotation (at most 64)
-        cache_bytes = first["key_cache"].numel() * 4
+        cache_bytes = first["key_cache"].numel() * first["key_cache"].element_size() * 2
         n_rep = max(2, min(64, math.ceil(400e6 / max(1, cache_bytes))))
         inst = [first]
         for s_ in range(1, n_rep):
             if c is None:
                 inst.append(_as_dtype(make_config(name, seed=s_), args.dtype))
             else:
-                inst.append(make_case(c["batch"], c["q_len"], [c["kv_len"]] * c["batch"], pool_factor=1.0,
-                                      dtype=DTYPES[args.dtype],
-                                      page_mode=args.page_mode, seed=s_))
+                inst.append(_as_dtype(make_case(c["batch"], c["q_len"], [c["kv_len"]] * c["batch"], pool_factor=1.0,
+                                                page_mode=args.page_mode, seed=s_), args.dtype))
         outs = [torch.empty_like(x["query"]) for x in inst]
         fn = lambda i: sqa.small_q_attention(  # noqa: E731
             inst[i]["query"], inst[i]["key_cache"], inst[i]["value_cache"], inst[i]["block_tables"],
@@ -685,8 +688,8 @@ def main():
     ap.add_argument("--matrix-only", action="store_true", help="run only the matrix sweep")
     ap.add_argument("--only", nargs="*", default=None)
     ap.add_argument("--page-mode", default="random", choices=("random", "unique", "shared"))
-    ap.add_argument("--dtype", default="f16", choices=("f16", "bf16"),
-                    help="matrix: element type of Q/K/V (the driver line is always f16)")
+    ap.add_argument("--dtype", default="f16", choices=("f16", "bf16", "fp8"),
+                    help="matrix: element type of Q/K/V (fp8: fp16 Q, fp8 e4m3 K/V; the driver line is always f16)")
     ap.add_argument("--settle", type=float, default=1.0,
                     help="matrix: seconds of idle before timing each case (clock recovery)")
     ap.add_argument("--kernel", type=int, default=0, choices=(0, 1, 2),

@@ -129,12 +129,19 @@ typedef struct sqa_args {
    * address one layer of a bigger pool or K and V interleaved per page
    * ([num_pages, 2, ...]); a multiple of 8 (16-byte aligned pages). */
   int64_t page_stride;
+  /* Element type of key_cache / value_cache: SQA_KV_SAME (as dtype) or
+   * SQA_KV_FP8_E4M3 (1 byte, with fp16 queries and output; tcgen05 kernel).
+   * fp8 values enter the products exactly (e4m3 -> fp16 is exact); fold the
+   * caches' dequantisation scales into sm_scale (K) and out_scale (V). */
+  int32_t kv_dtype;
 } sqa_args;
 
 #define SQA_DTYPE_F16 0
 #define SQA_DTYPE_BF16 1
 #define SQA_KV_NHD 0
 #define SQA_KV_HND 1
+#define SQA_KV_SAME 0
+#define SQA_KV_FP8_E4M3 1
 
 /* Workspace bytes sqa_forward needs for these arguments on `device`
  * (-1 = the current device).  Depends only on shapes and tuning fields.
@@ -219,7 +226,8 @@ SQA_API int sqa_forward_noalloc(const sqa_args* args, void* stream);
  *   new_keys, new_values  fp16 [batch, q_len, num_kv_heads, 128], 16-byte aligned
  *   key_cache, value_cache [num_pages, 16, num_kv_heads, 128] (NHD) or
  *                          [num_pages, num_kv_heads, 16, 128] (HND), 16-byte aligned.
- *   Any 2-byte element type (fp16 or bf16: the append is a copy). */
+ *   Any 2-byte element type (fp16 or bf16: the append is a copy), or fp8 e4m3
+ *   with kv_dtype = SQA_KV_FP8_E4M3 (new K/V already in fp8). */
 typedef struct sqa_append_args {
   const void* new_keys;
   const void* new_values;
@@ -237,6 +245,7 @@ typedef struct sqa_append_args {
   int32_t max_pages;
   int32_t kv_layout;           /* SQA_KV_NHD or SQA_KV_HND, as in sqa_args */
   int64_t page_stride;         /* elements from page to page, 0 = contiguous (as in sqa_args) */
+  int32_t kv_dtype;            /* SQA_KV_SAME (2-byte elements) or SQA_KV_FP8_E4M3 (1-byte) */
 } sqa_append_args;
 
 SQA_API int sqa_cache_append(const sqa_append_args* args, void* stream);

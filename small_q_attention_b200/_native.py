@@ -31,6 +31,10 @@ DTYPE_BF16 = 1
 KV_NHD = 0
 KV_HND = 1
 
+# cache element types (SQA_KV_SAME / SQA_KV_FP8_E4M3)
+KV_SAME = 0
+KV_FP8_E4M3 = 1
+
 # device status bits (SQA_DEV_*)
 DEV_TIMEOUT = 1
 DEV_SEQ_TOO_LONG = 2
@@ -73,6 +77,7 @@ class SqaAppendArgs(ctypes.Structure):
         ("max_pages", ctypes.c_int32),
         ("kv_layout", ctypes.c_int32),
         ("page_stride", ctypes.c_int64),
+        ("kv_dtype", ctypes.c_int32),
     ]
 
 
@@ -106,6 +111,7 @@ class SqaArgs(ctypes.Structure):
         ("sm_scale", ctypes.c_float),
         ("out_scale", ctypes.c_float),
         ("page_stride", ctypes.c_int64),
+        ("kv_dtype", ctypes.c_int32),
     ]
 
 

@@ -27,6 +27,7 @@ GQA_GROUP = 4
 MAX_Q_LEN = 16
 
 _DTYPES = (torch.float16, torch.bfloat16)
+_FP8 = getattr(torch, "float8_e4m3fn", None)
 _ws_lock = threading.Lock()
 _workspaces: dict[tuple[int, int], torch.Tensor] = {}
 
@@ -96,9 +97,10 @@ def _cache_page_stride(key_cache, value_cache) -> int:
     st = key_cache.stride()
     inner = key_cache.shape[1] * key_cache.shape[2] * key_cache.shape[3]
     packed = (key_cache.shape[2] * key_cache.shape[3], key_cache.shape[3], 1)
-    if value_cache.stride() != st or tuple(st[1:]) != packed or st[0] < inner or st[0] % 8:
+    align = 16 // key_cache.element_size()  # 16-byte aligned pages
+    if value_cache.stride() != st or tuple(st[1:]) != packed or st[0] < inner or st[0] % align:
         raise ValueError("key_cache / value_cache must be packed within a page, with one page stride "
-                         "(a multiple of 8 elements) shared by K and V")
+                         "(16-byte aligned) shared by K and V")
     return int(st[0])
 
 
@@ -119,8 +121,9 @@ def _check_inputs(query, key_cache, value_cache, block_tables, seq_lens, page_si
             raise ValueError("all inputs must be contiguous")
     _cache_page_stride(key_cache, value_cache)
     qd = query.dtype
-    if qd not in _DTYPES or key_cache.dtype != qd or value_cache.dtype != qd:
-        raise ValueError("the kernel requires FP16 (or BF16) Q/K/V, all of one type")
+    kd = key_cache.dtype
+    if qd not in _DTYPES or value_cache.dtype != kd or not (kd == qd or (kd == _FP8 and qd == torch.float16)):
+        raise ValueError("the kernel requires FP16 (or BF16) Q/K/V of one type, or FP16 Q with FP8-E4M3 K/V")
     for t in tensors[3:]:
         if t.dtype != torch.int32:
             raise ValueError("block_tables, seq_lens and mask_lens must be int32")
@@ -166,7 +169,8 @@ def _fill_args(query, key_cache, value_cache, block_tables, seq_lens, mask_lens,
         int(num_ctas), int(min_pages_per_cta), int(kernel),
         _native.DTYPE_BF16 if query.dtype == torch.bfloat16 else _native.DTYPE_F16, layout,
         0.0 if sm_scale is None else float(sm_scale), float(out_scale),
-        _cache_page_stride(key_cache, value_cache))
+        _cache_page_stride(key_cache, value_cache),
+        _native.KV_FP8_E4M3 if key_cache.dtype == _FP8 else _native.KV_SAME)
 
 
 _need_cache: dict[tuple, int] = {}
@@ -274,7 +278,9 @@ def small_q_attention(query, key_cache, value_cache, block_tables, seq_lens, pag
     """Causal paged MTP attention; returns ``[batch, q_len, Hq, 128]`` in the input type.
 
     Q/K/V are FP16 (the upstream contract) or BF16 (all three of one type;
-    accumulation is FP32 either way).
+    accumulation is FP32 either way), or FP16 Q with FP8-E4M3 K/V (tcgen05
+    kernel; the fp8 values enter exactly: pass the caches' dequantisation scales
+    as ``sm_scale = k_scale / sqrt(128)`` and ``out_scale = v_scale``).
 
     ``seq_lens[b]`` is the KV length including the ``q_len`` draft tokens and
     draft row ``qi`` sees tokens ``< seq_lens[b] - q_len + qi + 1``

@@ -55,8 +55,10 @@ def cache_append(new_keys, new_values, key_cache, value_cache, block_tables, seq
         raise ValueError("all inputs must be on the same CUDA device")
     if any(not t.is_contiguous() for t in (new_keys, new_values, block_tables, seq_lens)):
         raise ValueError("all inputs must be contiguous")
-    if new_keys.dtype not in (torch.float16, torch.bfloat16) or any(t.dtype != new_keys.dtype for t in tensors[1:4]):
-        raise ValueError("new K/V and the caches must be FP16 (or BF16), all of one type")
+    fp8 = getattr(torch, "float8_e4m3fn", None)
+    if new_keys.dtype not in (torch.float16, torch.bfloat16, fp8) or any(t.dtype != new_keys.dtype
+                                                                          for t in tensors[1:4]):
+        raise ValueError("new K/V and the caches must be FP16, BF16 or FP8-E4M3, all of one type")
     if block_tables.dtype != torch.int32 or seq_lens.dtype != torch.int32:
         raise ValueError("block_tables and seq_lens must be int32")
     if new_keys.dim() != 4 or new_values.shape != new_keys.shape:
@@ -93,6 +95,7 @@ def cache_append(new_keys, new_values, key_cache, value_cache, block_tables, seq
     a.num_pages, a.max_pages = int(key_cache.shape[0]), int(block_tables.shape[1])
     a.kv_layout = layout
     a.page_stride = _cache_page_stride(key_cache, value_cache)
+    a.kv_dtype = _native.KV_FP8_E4M3 if key_cache.element_size() == 1 else _native.KV_SAME
     with _on_device(device):
         code = _native.library().sqa_cache_append(ctypes.byref(a), ctypes.c_void_p(_stream_handle(device)))
         _native.check(code, "sqa_cache_append")

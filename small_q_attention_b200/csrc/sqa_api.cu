@@ -14,7 +14,7 @@
 namespace sqa {
 namespace {
 
-constexpr int kAbiVersion = 106;
+constexpr int kAbiVersion = 107;
 constexpr size_t kAlign = 256;
 constexpr int kMaxDevices = 64;
 constexpr int kCtasPerSm = 2;
@@ -30,6 +30,12 @@ constexpr int kMaxSmemPerCta = 227 * 1024;  // dynamic shared memory limit of on
 constexpr long long kAutoTcUnitsQ2 = 131072;
 constexpr long long kAutoTcUnitsQ4 = 2048;
 constexpr long long kAutoTcUnitsQ8 = 512;
+// fp8 caches: fp16 operand blocks between the converters and the MMAs (the rest
+// of shared memory stages fp8 blocks).
+#ifndef SQA_FP8_OPERAND_BLOCKS
+#define SQA_FP8_OPERAND_BLOCKS 2
+#endif
+constexpr int kFp8OperandBlocks = SQA_FP8_OPERAND_BLOCKS;
 constexpr int kDefaultMinPagesPerCta = 4;
 
 size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
@@ -72,29 +78,33 @@ EncodeTiledFn encode_fn() {
 // d2 = token (Hkv * 256 B apart); HND has d1 = token (256 B apart), d2 = head
 // (4 KB apart); pages are `page_stride` bytes apart (16 * Hkv * 256 when the
 // cache is one contiguous tensor).
+// fp8 caches: the same map with 1-byte elements and a 128-dim (128-byte) box,
+// no swizzle (the converters read plain rows).
 bool encode_cache_map_uncached(CUtensorMap* map, const void* base, int num_pages, int hkv, bool hnd,
-                               uint64_t page_stride) {
+                               uint64_t page_stride, bool fp8) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
-  const cuuint64_t row = (cuuint64_t)kHeadDim * 2;
+  const cuuint64_t row = (cuuint64_t)kHeadDim * (fp8 ? 1 : 2);
   const cuuint64_t dims[4] = {(cuuint64_t)kHeadDim, hnd ? (cuuint64_t)kPageSize : (cuuint64_t)hkv,
                               hnd ? (cuuint64_t)hkv : (cuuint64_t)kPageSize, (cuuint64_t)num_pages};
   const cuuint64_t strides[3] = {row, hnd ? row * kPageSize : row * hkv, (cuuint64_t)page_stride};
-  const cuuint32_t box[4] = {64, hnd ? (cuuint32_t)kPageSize : 1u, hnd ? 1u : (cuuint32_t)kPageSize, 1u};
+  const cuuint32_t box[4] = {fp8 ? 128u : 64u, hnd ? (cuuint32_t)kPageSize : 1u, hnd ? 1u : (cuuint32_t)kPageSize, 1u};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+  return fn(map, fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base),
+            dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            fp8 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // A serving loop passes the same caches on every call: keep the last few
 // encoded maps per host thread (a map depends only on base, pages and heads;
 // the element type does not matter to a copy of 2-byte elements).
-bool encode_cache_map(CUtensorMap* map, const void* base, int num_pages, int hkv, bool hnd, uint64_t page_stride) {
+bool encode_cache_map(CUtensorMap* map, const void* base, int num_pages, int hkv, bool hnd, uint64_t page_stride,
+                      bool fp8) {
   struct Entry {
     const void* base;
     int num_pages, hkv;
-    bool hnd;
+    bool hnd, fp8;
     uint64_t page_stride;
     CUtensorMap map;
   };
@@ -103,13 +113,13 @@ bool encode_cache_map(CUtensorMap* map, const void* base, int num_pages, int hkv
   thread_local int next = 0;
   for (int i = 0; i < kEntries; ++i) {
     if (cache[i].base == base && cache[i].num_pages == num_pages && cache[i].hkv == hkv && cache[i].hnd == hnd &&
-        cache[i].page_stride == page_stride && base != nullptr) {
+        cache[i].fp8 == fp8 && cache[i].page_stride == page_stride && base != nullptr) {
       *map = cache[i].map;
       return true;
     }
   }
-  if (!encode_cache_map_uncached(map, base, num_pages, hkv, hnd, page_stride)) return false;
-  cache[next] = Entry{base, num_pages, hkv, hnd, page_stride, *map};
+  if (!encode_cache_map_uncached(map, base, num_pages, hkv, hnd, page_stride, fp8)) return false;
+  cache[next] = Entry{base, num_pages, hkv, hnd, fp8, page_stride, *map};
   next = (next + 1) % kEntries;
   return true;
 }
@@ -117,8 +127,8 @@ bool encode_cache_map(CUtensorMap* map, const void* base, int num_pages, int hkv
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // Elements between consecutive pages (0 = contiguous cache) -> bytes.
-uint64_t page_stride_bytes(int64_t page_stride, int hkv) {
-  return (uint64_t)(page_stride > 0 ? page_stride : (int64_t)kPageSize * hkv * kHeadDim) * 2;
+uint64_t page_stride_bytes(int64_t page_stride, int hkv, int elem_bytes) {
+  return (uint64_t)(page_stride > 0 ? page_stride : (int64_t)kPageSize * hkv * kHeadDim) * elem_bytes;
 }
 
 // Debug builds synchronise after each launch (outside stream capture) and
@@ -148,6 +158,7 @@ struct Plan {
   int smem;
   int segments;
   int pieces;
+  int stages8 = 0;
   size_t off_seg, off_lse, off_o, off_timeline = 0, bytes;
 };
 
@@ -162,9 +173,13 @@ int validate(const sqa_args* a) {
   if (a->kernel < 0 || a->kernel > 2) return SQA_ERR_INVALID_ARGUMENT;
   if (a->dtype != SQA_DTYPE_F16 && a->dtype != SQA_DTYPE_BF16) return SQA_ERR_UNSUPPORTED;
   if (a->kv_layout != SQA_KV_NHD && a->kv_layout != SQA_KV_HND) return SQA_ERR_UNSUPPORTED;
+  if (a->kv_dtype != SQA_KV_SAME && a->kv_dtype != SQA_KV_FP8_E4M3) return SQA_ERR_UNSUPPORTED;
+  // fp8 caches: fp16 queries, tcgen05 kernel
+  if (a->kv_dtype == SQA_KV_FP8_E4M3 && (a->dtype != SQA_DTYPE_F16 || a->kernel == 1)) return SQA_ERR_UNSUPPORTED;
   // a page must hold 16 x Hkv x 128 elements and start 16-byte aligned (TMA strides)
+  const int64_t align_elems = a->kv_dtype == SQA_KV_FP8_E4M3 ? 16 : 8;
   if (a->page_stride < 0 || (a->page_stride > 0 && (a->page_stride < (int64_t)kPageSize * a->num_kv_heads * kHeadDim ||
-                                                    a->page_stride % 8 != 0)))
+                                                    a->page_stride % align_elems != 0)))
     return SQA_ERR_INVALID_ARGUMENT;
   if (!(a->sm_scale >= 0.f) || !std::isfinite(a->sm_scale) || !std::isfinite(a->out_scale))
     return SQA_ERR_INVALID_ARGUMENT;
@@ -203,7 +218,9 @@ int make_plan(const sqa_args* a, int device, Plan* plan) {
   // Auto (measured on B200): the tcgen05 kernel streams at the HBM roofline for
   // every q_len but has the longer per-CTA latency chain (TMEM, asynchronous MMA
   // completions, replica merge); the warp-level kernel wins small launches.
-  if (a->kernel == 0) {
+  if (a->kv_dtype == SQA_KV_FP8_E4M3) {
+    pl.tc = true;  // the converters live in the tcgen05 kernel
+  } else if (a->kernel == 0) {
     if (a->q_len >= 9) pl.tc = true;
     else if (a->q_len >= 5) pl.tc = units_upper > kAutoTcUnitsQ8;
     else if (a->q_len >= 3) pl.tc = units_upper >= kAutoTcUnitsQ4;
@@ -212,7 +229,15 @@ int make_plan(const sqa_args* a, int device, Plan* plan) {
     pl.tc = a->kernel == 2;
   }
   int ctas_per_sm = kCtasPerSm;
-  if (pl.tc) {  // one CTA per SM: a ring of 4-page blocks in up to 227 KB of shared memory
+  if (pl.tc && a->kv_dtype == SQA_KV_FP8_E4M3) {
+    // fp8: two fp16 operand blocks; the rest of 227 KB stages fp8 blocks (the bytes in flight)
+    ctas_per_sm = 1;
+    pl.stages = kFp8OperandBlocks;
+    const int fixed = split_kv_tc_smem_bytes(pl.stages, 0);
+    pl.stages8 = (kMaxSmemPerCta - fixed) / (split_kv_tc_block_bytes() / 2 + 16);
+    if (pl.stages8 > kMaxStages) pl.stages8 = kMaxStages;
+    pl.smem = split_kv_tc_smem_bytes(pl.stages, pl.stages8);
+  } else if (pl.tc) {  // one CTA per SM: a ring of 4-page blocks in up to 227 KB of shared memory
     ctas_per_sm = 1;
     const int fixed = split_kv_tc_smem_bytes(0);
     pl.stages = (kMaxSmemPerCta - fixed) / (split_kv_tc_block_bytes() + 16);
@@ -322,9 +347,10 @@ int forward_impl(const sqa_args* a, void* workspace, size_t workspace_bytes, voi
 
   CUtensorMap tm_k, tm_v;
   const bool hnd = a->kv_layout == SQA_KV_HND;
-  const uint64_t page_stride = page_stride_bytes(a->page_stride, a->num_kv_heads);
-  if (!encode_cache_map(&tm_k, a->key_cache, a->num_pages, a->num_kv_heads, hnd, page_stride) ||
-      !encode_cache_map(&tm_v, a->value_cache, a->num_pages, a->num_kv_heads, hnd, page_stride))
+  const bool fp8 = a->kv_dtype == SQA_KV_FP8_E4M3;
+  const uint64_t page_stride = page_stride_bytes(a->page_stride, a->num_kv_heads, fp8 ? 1 : 2);
+  if (!encode_cache_map(&tm_k, a->key_cache, a->num_pages, a->num_kv_heads, hnd, page_stride, fp8) ||
+      !encode_cache_map(&tm_v, a->value_cache, a->num_pages, a->num_kv_heads, hnd, page_stride, fp8))
     return SQA_ERR_CUDA;
 
   uint8_t* ws = static_cast<uint8_t*>(workspace);
@@ -354,6 +380,8 @@ int forward_impl(const sqa_args* a, void* workspace, size_t workspace_bytes, voi
   p.bf16 = a->dtype == SQA_DTYPE_BF16;
   p.hnd = hnd;
   p.out_scale = a->out_scale != 0.f ? a->out_scale : 1.f;
+  p.kv_fp8 = fp8;
+  p.num_stages8 = pl.stages8;
 
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_ptr);
   if (ev_before && cudaEventRecord(reinterpret_cast<cudaEvent_t>(ev_before), stream) != cudaSuccess)

@@ -8,7 +8,7 @@
 // t % 16, at element ((page * 16 + slot) * Hkv + kvh) * 128 + d of each cache
 // (the layout of csrc/small_q_attention_ext.cu:466).
 //
-// One thread moves 16 bytes: a token row of one KV head (256 B) is 16 threads,
+// One thread moves 16 bytes: a token row of one KV head (256 B; 128 B for fp8) is 16 (8) threads,
 // consecutive threads read consecutive bytes of new_keys / new_values and
 // write consecutive bytes of one 256-byte cache row.  The step is a pure copy
 // (bit-exact).  A sequence shorter than q_len or with more pages than its
@@ -29,7 +29,8 @@ struct AppendParams {
   const int32_t* block_tables;
   const int32_t* seq_lens;
   unsigned int* status;     // may be null
-  long long items;          // batch * q_len * hkv * 16
+  long long items;          // batch * q_len * hkv * row16
+  int row16;                // 16-byte units per token row of one KV head (16 for 2-byte, 8 for 1-byte elements)
   int q_len, hkv, num_pages, max_pages;
   int hnd;                  // caches are [P, Hkv, 16, 128] (else [P, 16, Hkv, 128])
   long long page_stride16;  // 16-byte units from one page to the next
@@ -41,8 +42,8 @@ __global__ void __launch_bounds__(256) sqa_cache_append_kernel(const AppendParam
   unsigned int bad = 0;
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < p.items; i += stride) {
-    const long long row = i >> 4;  // (b, qi, kvh)
-    const int c = (int)(i & 15);
+    const long long row = i / p.row16;  // (b, qi, kvh)
+    const int c = (int)(i - row * p.row16);
     const int h = (int)(row % p.hkv);
     const long long bq = row / p.hkv;
     const int qi = (int)(bq % p.q_len);
@@ -63,8 +64,8 @@ __global__ void __launch_bounds__(256) sqa_cache_append_kernel(const AppendParam
       bad |= err;
       continue;
     }
-    const size_t in_page = p.hnd ? ((size_t)h * kPageSize + (t % kPageSize)) * 16 + c
-                                 : ((size_t)(t % kPageSize) * p.hkv + h) * 16 + c;
+    const size_t in_page = p.hnd ? ((size_t)h * kPageSize + (t % kPageSize)) * p.row16 + c
+                                 : ((size_t)(t % kPageSize) * p.hkv + h) * p.row16 + c;
     const size_t dst = (size_t)page * p.page_stride16 + in_page;
     p.k_cache[dst] = __ldg(p.new_k + i);
     p.v_cache[dst] = __ldg(p.new_v + i);
@@ -83,8 +84,9 @@ extern "C" SQA_API int sqa_cache_append(const sqa_append_args* a, void* stream) 
   if (a->batch < 0 || a->q_len <= 0 || a->num_kv_heads <= 0 || a->num_pages <= 0 || a->max_pages <= 0)
     return SQA_ERR_INVALID_ARGUMENT;
   if (a->kv_layout != SQA_KV_NHD && a->kv_layout != SQA_KV_HND) return SQA_ERR_UNSUPPORTED;
+  if (a->kv_dtype != SQA_KV_SAME && a->kv_dtype != SQA_KV_FP8_E4M3) return SQA_ERR_UNSUPPORTED;
   if (a->page_stride < 0 || (a->page_stride > 0 && (a->page_stride < (int64_t)kPageSize * a->num_kv_heads * kHeadDim ||
-                                                    a->page_stride % 8 != 0)))
+                                                    a->page_stride % (a->kv_dtype == SQA_KV_FP8_E4M3 ? 16 : 8) != 0)))
     return SQA_ERR_INVALID_ARGUMENT;
   if (a->batch == 0) return SQA_OK;
   if (!a->new_keys || !a->new_values || !a->key_cache || !a->value_cache || !a->block_tables || !a->seq_lens)
@@ -103,13 +105,16 @@ extern "C" SQA_API int sqa_cache_append(const sqa_append_args* a, void* stream) 
   p.block_tables = a->block_tables;
   p.seq_lens = a->seq_lens;
   p.status = a->status;
-  p.items = (long long)a->batch * a->q_len * a->num_kv_heads * 16;
+  const bool fp8 = a->kv_dtype == SQA_KV_FP8_E4M3;
+  p.row16 = fp8 ? 8 : 16;
+  p.items = (long long)a->batch * a->q_len * a->num_kv_heads * p.row16;
   p.q_len = a->q_len;
   p.hkv = a->num_kv_heads;
   p.num_pages = a->num_pages;
   p.max_pages = a->max_pages;
   p.hnd = a->kv_layout == SQA_KV_HND;
-  p.page_stride16 = (a->page_stride > 0 ? a->page_stride : (int64_t)kPageSize * a->num_kv_heads * kHeadDim) / 8;
+  p.page_stride16 =
+      (a->page_stride > 0 ? a->page_stride : (int64_t)kPageSize * a->num_kv_heads * kHeadDim) / (fp8 ? 16 : 8);
 
   int dev = 0, sms = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) !=

@@ -168,6 +168,15 @@ __device__ __forceinline__ bool mbar_drain(uint32_t bar, uint32_t parity, uint64
   }
 }
 
+// 16-byte shared-memory load / store through a 32-bit shared-window address.
+__device__ __forceinline__ void lds_v4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void sts_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
 // ---------------------------------------------------------------- TMA
 // 3-D tiled bulk tensor load global -> shared, completion on an mbarrier.
 // Coordinates are innermost first.  The innermost coordinate is always 0 or 64

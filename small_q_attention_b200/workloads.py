@@ -54,11 +54,12 @@ def config_lens(name: str, seed: int = 0) -> list[int]:
     return [c["kv_len"]] * c["batch"]
 
 
-def algorithmic_bytes(batch: int, q_len: int, lens, hq: int = HQ, hkv: int = HKV) -> int:
+def algorithmic_bytes(batch: int, q_len: int, lens, hq: int = HQ, hkv: int = HKV, kv_bytes: int = 2) -> int:
     """Bytes the operator must move at least once: K and V of every visible
-    token of every KV head, Q in, O out, the used page-table entries and the
+    token of every KV head (``kv_bytes`` per element: 2 for fp16/bf16, 1 for
+    fp8), Q in, O out (2 bytes each), the used page-table entries and the
     lengths."""
-    kv = sum(int(n) for n in lens) * hkv * HEAD_DIM * 2 * 2
+    kv = sum(int(n) for n in lens) * hkv * HEAD_DIM * 2 * kv_bytes
     qo = 2 * batch * q_len * hq * HEAD_DIM * 2
     table = sum((int(n) + PAGE - 1) // PAGE for n in lens) * 4
     return kv + qo + table + 4 * batch

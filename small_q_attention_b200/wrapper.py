@@ -54,7 +54,8 @@ class PagedMTPAttention:
     def plan(self, batch: int, q_len: int, num_kv_heads: int, num_pages: int, max_pages: int,
              max_seq_len: int = 0, *, page_size: int = PAGE_SIZE, head_dim: int = HEAD_DIM,
              num_ctas: int = 0, min_pages_per_cta: int = 0, kv_layout: str = "NHD",
-             sm_scale: float | None = None, out_scale: float = 1.0) -> "PagedMTPAttention":
+             sm_scale: float | None = None, out_scale: float = 1.0,
+             cache_dtype: torch.dtype | None = None) -> "PagedMTPAttention":
         """Fix the shapes of the following ``run`` calls and size the workspace.
 
         ``max_seq_len`` bounds ``seq_lens`` for the launch size (0: the page-table
@@ -72,6 +73,8 @@ class PagedMTPAttention:
         a.num_kv_heads, a.page_size, a.num_pages, a.max_pages = num_kv_heads, page_size, num_pages, max_pages
         a.max_seq_len, a.num_ctas, a.min_pages_per_cta, a.kernel = max_seq_len, num_ctas, min_pages_per_cta, self._kernel
         a.kv_layout = _layout_code(kv_layout)
+        if cache_dtype is not None and cache_dtype == getattr(torch, "float8_e4m3fn", None):
+            a.kv_dtype = _native.KV_FP8_E4M3  # fp8 caches run on the tcgen05 kernel
         lib = _native.library()
         st = ctypes.c_int(0)
         need = int(lib.sqa_workspace_bytes(ctypes.byref(a), self.device.index, ctypes.byref(st)))

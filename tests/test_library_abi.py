@@ -42,7 +42,7 @@ def test_every_declared_symbol_is_exported(lib):
 
 
 def test_abi_version_and_status_strings(lib):
-    assert lib.sqa_abi_version() == 106
+    assert lib.sqa_abi_version() == 107
     for code in range(6):
         assert lib.sqa_status_string(code).decode()
     assert lib.sqa_status_string(99).decode() == "unknown status"
