@@ -19,8 +19,11 @@ __global__ void __launch_bounds__(128) sqa_segment_merge_kernel(const MergeParam
   unsigned long long* tl =
       p.timeline ? p.timeline + ((size_t)blockIdx.y * gridDim.x + blockIdx.x) * 4 : nullptr;
   if (threadIdx.x == 0) SQA_STAMP(tl, 0);
+  // The next kernel may launch now: it waits for this grid's completion before
+  // it touches memory, and until then its CTAs take SMs as the split-KV CTAs
+  // leave them (and prefetch).
+  allow_dependent_launch();
   grid_dependency_wait();    // the split-KV grid has finished writing the partials
-  allow_dependent_launch();  // the next call's split-KV kernel may start its prologue
   if (threadIdx.x == 0) SQA_STAMP(tl, 1);
   const int s = blockIdx.x;
   const int b = s / p.hkv;
@@ -34,6 +37,8 @@ __global__ void __launch_bounds__(128) sqa_segment_merge_kernel(const MergeParam
   float* out_o = p.out_o ? p.out_o + out_row * kHeadDim : nullptr;
   float* out_lse = p.out_lse ? p.out_lse + out_row : nullptr;
 
+  // both loads in flight together
+  const int2 info = p.seg_info[s];
   const int len = max(__ldg(p.seq_lens + b), 0);
   if (len == 0) {  // no page was processed for this sequence: nothing is visible
     if (out) reinterpret_cast<uint2*>(out)[lane] = make_uint2(0u, 0u);  // +0 in fp16 and bf16
@@ -41,7 +46,6 @@ __global__ void __launch_bounds__(128) sqa_segment_merge_kernel(const MergeParam
     if (out_lse && lane == 0) *out_lse = -INFINITY;
     return;
   }
-  const int2 info = p.seg_info[s];
   if (info.y <= 1) return;  // written directly by the split-KV kernel
   if (!SQA_CHECK(info.x >= 0 && info.x + info.y <= p.num_parts, p.status, 8, s)) return;
   const size_t first = (size_t)info.x * p.piece_rows + row;
@@ -52,8 +56,8 @@ __global__ void __launch_bounds__(128) sqa_segment_merge_kernel(const MergeParam
 
 // Cross-device merge: rows given explicitly, 4 rows per CTA.
 __global__ void __launch_bounds__(128) sqa_partials_merge_kernel(const MergeParams p) {
-  grid_dependency_wait();
   allow_dependent_launch();
+  grid_dependency_wait();
   const long long row = (long long)blockIdx.x * 4 + (threadIdx.x >> 5);
   if (row >= p.rows) return;
   merge_row<false>(p.parts_o + row * kHeadDim, (size_t)p.rows * kHeadDim, p.parts_lse + row, (size_t)p.rows,

@@ -11,6 +11,7 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cuda_fp8.h>
 #include <stdint.h>
 
 namespace sqa {
@@ -202,6 +203,21 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+// L2 prefetch of one box of a 4-D tensor map (no shared memory, no barrier;
+// coordinates outside the map are not read).
+__device__ __forceinline__ void tma_prefetch_4d(const CUtensorMap* map, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
+
+// L2 prefetch of `bytes` (a multiple of 16) from a 16-byte aligned global address.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
+               : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -352,6 +368,40 @@ __device__ __forceinline__ bool elect_one() {
   return pred != 0;
 }
 
+// kind::f8f6f4 forms (8-bit A and B; fp32 D): A from TMEM (4 elements per
+// 32-bit column), B from a shared-memory descriptor; K = 32 per instruction.
+__device__ __forceinline__ void tc_mma_ts_f8(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], [%1], %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void tc_mma_ts_f8_lanes(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                                   uint32_t accumulate, const uint32_t (&off)[4]) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(off[0]), "r"(off[1]),
+      "r"(off[2]), "r"(off[3])
+      : "memory");
+}
+
+// Two floats -> two e4m3 (round to nearest even, saturating to +-448), low float in the low byte.
+__device__ __forceinline__ uint32_t pack_e4m3x2(float lo, float hi) {
+  return (uint32_t)__nv_cvt_float2_to_fp8x2(make_float2(lo, hi), __NV_SATFINITE, __NV_E4M3);
+}
+// Two e4m3 (low byte first) -> two floats (exact).
+__device__ __forceinline__ float2 unpack_e4m3x2(uint32_t v) {
+  const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(v & 0xffffu), __NV_E4M3);
+  __half2 hh;
+  *reinterpret_cast<__half2_raw*>(&hh) = h;
+  return __half22float2(hh);
+}
+
 // Arrive on an mbarrier once every tcgen05.mma issued so far by this thread has completed.
 __device__ __forceinline__ void tc_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
@@ -416,7 +466,8 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo
 }
 
 // Instruction descriptor of tcgen05.mma.kind::f16: fp16 (bf16 = false) or bf16
-// A and B (always the same type), fp32 D.
+// A and B (always the same type), fp32 D.  The same fields with format code 0
+// describe e4m3 A and B for kind::f8f6f4.
 __host__ __device__ constexpr uint32_t mma_idesc_f16(int m, int n, bool a_mn_major, bool b_mn_major,
                                                      bool bf16 = false) {
   return (1u << 4)                                           // D format: f32
@@ -428,6 +479,11 @@ __host__ __device__ constexpr uint32_t mma_idesc_f16(int m, int n, bool a_mn_maj
 // Named barrier over `count` threads (the consumer warps only).
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+// Arrive on a named barrier without waiting (pairs with named_bar_sync of the
+// waiting threads; `count` counts both).
+__device__ __forceinline__ void named_bar_arrive(uint32_t id, uint32_t count) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
 }  // namespace sqa

@@ -20,8 +20,16 @@ struct SegWalk {
   int seg_start;  // global unit index of (b, h, page 0)
 };
 
+// kSpec: a read before the dependency wait, through L2 only (ld.global.cg), so
+// that no possibly stale line is left in L1 for the reads after the wait.
+template <bool kSpec = false>
+__device__ __forceinline__ int load_len(const SplitKvParams& p, int b) {
+  return kSpec ? __ldcg(p.seq_lens + b) : __ldg(p.seq_lens + b);
+}
+
+template <bool kSpec = false>
 __device__ __forceinline__ int seq_pages(const SplitKvParams& p, int b) {
-  const int len = max(__ldg(p.seq_lens + b), 0);
+  const int len = max(load_len<kSpec>(p, b), 0);
   return min((len + kPageSize - 1) / kPageSize, p.max_pages);
 }
 
@@ -45,8 +53,11 @@ struct Schedule {
   int abort;           // set by a timed-out wait
 };
 
-// Warp 0: total units, this CTA's range and the sequence it starts in.
-__device__ __forceinline__ void build_schedule(const SplitKvParams& p, Schedule* sch) {
+// Whole warp: total units, this CTA's range and the sequence it starts in
+// (every lane gets the result).  kSpec: computed before the dependency wait
+// from values that may be stale, for prefetches only; no status is raised.
+template <bool kSpec>
+__device__ __forceinline__ Schedule compute_schedule(const SplitKvParams& p) {
   const int lane = threadIdx.x & 31;
   unsigned int flags = 0;
   int total_pages = 0;
@@ -54,8 +65,8 @@ __device__ __forceinline__ void build_schedule(const SplitKvParams& p, Schedule*
     const int b = base + lane;
     int pages = 0;
     if (b < p.batch) {
-      const int len = __ldg(p.seq_lens + b);
-      pages = seq_pages(p, b);
+      const int len = load_len<kSpec>(p, b);
+      pages = min((max(len, 0) + kPageSize - 1) / kPageSize, p.max_pages);
       if (len > p.max_pages * kPageSize) flags |= 2u;                 // SQA_DEV_SEQ_TOO_LONG
       if (p.out != nullptr && len < p.q_len) flags |= 4u;             // SQA_DEV_SEQ_TOO_SHORT
     }
@@ -63,8 +74,10 @@ __device__ __forceinline__ void build_schedule(const SplitKvParams& p, Schedule*
     for (int off = 16; off > 0; off >>= 1) pages += __shfl_xor_sync(0xffffffffu, pages, off);
     total_pages += pages;
   }
-  flags = __reduce_or_sync(0xffffffffu, flags);
-  if (blockIdx.x == 0 && lane == 0 && flags) atomicOr(p.status, flags);
+  if (!kSpec) {
+    flags = __reduce_or_sync(0xffffffffu, flags);
+    if (blockIdx.x == 0 && lane == 0 && flags) atomicOr(p.status, flags);
+  }
 
   const int total = total_pages * p.hkv;
   const int per = max(1, (total + (int)gridDim.x - 1) / (int)gridDim.x);
@@ -77,7 +90,7 @@ __device__ __forceinline__ void build_schedule(const SplitKvParams& p, Schedule*
     int running = 0;  // units before this 32-sequence block
     for (int base = 0; base < p.batch; base += 32) {
       const int b = base + lane;
-      const int units = (b < p.batch) ? seq_pages(p, b) * p.hkv : 0;
+      const int units = (b < p.batch) ? seq_pages<kSpec>(p, b) * p.hkv : 0;
       int incl = units;
 #pragma unroll
       for (int off = 1; off < 32; off <<= 1) {
@@ -94,14 +107,20 @@ __device__ __forceinline__ void build_schedule(const SplitKvParams& p, Schedule*
       running += __shfl_sync(0xffffffffu, incl, 31);
     }
   }
-  if (lane == 0) {
-    sch->start = start;
-    sch->end = end;
-    sch->per_cta = per;
-    sch->b0 = b0;
-    sch->u_b0 = u_b0;
-    sch->abort = 0;
-  }
+  Schedule s;
+  s.start = start;
+  s.end = end;
+  s.per_cta = per;
+  s.b0 = b0;
+  s.u_b0 = u_b0;
+  s.abort = 0;
+  return s;
+}
+
+// Warp 0: the schedule into shared memory, before the CTA-wide barrier.
+__device__ __forceinline__ void build_schedule(const SplitKvParams& p, Schedule* sch) {
+  const Schedule s = compute_schedule<false>(p);
+  if ((threadIdx.x & 31) == 0) *sch = s;
 }
 
 __device__ __forceinline__ SegWalk first_segment(const SplitKvParams& p, const Schedule& s) {
@@ -113,6 +132,65 @@ __device__ __forceinline__ SegWalk first_segment(const SplitKvParams& p, const S
   w.pg = off - w.h * w.pages;
   w.seg_start = s.u_b0 + w.h * w.pages;
   return w;
+}
+
+// Producer warp, before the dependency wait: L2 prefetches of the first
+// `budget` pages (at most 32 per segment, two segments at most) and the first
+// Q rows this CTA will load, from a schedule and page ids read through L2
+// while the previous grid may still be running.  Those values may
+// be stale: they only steer prefetches (nothing is consumed or written, and a
+// page id outside the pool is skipped), and every value is read again after
+// the wait.  The loads after the wait then find their lines in L2.
+template <bool F8>
+__device__ __forceinline__ void prefetch_start(const SplitKvParams& p, const CUtensorMap* tm_k,
+                                               const CUtensorMap* tm_v, int budget) {
+  const int lane = threadIdx.x & 31;
+  const Schedule s = compute_schedule<true>(p);
+  if (s.start >= s.end) return;
+  int b = s.b0;
+  int pages = seq_pages<true>(p, b);
+  if (pages <= 0) return;
+  const int off = s.start - s.u_b0;
+  int h = off / pages;
+  int pg = off - h * pages;
+  if (h >= p.hkv) return;
+  if (lane < p.q_len) {  // the 4 query heads of (b, h) for draft token `lane`: 1 KB
+    bulk_prefetch_l2(p.q + ((size_t)(b * p.q_len + lane) * p.hq + h * kGroup) * kHeadDim,
+                     kGroup * kHeadDim * 2);
+  }
+  int unit = s.start;
+  for (int seg = 0; seg < 2 && budget > 0 && unit < s.end; ++seg) {
+    const int m = min(min(pages - pg, s.end - unit), min(budget, 32));
+    if (lane < m) {
+      const int id = __ldcg(p.block_tables + (size_t)b * p.max_pages + pg + lane);
+      if (id >= 0 && id < p.num_pages) {
+        const int k1 = p.hnd ? 0 : h, k2 = p.hnd ? h : 0;  // NHD (dim, head, token, page); HND (dim, token, head, page)
+        if constexpr (F8) {  // fp8 maps: one 128-dim box per page
+          tma_prefetch_4d(tm_k, 0, k1, k2, id);
+          tma_prefetch_4d(tm_v, 0, k1, k2, id);
+        } else {  // 16-bit maps: two 64-dim boxes per page
+          tma_prefetch_4d(tm_k, 0, k1, k2, id);
+          tma_prefetch_4d(tm_k, 64, k1, k2, id);
+          tma_prefetch_4d(tm_v, 0, k1, k2, id);
+          tma_prefetch_4d(tm_v, 64, k1, k2, id);
+        }
+      }
+    }
+    budget -= m;
+    unit += m;
+    pg += m;
+    if (pg >= pages) {  // the next segment: next KV head, or the next sequence with pages
+      pg = 0;
+      if (++h == p.hkv) {
+        h = 0;
+        do {
+          ++b;
+          pages = (b < p.batch) ? seq_pages<true>(p, b) : 0;
+        } while (pages == 0 && b < p.batch);
+        if (b >= p.batch) break;
+      }
+    }
+  }
 }
 
 }  // namespace sqa

@@ -440,12 +440,19 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int i = 0; i < p.num_stages; ++i) mbar_init(smem_u32(empty + i), WR);
     fence_mbar_init();
   }
-  if (warp == kConsumerWarps && (threadIdx.x & 31) == 0) {
-    prefetch_tensormap(&tm_k);
-    prefetch_tensormap(&tm_v);
+  if (warp == kConsumerWarps) {
+    if ((threadIdx.x & 31) == 0) {
+      prefetch_tensormap(&tm_k);
+      prefetch_tensormap(&tm_v);
+    }
+    __syncwarp();
+#ifndef SQA_NO_START_PREFETCH
+    prefetch_start<false>(p, &tm_k, &tm_v, p.num_stages);
+#endif
   }
-  // Everything above touches only shared memory and kernel parameters; the
-  // inputs and the workspace may still be in use by the previous kernel.
+  // Everything above writes only shared memory and reads the inputs only as
+  // prefetch hints; the inputs and the workspace may still be in use by the
+  // previous kernel.
   grid_dependency_wait();
   allow_dependent_launch();  // the merge kernel may be scheduled now; it waits for this grid
   if (threadIdx.x == 0) SQA_STAMP(tl, 1);  // after the dependency wait

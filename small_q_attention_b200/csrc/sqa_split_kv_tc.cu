@@ -672,6 +672,12 @@ __global__ void __launch_bounds__(kThreadsTc + (F8 ? kConvertWarps * 32 : 0), 1)
     prefetch_tensormap(&tm_k);
     prefetch_tensormap(&tm_v);
   }
+#ifndef SQA_NO_START_PREFETCH
+  // The PV issuer has nothing to do before the first P: it prefetches this
+  // CTA's first pages into L2 before the dependency wait (hints only), off the
+  // start-up path of the other warps.
+  if (warp == kPvWarp) prefetch_start<F8>(p, &tm_k, &tm_v, (F8 ? p.num_stages8 : p.num_stages) * kBP);
+#endif
   grid_dependency_wait();
   allow_dependent_launch();
   if (threadIdx.x == 0) SQA_STAMP(tl, 1);
@@ -681,7 +687,17 @@ __global__ void __launch_bounds__(kThreadsTc + (F8 ? kConvertWarps * 32 : 0), 1)
   }
   if (warp == 0) build_schedule(p, sm.sch);
   tc_fence_before();
-  __syncthreads();
+  // Start-up barrier: the TMEM address, the schedule and the mbarriers are
+  // ready.  Every warp but the PV issuer syncs on barrier 3 and arrives on
+  // barrier 2; the PV issuer waits on barrier 2 only, so its prefetches never
+  // hold up the others.
+  const uint32_t nthreads = blockDim.x;
+  if (warp == kPvWarp) {
+    named_bar_sync(2, nthreads);
+  } else {
+    named_bar_sync(3, nthreads - 32);
+    named_bar_arrive(2, nthreads);
+  }
   tc_fence_after();
   const uint32_t tmem = *sm.tmem_base;
   const Schedule s = *sm.sch;
