@@ -100,3 +100,35 @@ def test_tc_large_pool_repeat(sqa, q_len):
         ref = paged_mtp_attention_reference(c["query"][b:b + 1], kc, vc, c["block_tables"][b:b + 1],
                                             c["seq_lens"][b:b + 1], 16, 8)
         assert_close(first[b:b + 1], ref)
+
+
+def test_tc_workspace_shared_across_shapes(sqa):
+    """One workspace for calls of different shapes, interleaved: the in-kernel
+    merge's per-segment counters of one shape are left in place when the next
+    shape runs, and the launch generation keeps them apart."""
+    cases = [case(4, [3000, 900, 5000, 40], hkv=8, seed=31),
+             case(8, [700] * 40, hkv=8, seed=32),               # 320 segments
+             case(2, [9000], hkv=2, seed=33)]
+    refs = [oracle(c) for c in cases]
+    ws = torch.zeros(max(sqa.workspace_bytes(c["query"], c["key_cache"], c["value_cache"], c["block_tables"],
+                                             c["seq_lens"], 16, kernel=TC) for c in cases),
+                     dtype=torch.uint8, device="cuda")
+    for i in (0, 1, 0, 2, 1, 2, 0):
+        c = cases[i]
+        out = sqa.small_q_attention(c["query"], c["key_cache"], c["value_cache"], c["block_tables"], c["seq_lens"],
+                                    16, check=True, kernel=TC, workspace=ws, num_ctas=37, min_pages_per_cta=1)
+        assert_close(out, refs[i])
+
+
+def test_tc_empty_sequences_are_zero(sqa):
+    """A sequence with seq_lens 0 has no page to visit: its rows are written as 0."""
+    c = case(4, [2000, 16, 1200], hkv=8, seed=41)
+    ref = oracle(c)
+    lens = c["seq_lens"].clone()
+    lens[1] = 0
+    out = torch.full_like(c["query"], float("nan"))
+    sqa.small_q_attention(c["query"], c["key_cache"], c["value_cache"], c["block_tables"], lens, 16,
+                          out=out, kernel=TC, num_ctas=20, min_pages_per_cta=1)
+    assert torch.count_nonzero(out[1]).item() == 0
+    assert_close(out[0:1], ref[0:1])
+    assert_close(out[2:3], ref[2:3])
