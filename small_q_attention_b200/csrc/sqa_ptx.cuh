@@ -52,9 +52,16 @@ __device__ __forceinline__ bool debug_check(bool ok, unsigned int* status, unsig
   do {                     \
     if (tl) (tl)[idx] = global_timer_ns(); \
   } while (0)
+#define SQA_CLK(tl, idx) \
+  do {                   \
+    if (tl) (tl)[idx] = clock64(); \
+  } while (0)
 #else
 #define SQA_STAMP(tl, idx) \
   do {                     \
+  } while (0)
+#define SQA_CLK(tl, idx) \
+  do {                   \
   } while (0)
 #endif
 

@@ -50,30 +50,45 @@ struct Schedule {
   int start, end;      // this CTA's unit range
   int per_cta;         // units per CTA
   int b0, u_b0;        // sequence containing `start` and the units before it
+  int pages_b0;        // pages of sequence b0
   int abort;           // set by a timed-out wait
 };
 
 // Whole warp: total units, this CTA's range and the sequence it starts in
-// (every lane gets the result).  kSpec: computed before the dependency wait
-// from values that may be stale, for prefetches only; no status is raised.
+// (every lane gets the result).  Each lane reads the lengths of its sequences
+// once: the first kCachedChunks chunks of 32 sequences stay in registers for
+// the prefix scan, so a batch of up to 128 costs one memory round trip.
+// kSpec: computed before the dependency wait from values that may be stale,
+// for prefetches only; no status is raised.
 template <bool kSpec>
 __device__ __forceinline__ Schedule compute_schedule(const SplitKvParams& p) {
+  constexpr int kCachedChunks = 4;
   const int lane = threadIdx.x & 31;
   unsigned int flags = 0;
   int total_pages = 0;
-  for (int base = 0; base < p.batch; base += 32) {
-    const int b = base + lane;
+  int cached[kCachedChunks];
+  auto pages_of = [&](int b, unsigned int& fl) {
     int pages = 0;
     if (b < p.batch) {
       const int len = load_len<kSpec>(p, b);
       pages = min((max(len, 0) + kPageSize - 1) / kPageSize, p.max_pages);
-      if (len > p.max_pages * kPageSize) flags |= 2u;                 // SQA_DEV_SEQ_TOO_LONG
-      if (p.out != nullptr && len < p.q_len) flags |= 4u;             // SQA_DEV_SEQ_TOO_SHORT
+      if (len > p.max_pages * kPageSize) fl |= 2u;                 // SQA_DEV_SEQ_TOO_LONG
+      if (p.out != nullptr && len < p.q_len) fl |= 4u;             // SQA_DEV_SEQ_TOO_SHORT
     }
+    return pages;
+  };
+  auto warp_sum = [](int v) {
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) pages += __shfl_xor_sync(0xffffffffu, pages, off);
-    total_pages += pages;
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    return v;
+  };
+#pragma unroll
+  for (int c = 0; c < kCachedChunks; ++c) {  // every load of the cached chunks in flight at once
+    cached[c] = pages_of(c * 32 + lane, flags);
   }
+#pragma unroll
+  for (int c = 0; c < kCachedChunks; ++c) total_pages += warp_sum(cached[c]);
+  for (int base = kCachedChunks * 32; base < p.batch; base += 32) total_pages += warp_sum(pages_of(base + lane, flags));
   if (!kSpec) {
     flags = __reduce_or_sync(0xffffffffu, flags);
     if (blockIdx.x == 0 && lane == 0 && flags) atomicOr(p.status, flags);
@@ -85,12 +100,20 @@ __device__ __forceinline__ Schedule compute_schedule(const SplitKvParams& p) {
   const int end = min(total, start + per);
 
   // Sequence containing unit `start`: first b whose inclusive unit prefix exceeds it.
-  int b0 = p.batch, u_b0 = 0;
+  int b0 = p.batch, u_b0 = 0, pages_b0 = 0;
   if (start < end) {
     int running = 0;  // units before this 32-sequence block
     for (int base = 0; base < p.batch; base += 32) {
-      const int b = base + lane;
-      const int units = (b < p.batch) ? seq_pages<kSpec>(p, b) * p.hkv : 0;
+      const int c = base / 32;
+      int pg = 0;
+#pragma unroll
+      for (int k = 0; k < kCachedChunks; ++k)
+        if (k == c) pg = cached[k];
+      if (c >= kCachedChunks) {
+        unsigned int unused = 0;
+        pg = pages_of(base + lane, unused);
+      }
+      const int units = pg * p.hkv;
       int incl = units;
 #pragma unroll
       for (int off = 1; off < 32; off <<= 1) {
@@ -102,6 +125,7 @@ __device__ __forceinline__ Schedule compute_schedule(const SplitKvParams& p) {
         const int l = __ffs(hit) - 1;
         b0 = base + l;
         u_b0 = running + __shfl_sync(0xffffffffu, incl - units, l);
+        pages_b0 = __shfl_sync(0xffffffffu, pg, l);
         break;
       }
       running += __shfl_sync(0xffffffffu, incl, 31);
@@ -113,6 +137,7 @@ __device__ __forceinline__ Schedule compute_schedule(const SplitKvParams& p) {
   s.per_cta = per;
   s.b0 = b0;
   s.u_b0 = u_b0;
+  s.pages_b0 = pages_b0;
   s.abort = 0;
   return s;
 }
@@ -126,7 +151,7 @@ __device__ __forceinline__ void build_schedule(const SplitKvParams& p, Schedule*
 __device__ __forceinline__ SegWalk first_segment(const SplitKvParams& p, const Schedule& s) {
   SegWalk w;
   w.b = s.b0;
-  w.pages = (s.start < s.end) ? seq_pages(p, s.b0) : 1;
+  w.pages = (s.start < s.end) ? s.pages_b0 : 1;
   const int off = s.start - s.u_b0;
   w.h = off / w.pages;
   w.pg = off - w.h * w.pages;
@@ -148,7 +173,7 @@ __device__ __forceinline__ void prefetch_start(const SplitKvParams& p, const CUt
   const Schedule s = compute_schedule<true>(p);
   if (s.start >= s.end) return;
   int b = s.b0;
-  int pages = seq_pages<true>(p, b);
+  int pages = s.pages_b0;
   if (pages <= 0) return;
   const int off = s.start - s.u_b0;
   int h = off / pages;

@@ -61,16 +61,29 @@ __device__ void producer_loop(const SplitKvParams& p, const Schedule& sch, const
   unsigned int bad_page = 0;
   int issued = 0;  // pages whose loads were issued (a prefix of the range)
   int unit = sch.start;
+  // Page ids are read 32 at a time, one chunk ahead of the loads they feed,
+  // across piece boundaries too: a new piece never waits for its table row.
+  int ids = 0;
+  if (unit < sch.end) {
+    const int n0 = min(sch.end, w.seg_start + w.pages) - unit;
+    ids = (lane < n0) ? __ldg(p.block_tables + (size_t)w.b * p.max_pages + w.pg + lane) : 0;
+  }
   while (unit < sch.end) {
     const int seg_end = w.seg_start + w.pages;
     const int n = min(sch.end, seg_end) - unit;
     const int32_t* row = p.block_tables + (size_t)w.b * p.max_pages + w.pg;
-    int ids = (lane < n) ? __ldg(row + lane) : 0;
+    const int unit_next = unit + n;  // the next piece, for the look-ahead at this piece's last chunk
+    SegWalk wn = w;
+    if (unit_next < sch.end) next_segment(p, wn);
     for (int c0 = 0; c0 < n; c0 += 32) {
       const int cnt = min(32, n - c0);
-      // prefetch the next 32 page ids while this block is issued
-      const int nxt = c0 + 32 + lane;
-      const int ids_next = (nxt < n) ? __ldg(row + nxt) : 0;
+      int ids_next = 0;
+      if (c0 + 32 < n) {
+        ids_next = (c0 + 32 + lane < n) ? __ldg(row + c0 + 32 + lane) : 0;
+      } else if (unit_next < sch.end) {
+        const int n2 = min(sch.end, wn.seg_start + wn.pages) - unit_next;
+        ids_next = (lane < n2) ? __ldg(p.block_tables + (size_t)wn.b * p.max_pages + wn.pg + lane) : 0;
+      }
       for (int j = 0; j < cnt; ++j) {
         int page = __shfl_sync(0xffffffffu, ids, j);
         if (page < 0 || page >= p.num_pages) {
@@ -122,9 +135,8 @@ __device__ void producer_loop(const SplitKvParams& p, const Schedule& sch, const
       }
       ids = ids_next;
     }
-    unit += n;
-    if (unit >= seg_end) next_segment(p, w);
-    else w.pg += n;
+    unit = unit_next;
+    w = wn;
   }
   if (__any_sync(0xffffffffu, bad_page) && lane == 0) atomicOr(p.status, 8u);  // SQA_DEV_BAD_PAGE
   // No bulk copy may still be landing in this CTA's shared memory when it

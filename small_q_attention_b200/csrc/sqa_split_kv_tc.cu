@@ -121,15 +121,29 @@ __device__ void tc_producer(const SplitKvParams& p, const Schedule& sch, const C
   unsigned int bad_page = 0;
   int issued = 0;  // blocks whose loads were issued (a prefix)
   int unit = sch.start;
+  // Page ids are read 32 at a time, one chunk ahead of the loads they feed,
+  // across piece boundaries too: a new piece never waits for its table row.
+  int ids = 0;
+  if (unit < sch.end) {
+    const int n0 = min(sch.end, w.seg_start + w.pages) - unit;
+    ids = (lane < n0) ? __ldg(p.block_tables + (size_t)w.b * p.max_pages + w.pg + lane) : 0;
+  }
   while (unit < sch.end) {
     const int seg_end = w.seg_start + w.pages;
     const int n = min(sch.end, seg_end) - unit;
     const int32_t* row = p.block_tables + (size_t)w.b * p.max_pages + w.pg;
-    int ids = (lane < n) ? __ldg(row + lane) : 0;
+    const int unit_next = unit + n;  // the next piece, for the look-ahead at this piece's last chunk
+    SegWalk wn = w;
+    if (unit_next < sch.end) next_segment(p, wn);
     for (int c0 = 0; c0 < n; c0 += 32) {  // 32 is a multiple of kBP: blocks never straddle chunks
       const int cnt = min(32, n - c0);
-      const int nxt = c0 + 32 + lane;
-      const int ids_next = (nxt < n) ? __ldg(row + nxt) : 0;
+      int ids_next = 0;
+      if (c0 + 32 < n) {
+        ids_next = (c0 + 32 + lane < n) ? __ldg(row + c0 + 32 + lane) : 0;
+      } else if (unit_next < sch.end) {
+        const int n2 = min(sch.end, wn.seg_start + wn.pages) - unit_next;
+        ids_next = (lane < n2) ? __ldg(p.block_tables + (size_t)wn.b * p.max_pages + wn.pg + lane) : 0;
+      }
       for (int jb = 0; jb < cnt; jb += kBP) {
         const int np = min(kBP, cnt - jb);
         int pages[kBP];
@@ -178,9 +192,8 @@ __device__ void tc_producer(const SplitKvParams& p, const Schedule& sch, const C
       }
       ids = ids_next;
     }
-    unit += n;
-    if (unit >= seg_end) next_segment(p, w);
-    else w.pg += n;
+    unit = unit_next;
+    w = wn;
   }
   if (__any_sync(0xffffffffu, bad_page) && lane == 0) atomicOr(p.status, 8u);  // SQA_DEV_BAD_PAGE
   if (lane == 0 && *abort) {  // only an abort can leave loads in flight
@@ -307,7 +320,10 @@ __device__ void tc_mma_qk(const SplitKvParams& p, const Schedule& sch, const TcS
       mbar_wait_bounded(smem_u32(sm.full + slot), (uint32_t)(h / NB) & 1u, abort, p.status, 5, h);
       __syncwarp();
       tc_fence_after();
-      if (h == 0 && (threadIdx.x & 31) == 0 && p.timeline) SQA_STAMP(p.timeline + (size_t)blockIdx.x * 32, 3);
+      if (h == 0 && (threadIdx.x & 31) == 0 && p.timeline) {
+        SQA_STAMP(p.timeline + (size_t)blockIdx.x * 32, 3);
+        SQA_CLK(p.timeline + (size_t)blockIdx.x * 32, 12);
+      }
       const uint64_t t_qk = SQA_T0();
       if (elect_one()) {
         const uint32_t k_base = smem_u32(sm.ring + (size_t)slot * kBlockBytes);
@@ -401,19 +417,17 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
   // This thread's lane of Q slot `qs` gets packed row lrow of (b, h) (zeros past the rows).
   auto write_q = [&](int b, int h, int qs) {
     const __half* src = p.q + ((size_t)(b * p.q_len + (lrow >> 2)) * p.hq + h * kGroup + (lrow & 3)) * kHeadDim;
+    uint32_t qv[2][32];  // the whole row first: one memory round trip
 #pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      uint32_t qv[32];
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        uint4 v = active ? __ldg(reinterpret_cast<const uint4*>(src + hh * 64) + c) : make_uint4(0u, 0u, 0u, 0u);
-        qv[4 * c] = v.x;
-        qv[4 * c + 1] = v.y;
-        qv[4 * c + 2] = v.z;
-        qv[4 * c + 3] = v.w;
-      }
-      tmem_st32(tl + kColQ + qs * 64 + hh * 32, qv);
+    for (int c = 0; c < 16; ++c) {
+      uint4 v = active ? __ldg(reinterpret_cast<const uint4*>(src) + c) : make_uint4(0u, 0u, 0u, 0u);
+      qv[c >> 3][4 * (c & 7)] = v.x;
+      qv[c >> 3][4 * (c & 7) + 1] = v.y;
+      qv[c >> 3][4 * (c & 7) + 2] = v.z;
+      qv[c >> 3][4 * (c & 7) + 3] = v.w;
     }
+    tmem_st32(tl + kColQ + qs * 64, qv[0]);
+    tmem_st32(tl + kColQ + qs * 64 + 32, qv[1]);
     tmem_wait_st();
     tc_fence_before();
     __syncwarp();
@@ -444,7 +458,10 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
     // of the next piece can run while this piece's epilogue is still merging.
     // Slot (pc + 1) % 2 is free: every QK product of piece pc - 1 is complete
     // (all its S blocks were consumed).
-    if (pc == 0) write_q(w.b, w.h, 0);
+    if (pc == 0) {
+      write_q(w.b, w.h, 0);
+      if (tid == 0 && p.timeline) SQA_CLK(p.timeline + (size_t)blockIdx.x * 32, 13);
+    }
     if (seg_end < sch.end) {  // the next piece starts the next segment
       SegWalk nw = w;
       next_segment(p, nw);
@@ -459,6 +476,7 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
       const int valid = np * kPageSize - tok_lo;                 // valid columns of this replica (may be <= 0)
       mbar_wait_bounded(smem_u32(sm.s_full + (g % kNumS)), (uint32_t)(g / kNumS) & 1u, abort, p.status, 7, g);
       tc_fence_after();
+      if (g == 0 && tid == 0 && p.timeline) SQA_CLK(p.timeline + (size_t)blockIdx.x * 32, 14);
       const uint64_t t_sm = SQA_T0();
       const uint32_t slot_col = tl + kColS + (g % kNumS) * kSlotCols;
       uint32_t sraw[kTok];
@@ -625,6 +643,9 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
     if (unit >= seg_end) next_segment(p, w);
     else w.pg += n;
   }
+#ifdef SQA_DEBUG_TIMELINE
+  if (tid == 0 && p.timeline) p.timeline[(size_t)blockIdx.x * 32 + 15] = (unsigned long long)gb0 * 100 + pc;
+#endif
 }
 
 template <int R, bool BF, bool F8>
@@ -680,7 +701,10 @@ __global__ void __launch_bounds__(kThreadsTc + (F8 ? kConvertWarps * 32 : 0), 1)
 #endif
   grid_dependency_wait();
   allow_dependent_launch();
-  if (threadIdx.x == 0) SQA_STAMP(tl, 1);
+  if (threadIdx.x == 0) {
+    SQA_STAMP(tl, 1);
+    SQA_CLK(tl, 8);
+  }
   if (warp == kMmaWarp) {
     tmem_alloc(smem_u32(sm.tmem_base), kTmemCols);
     tmem_relinquish();
@@ -702,7 +726,10 @@ __global__ void __launch_bounds__(kThreadsTc + (F8 ? kConvertWarps * 32 : 0), 1)
   const uint32_t tmem = *sm.tmem_base;
   const Schedule s = *sm.sch;
   volatile int* abort = &sm.sch->abort;
-  if (threadIdx.x == 0) SQA_STAMP(tl, 2);
+  if (threadIdx.x == 0) {
+    SQA_STAMP(tl, 2);
+    SQA_CLK(tl, 9);
+  }
 
   if (warp == kProducerWarp) {
     tc_producer<F8>(p, s, &tm_k, &tm_v, sm, abort);
@@ -729,7 +756,7 @@ __global__ void __launch_bounds__(kThreadsTc + (F8 ? kConvertWarps * 32 : 0), 1)
     unsigned int smid;
     asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
     tl[7] = smid;
-    for (int k = 0; k < 16; ++k) tl[16 + k] = sqa_wait_ns[k];
+    for (int k = 1; k < 16; ++k) tl[16 + k] = sqa_wait_ns[k];
   }
 #endif
 }

@@ -127,8 +127,12 @@ def test_tc_empty_sequences_are_zero(sqa):
     lens = c["seq_lens"].clone()
     lens[1] = 0
     out = torch.full_like(c["query"], float("nan"))
+    # own workspace: the unchecked call leaves SQA_DEV_SEQ_TOO_SHORT in its status word
+    ws = torch.zeros(sqa.workspace_bytes(c["query"], c["key_cache"], c["value_cache"], c["block_tables"], lens, 16,
+                                         kernel=TC, num_ctas=20, min_pages_per_cta=1),
+                     dtype=torch.uint8, device="cuda")
     sqa.small_q_attention(c["query"], c["key_cache"], c["value_cache"], c["block_tables"], lens, 16,
-                          out=out, kernel=TC, num_ctas=20, min_pages_per_cta=1)
+                          out=out, kernel=TC, num_ctas=20, min_pages_per_cta=1, workspace=ws)
     assert torch.count_nonzero(out[1]).item() == 0
     assert_close(out[0:1], ref[0:1])
     assert_close(out[2:3], ref[2:3])
