@@ -81,10 +81,15 @@ struct TcSmem {
   Schedule* sch;
 };
 
-__device__ __forceinline__ TcSmem carve(uint8_t* smem, int nb, int nb8) {
+// KV: 0 = 16-bit caches; 1 = fp8 caches converted to fp16 in shared memory;
+// 2 = fp8 caches read by the tensor core as fp8 (kind::f8f6f4).
+template <int KV>
+__host__ __device__ constexpr int ring_block_bytes() { return KV == 2 ? kBlockBytes8 : kBlockBytes; }
+
+__device__ __forceinline__ TcSmem carve(uint8_t* smem, int nb, int nb8, int ring_bytes) {
   TcSmem t;
   t.ring = smem;
-  t.stage8 = smem + (size_t)nb * kBlockBytes;
+  t.stage8 = smem + (size_t)nb * ring_bytes;
   t.merge = reinterpret_cast<float*>(t.stage8 + (size_t)nb8 * kBlockBytes8);
   t.ml = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(t.merge) + kMergeBytes);
   uint64_t* b = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(t.ml) + kMlBytes);
@@ -105,11 +110,13 @@ __device__ __forceinline__ TcSmem carve(uint8_t* smem, int nb, int nb8) {
 __device__ __forceinline__ int blocks_of(int n) { return (n + kBP - 1) / kBP; }
 
 // ------------------------------------------------------------------ producer (whole warp)
-// F8: fp8 caches land in the staging ring (full8 / empty8), one 2 KB box per page
-// per tensor; otherwise fp16 halves land in the operand ring (full / empty).
-template <bool F8>
+// KV 1: fp8 caches land in the staging ring (full8 / empty8), one 2 KB box per page
+// per tensor; KV 2: the same fp8 boxes (128-byte swizzled) land in the operand ring;
+// KV 0: fp16 halves land in the operand ring (full / empty).
+template <int KV>
 __device__ void tc_producer(const SplitKvParams& p, const Schedule& sch, const CUtensorMap* tm_k,
                             const CUtensorMap* tm_v, const TcSmem& sm, volatile int* abort) {
+  constexpr bool F8 = KV == 1;
   const int lane = threadIdx.x & 31;
   const uint64_t policy = l2_policy_evict_first();
   const int NB = F8 ? p.num_stages8 : p.num_stages;
@@ -163,9 +170,9 @@ __device__ void tc_producer(const SplitKvParams& p, const Schedule& sch, const C
             // NHD map: (dim, head, token, page); HND map: (dim, token, head, page)
             const int c1 = p.hnd ? 0 : w.h;
             const int c2 = p.hnd ? w.h : 0;
-            if constexpr (F8) {
+            if constexpr (KV != 0) {
               mbar_arrive_expect_tx(f, np * 4096);
-              const uint32_t base = smem_u32(sm.stage8 + (size_t)slot * kBlockBytes8);
+              const uint32_t base = smem_u32((F8 ? sm.stage8 : sm.ring) + (size_t)slot * kBlockBytes8);
               for (int j = 0; j < np; ++j) {  // 128 fp8 dims x 16 tokens = 2 KB per tensor
                 tma_load_4d(base + j * 2048, tm_k, f, 0, c1, c2, pages[j], policy);
                 tma_load_4d(base + kBlockBytes8 / 2 + j * 2048, tm_v, f, 0, c1, c2, pages[j], policy);
@@ -296,10 +303,13 @@ __device__ __forceinline__ void tc_mma_drain(const SplitKvParams& p, const TcSme
 
 // S(h) = Q K_h^T into slot h % kNumS, once the block's pages are in and PV(h - kNumS)
 // has released the slot; Q of a piece is in TMEM once q_ready completes.
-template <bool BF>
+// KV 2: Q is in TMEM as two e4m3 parts (high: columns 0-31, low: 32-63 of its
+// slot, 4 dims per column); S = Q_hi K^T + Q_lo K^T, eight K32 products.
+template <bool BF, int KV>
 __device__ void tc_mma_qk(const SplitKvParams& p, const Schedule& sch, const TcSmem& sm, uint32_t tmem,
                           volatile int* abort) {
-  constexpr uint32_t kIdescQK = mma_idesc_f16(128, kBlockTokens, false, false, BF);  // Q (TMEM) x K_block (K-major)
+  // Q (TMEM) x K_block (K-major); for e4m3 A and B the format fields are 0, as for fp16
+  constexpr uint32_t kIdescQK = mma_idesc_f16(128, kBlockTokens, false, false, BF);
   const int NB = p.num_stages;
   SegWalk w = first_segment(p, sch);
   int h = 0;   // CTA block counter
@@ -326,12 +336,22 @@ __device__ void tc_mma_qk(const SplitKvParams& p, const Schedule& sch, const TcS
       }
       const uint64_t t_qk = SQA_T0();
       if (elect_one()) {
-        const uint32_t k_base = smem_u32(sm.ring + (size_t)slot * kBlockBytes);
         const uint32_t d = tmem + kColS + (h % kNumS) * kSlotCols;
+        if constexpr (KV == 2) {
+          // K: 64 token rows of 128 fp8 dims (128 B, swizzled), 8-row groups 1 KB apart
+          const uint32_t k_base = smem_u32(sm.ring + (size_t)slot * kBlockBytes8);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t b = smem_desc_sw128(k_base + (kk >> 2) * kRegionBytes + (kk & 3) * 32u, 16, 1024);
-          tc_mma_ts(d, q_col + kk * 8, b, kIdescQK, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < 8; ++kk) {  // high part, then low part; 32 dims (32 B) per step
+            const uint64_t b = smem_desc_sw128(k_base + (kk & 3) * 32u, 16, 1024);
+            tc_mma_ts_f8(d, q_col + (kk >> 2) * 32 + (kk & 3) * 8, b, kIdescQK, kk > 0 ? 1u : 0u);
+          }
+        } else {
+          const uint32_t k_base = smem_u32(sm.ring + (size_t)slot * kBlockBytes);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint64_t b = smem_desc_sw128(k_base + (kk >> 2) * kRegionBytes + (kk & 3) * 32u, 16, 1024);
+            tc_mma_ts(d, q_col + kk * 8, b, kIdescQK, kk > 0 ? 1u : 0u);
+          }
         }
         tc_commit(smem_u32(sm.s_full + (h % kNumS)));
       }
@@ -349,7 +369,10 @@ __device__ void tc_mma_qk(const SplitKvParams& p, const Schedule& sch, const TcS
 
 // O += P V_g once the softmax has written P(g); then the block's ring slot and
 // S/P slot are released by commits.
-template <int R, bool BF>
+// KV 2: P is in TMEM as two e4m3 parts over all 64 tokens of the block (high:
+// columns 0-15, low: 16-31 of the S/P slot; zero outside the row's replica), so
+// four K32 products with no lane mask cover every replica at once.
+template <int R, bool BF, int KV>
 __device__ void tc_mma_pv(const SplitKvParams& p, const Schedule& sch, const TcSmem& sm, uint32_t tmem,
                           volatile int* abort) {
   constexpr uint32_t kIdescPV = mma_idesc_f16(128, 128, false, true, BF);  // P (TMEM) x V (MN-major)
@@ -371,17 +394,32 @@ __device__ void tc_mma_pv(const SplitKvParams& p, const Schedule& sch, const TcS
       tc_fence_after();
       const uint64_t t_pv = SQA_T0();
       if (elect_one()) {
-        const uint32_t v_base = smem_u32(sm.ring + (size_t)slot * kBlockBytes + 2 * kRegionBytes);
         const uint32_t p_col = tmem + kColS + (g % kNumS) * kSlotCols;
-        for (int kk = 0; kk < np; ++kk) {  // 16 tokens (one page) per step
-          const int rep = kk / kPPR;
-          uint32_t off[4];
+        if constexpr (KV == 2) {
+          // V: 64 token rows of 128 fp8 dims, one 128-byte MN atom wide; 8-row groups 1 KB apart
+          const uint32_t v_base = smem_u32(sm.ring + (size_t)slot * kBlockBytes8 + kBlockBytes8 / 2);
+          const int halves = np > 2 ? 2 : 1;  // 32 tokens per product; absent pages hold zero V
 #pragma unroll
-          for (int e = 0; e < 4; ++e) off[e] = (e * 32 >= rep * kLanesPR && e * 32 < (rep + 1) * kLanesPR) ? 0u : ~0u;
-          // MN atoms (64 dims) kRegionBytes apart: V lo -> V hi; K atoms (8 tokens) 1 KB apart
-          const uint64_t b = smem_desc_sw128(v_base + kk * 2048, kRegionBytes, 1024);
-          // a replica's first page of the piece overwrites its O rows
-          tc_mma_ts_lanes(tmem + kColO, p_col + kk * 8, b, kIdescPV, (k > 0 || (kk % kPPR) != 0) ? 1u : 0u, off);
+          for (int part = 0; part < 2; ++part) {
+            for (int hf = 0; hf < halves; ++hf) {
+              const uint64_t b = smem_desc_sw128(v_base + hf * 4096, kBlockBytes8, 1024);
+              // the piece's first product overwrites O
+              tc_mma_ts_f8(tmem + kColO, p_col + part * 16 + hf * 8, b, kIdescPV,
+                           (k > 0 || part > 0 || hf > 0) ? 1u : 0u);
+            }
+          }
+        } else {
+          const uint32_t v_base = smem_u32(sm.ring + (size_t)slot * kBlockBytes + 2 * kRegionBytes);
+          for (int kk = 0; kk < np; ++kk) {  // 16 tokens (one page) per step
+            const int rep = kk / kPPR;
+            uint32_t off[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) off[e] = (e * 32 >= rep * kLanesPR && e * 32 < (rep + 1) * kLanesPR) ? 0u : ~0u;
+            // MN atoms (64 dims) kRegionBytes apart: V lo -> V hi; K atoms (8 tokens) 1 KB apart
+            const uint64_t b = smem_desc_sw128(v_base + kk * 2048, kRegionBytes, 1024);
+            // a replica's first page of the piece overwrites its O rows
+            tc_mma_ts_lanes(tmem + kColO, p_col + kk * 8, b, kIdescPV, (k > 0 || (kk % kPPR) != 0) ? 1u : 0u, off);
+          }
         }
         tc_commit(smem_u32(sm.empty + slot));              // the block's ring slot may be refilled
         tc_commit(smem_u32(sm.pv_done + (g % kNumS)));     // S/P slot free, O up to date
@@ -398,7 +436,12 @@ __device__ void tc_mma_pv(const SplitKvParams& p, const Schedule& sch, const TcS
 }
 
 // ------------------------------------------------------------------ softmax + epilogue (4 warps)
-template <int R, bool BF>
+// KV 2 (fp8 caches read as fp8): each Q row is scaled by a power of two 2^e
+// that brings its largest magnitude into [128, 256) and split into two e4m3
+// parts, hi = e4m3(2^e q) and lo = e4m3(2^e q - hi), so S = (Q_hi + Q_lo) K^T
+// carries about 8 significant bits of q (the 2^-e is folded into the exponent's
+// scale).  P is split the same way (P <= 2^8 < 448 by the rescale rule).
+template <int R, bool BF, int KV>
 __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const TcSmem& sm, uint32_t tmem,
                            volatile int* abort) {
   constexpr int kLanesPR = 128 / R;          // lanes (rows) per replica
@@ -426,13 +469,42 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
       qv[c >> 3][4 * (c & 7) + 2] = v.z;
       qv[c >> 3][4 * (c & 7) + 3] = v.w;
     }
-    tmem_st32(tl + kColQ + qs * 64, qv[0]);
-    tmem_st32(tl + kColQ + qs * 64 + 32, qv[1]);
+    float qinv = 1.f;  // KV 2: 2^-e of this row
+    if constexpr (KV == 2) {
+      float mx = 0.f;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&qv[i >> 5][i & 31]));
+        mx = fmaxf(mx, fmaxf(fabsf(f.x), fabsf(f.y)));
+      }
+      // mx in [2^(x-127), 2^(x-126)) for biased exponent x: 2^e mx in [128, 256) for e = 134 - x
+      const int e = (mx > 0.f) ? max(-100, min(100, 134 - (int)((__float_as_uint(mx) >> 23) & 0xffu))) : 0;
+      const float sc = __uint_as_float((uint32_t)(127 + e) << 23);
+      qinv = __uint_as_float((uint32_t)(127 - e) << 23);
+      uint32_t hi[32], lo[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {  // 4 dims per column: words 2i, 2i + 1 of the row
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&qv[(2 * i) >> 5][(2 * i) & 31]));
+        const float2 c = __half22float2(*reinterpret_cast<const __half2*>(&qv[(2 * i + 1) >> 5][(2 * i + 1) & 31]));
+        const float x0 = a.x * sc, x1 = a.y * sc, x2 = c.x * sc, x3 = c.y * sc;
+        const uint32_t h01 = pack_e4m3x2(x0, x1), h23 = pack_e4m3x2(x2, x3);
+        const float2 d01 = unpack_e4m3x2(h01), d23 = unpack_e4m3x2(h23);
+        hi[i] = h01 | (h23 << 16);
+        lo[i] = pack_e4m3x2(x0 - d01.x, x1 - d01.y) | (pack_e4m3x2(x2 - d23.x, x3 - d23.y) << 16);
+      }
+      tmem_st32(tl + kColQ + qs * 64, hi);
+      tmem_st32(tl + kColQ + qs * 64 + 32, lo);
+    } else {
+      tmem_st32(tl + kColQ + qs * 64, qv[0]);
+      tmem_st32(tl + kColQ + qs * 64 + 32, qv[1]);
+    }
     tmem_wait_st();
     tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(smem_u32(sm.q_ready + qs));
+    return qinv;
   };
+  float qinv_slot[2] = {1.f, 1.f};  // KV 2: 2^-e of this thread's row in each Q slot
 
   SegWalk w = first_segment(p, sch);
   int gb0 = 0;
@@ -459,13 +531,17 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
     // Slot (pc + 1) % 2 is free: every QK product of piece pc - 1 is complete
     // (all its S blocks were consumed).
     if (pc == 0) {
-      write_q(w.b, w.h, 0);
+      qinv_slot[0] = write_q(w.b, w.h, 0);
       if (tid == 0 && p.timeline) SQA_CLK(p.timeline + (size_t)blockIdx.x * 32, 13);
     }
+    // this piece's score scale (KV 2: with the row's 2^-e)
+    const float cs = p.scale_log2 * ((pc & 1) ? qinv_slot[1] : qinv_slot[0]);
     if (seg_end < sch.end) {  // the next piece starts the next segment
       SegWalk nw = w;
       next_segment(p, nw);
-      write_q(nw.b, nw.h, (pc + 1) & 1);
+      const float qi = write_q(nw.b, nw.h, (pc + 1) & 1);
+      if ((pc + 1) & 1) qinv_slot[1] = qi;
+      else qinv_slot[0] = qi;
     }
 
     float m_used = -INFINITY, l = 0.f;
@@ -496,7 +572,7 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
         mx0 = fmaxf(mx0, __uint_as_float(sraw[t]));
         mx1 = fmaxf(mx1, __uint_as_float(sraw[t + 1]));
       }
-      const float m_new = fmaxf(m_used, fmaxf(mx0, mx1) * p.scale_log2);
+      const float m_new = fmaxf(m_used, fmaxf(mx0, mx1) * cs);
       const bool need = active && (m_new > m_used + kRescaleLog2);
       if (k == 0) {
         m_used = m_new;  // the piece's first PV of this replica overwrites its O rows
@@ -521,25 +597,66 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
         }
         tmem_wait_st();
       }
-      // p = 2^(c*s - m): one FFMA and one ex2 per score; P as fp16 pairs over
-      // this replica's columns in the first half of the block's S slot
+      // p = 2^(c*s - m): one FFMA and one ex2 per score
       const float nbase = active ? -((m_used == -INFINITY) ? 0.f : m_used) : -INFINITY;
-      const float cs = p.scale_log2;
-      uint32_t pk[kTok / 2];
       float ls[2] = {0.f, 0.f};
+      if constexpr (KV == 2) {
+        // P as e4m3 high and low parts over all 64 tokens of the block (columns
+        // 0-15 and 16-31 of the S slot, 4 tokens per column), zero outside this
+        // replica's tokens so that the PV products need no lane mask
+        constexpr int kW = kTok / 4;  // columns of this replica per part
+        uint32_t ph[kW], pl[kW];
 #pragma unroll
-      for (int t = 0; t < kTok / 2; ++t) {
-        const float p0 = ex2(fmaf(__uint_as_float(sraw[2 * t]), cs, nbase));
-        const float p1 = ex2(fmaf(__uint_as_float(sraw[2 * t + 1]), cs, nbase));
-        ls[t & 1] += p0 + p1;
-        pk[t] = pack2<BF>(p0, p1);
+        for (int t = 0; t < kW; ++t) {
+          const float p0 = ex2(fmaf(__uint_as_float(sraw[4 * t]), cs, nbase));
+          const float p1 = ex2(fmaf(__uint_as_float(sraw[4 * t + 1]), cs, nbase));
+          const float p2 = ex2(fmaf(__uint_as_float(sraw[4 * t + 2]), cs, nbase));
+          const float p3 = ex2(fmaf(__uint_as_float(sraw[4 * t + 3]), cs, nbase));
+          ls[t & 1] += (p0 + p1) + (p2 + p3);
+          // high part e4m3(p), low part e4m3(p - high) (the high part read back exactly)
+          const uint32_t h01 = pack_e4m3x2(p0, p1), h23 = pack_e4m3x2(p2, p3);
+          const float2 d01 = unpack_e4m3x2(h01), d23 = unpack_e4m3x2(h23);
+          ph[t] = h01 | (h23 << 16);
+          pl[t] = pack_e4m3x2(p0 - d01.x, p1 - d01.y) | (pack_e4m3x2(p2 - d23.x, p3 - d23.y) << 16);
+        }
+        uint32_t pw[32];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          pw[i] = (i / kW == rep) ? ph[i % kW] : 0u;
+          pw[16 + i] = (i / kW == rep) ? pl[i % kW] : 0u;
+        }
+        tmem_st32(slot_col, pw);
+      } else {
+        // P as fp16 / bf16 pairs over this replica's columns in the first half of the S slot
+        uint32_t pk[kTok / 2];
+#pragma unroll
+        for (int t = 0; t < kTok / 2; ++t) {
+          const float p0 = ex2(fmaf(__uint_as_float(sraw[2 * t]), cs, nbase));
+          const float p1 = ex2(fmaf(__uint_as_float(sraw[2 * t + 1]), cs, nbase));
+          ls[t & 1] += p0 + p1;
+          pk[t] = pack2<BF>(p0, p1);
+        }
+        if constexpr (kTok == 16) tmem_st8(slot_col + tok_lo / 2, pk);
+        else tmem_st16(slot_col + tok_lo / 2, pk);
       }
       l += ls[0] + ls[1];
-      if constexpr (kTok == 16) tmem_st8(slot_col + tok_lo / 2, pk);
-      else tmem_st16(slot_col + tok_lo / 2, pk);
       tmem_wait_st();
       const int btok = (w.pg + k * kBP) * kPageSize;
-      if (btok + np * kPageSize > len && warp == 0) {
+      if (KV == 2 && (btok + np * kPageSize > len || np < kBP) && warp == 0) {
+        // fp8 V rows (128 B, swizzled within the row only) of tokens at or past the
+        // sequence end, and of the absent pages a 32-token product still reads: zero
+        uint8_t* vreg = sm.ring + (size_t)(g % NB) * kBlockBytes8 + kBlockBytes8 / 2;
+        const int pages_read = np > 2 ? kBP : 2;
+        for (int j = 0; j < pages_read; ++j) {
+          const int first = (j < np) ? max(len - (btok + j * kPageSize), 0) : 0;
+          if (first >= kPageSize) continue;
+          for (int c = lane; c < (kPageSize - first) * 8; c += 32)
+            *reinterpret_cast<uint4*>(vreg + j * 2048 + (first + (c >> 3)) * 128 + (c & 7) * 16) =
+                make_uint4(0u, 0u, 0u, 0u);
+        }
+        fence_proxy_async_smem();
+      }
+      if (KV != 2 && btok + np * kPageSize > len && warp == 0) {
         // tokens at or past the sequence end: zero their V rows (the pool may hold NaN there)
         uint8_t* vreg = sm.ring + (size_t)(g % NB) * kBlockBytes + 2 * kRegionBytes;
         for (int j = 0; j < np; ++j) {
@@ -648,13 +765,14 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
 #endif
 }
 
-template <int R, bool BF, bool F8>
-__global__ void __launch_bounds__(kThreadsTc + (F8 ? kConvertWarps * 32 : 0), 1)
+template <int R, bool BF, int KV>
+__global__ void __launch_bounds__(kThreadsTc + (KV == 1 ? kConvertWarps * 32 : 0), 1)
     sqa_split_kv_tc_kernel(const SplitKvParams p, const __grid_constant__ CUtensorMap tm_k,
                            const __grid_constant__ CUtensorMap tm_v) {
+  constexpr bool F8 = KV == 1;  // fp8 caches through the converter warps
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const TcSmem sm = carve(smem, p.num_stages, F8 ? p.num_stages8 : 0);
+  const TcSmem sm = carve(smem, p.num_stages, F8 ? p.num_stages8 : 0, ring_block_bytes<KV>());
   const int warp = threadIdx.x >> 5;
   constexpr int kMmaWarp = kSoftmaxWarps;         // QK issuer; owns the TMEM allocation
   constexpr int kPvWarp = kSoftmaxWarps + 1;
@@ -697,7 +815,7 @@ __global__ void __launch_bounds__(kThreadsTc + (F8 ? kConvertWarps * 32 : 0), 1)
   // The PV issuer has nothing to do before the first P: it prefetches this
   // CTA's first pages into L2 before the dependency wait (hints only), off the
   // start-up path of the other warps.
-  if (warp == kPvWarp) prefetch_start<F8>(p, &tm_k, &tm_v, (F8 ? p.num_stages8 : p.num_stages) * kBP);
+  if (warp == kPvWarp) prefetch_start<KV != 0>(p, &tm_k, &tm_v, (F8 ? p.num_stages8 : p.num_stages) * kBP);
 #endif
   grid_dependency_wait();
   allow_dependent_launch();
@@ -732,15 +850,15 @@ __global__ void __launch_bounds__(kThreadsTc + (F8 ? kConvertWarps * 32 : 0), 1)
   }
 
   if (warp == kProducerWarp) {
-    tc_producer<F8>(p, s, &tm_k, &tm_v, sm, abort);
+    tc_producer<KV>(p, s, &tm_k, &tm_v, sm, abort);
   } else if (warp > kProducerWarp) {
     if constexpr (F8) tc_convert(p, s, sm, abort);
   } else if (warp == kMmaWarp) {
-    tc_mma_qk<BF>(p, s, sm, tmem, abort);
+    tc_mma_qk<BF, KV>(p, s, sm, tmem, abort);
   } else if (warp == kPvWarp) {
-    tc_mma_pv<R, BF>(p, s, sm, tmem, abort);
+    tc_mma_pv<R, BF, KV>(p, s, sm, tmem, abort);
   } else {
-    tc_softmax<R, BF>(p, s, sm, tmem, abort);
+    tc_softmax<R, BF, KV>(p, s, sm, tmem, abort);
   }
 
   tc_fence_before();
@@ -761,10 +879,10 @@ __global__ void __launch_bounds__(kThreadsTc + (F8 ? kConvertWarps * 32 : 0), 1)
 #endif
 }
 
-template <int R, bool BF, bool F8>
+template <int R, bool BF, int KV>
 cudaError_t launch_tc(const SplitKvParams& p, const CUtensorMap& tm_k, const CUtensorMap& tm_v, int grid,
                       int smem_bytes, cudaStream_t stream) {
-  auto kernel = sqa_split_kv_tc_kernel<R, BF, F8>;
+  auto kernel = sqa_split_kv_tc_kernel<R, BF, KV>;
   static int configured[64] = {0};
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
@@ -776,7 +894,7 @@ cudaError_t launch_tc(const SplitKvParams& p, const CUtensorMap& tm_k, const CUt
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kThreadsTc + (F8 ? kConvertWarps * 32 : 0));
+  cfg.blockDim = dim3(kThreadsTc + (KV == 1 ? kConvertWarps * 32 : 0));
   cfg.dynamicSmemBytes = smem_bytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -791,25 +909,29 @@ cudaError_t launch_tc(const SplitKvParams& p, const CUtensorMap& tm_k, const CUt
 
 }  // namespace
 
-int split_kv_tc_block_bytes() { return kBlockBytes; }
+int split_kv_tc_block_bytes(bool fp8_native) { return fp8_native ? kBlockBytes8 : kBlockBytes; }
 
-int split_kv_tc_smem_bytes(int num_blocks, int num_blocks8) {
-  return 1024 + num_blocks * kBlockBytes + num_blocks8 * kBlockBytes8 + kMergeBytes + kMlBytes +
-         (2 * num_blocks + 2 * num_blocks8 + 3 * kNumS + 3) * 8 + 8 + 64;
+int split_kv_tc_smem_bytes(int num_blocks, int num_blocks8, bool fp8_native) {
+  return 1024 + num_blocks * split_kv_tc_block_bytes(fp8_native) + num_blocks8 * kBlockBytes8 + kMergeBytes +
+         kMlBytes + (2 * num_blocks + 2 * num_blocks8 + 3 * kNumS + 3) * 8 + 8 + 64;
 }
 
 cudaError_t launch_split_kv_tc(const SplitKvParams& p, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
                                int grid, int smem_bytes, cudaStream_t stream) {
   const bool r4 = kGroup * p.q_len <= 32;
-  if (p.kv_fp8) {  // fp16 queries only (checked by the caller)
-    return r4 ? launch_tc<4, false, true>(p, tm_k, tm_v, grid, smem_bytes, stream)
-              : launch_tc<2, false, true>(p, tm_k, tm_v, grid, smem_bytes, stream);
+  if (p.kv_fp8 == 2) {  // fp8 caches read as fp8; fp16 queries only (checked by the caller)
+    return r4 ? launch_tc<4, false, 2>(p, tm_k, tm_v, grid, smem_bytes, stream)
+              : launch_tc<2, false, 2>(p, tm_k, tm_v, grid, smem_bytes, stream);
+  }
+  if (p.kv_fp8) {  // fp8 caches converted to fp16 in shared memory
+    return r4 ? launch_tc<4, false, 1>(p, tm_k, tm_v, grid, smem_bytes, stream)
+              : launch_tc<2, false, 1>(p, tm_k, tm_v, grid, smem_bytes, stream);
   }
   if (p.bf16)
-    return r4 ? launch_tc<4, true, false>(p, tm_k, tm_v, grid, smem_bytes, stream)
-              : launch_tc<2, true, false>(p, tm_k, tm_v, grid, smem_bytes, stream);
-  return r4 ? launch_tc<4, false, false>(p, tm_k, tm_v, grid, smem_bytes, stream)
-            : launch_tc<2, false, false>(p, tm_k, tm_v, grid, smem_bytes, stream);
+    return r4 ? launch_tc<4, true, 0>(p, tm_k, tm_v, grid, smem_bytes, stream)
+              : launch_tc<2, true, 0>(p, tm_k, tm_v, grid, smem_bytes, stream);
+  return r4 ? launch_tc<4, false, 0>(p, tm_k, tm_v, grid, smem_bytes, stream)
+            : launch_tc<2, false, 0>(p, tm_k, tm_v, grid, smem_bytes, stream);
 }
 
 }  // namespace sqa
