@@ -44,6 +44,16 @@ constexpr bool kFp8Native = true;
 #endif
 constexpr int kFp8OperandBlocks = SQA_FP8_OPERAND_BLOCKS;
 constexpr int kDefaultMinPagesPerCta = 4;
+// Schedule: a segment start costs a CTA as much as this many pages (one more
+// piece epilogue and pipeline refill; measured per kernel on B200).
+#ifndef SQA_SEGMENT_COST_TC
+#define SQA_SEGMENT_COST_TC 24
+#endif
+#ifndef SQA_SEGMENT_COST_MMA
+#define SQA_SEGMENT_COST_MMA 4
+#endif
+constexpr int kSegmentCostTc = SQA_SEGMENT_COST_TC;
+constexpr int kSegmentCostMma = SQA_SEGMENT_COST_MMA;
 
 size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 
@@ -402,6 +412,7 @@ int forward_impl(const sqa_args* a, void* workspace, size_t workspace_bytes, voi
   p.out_scale = a->out_scale != 0.f ? a->out_scale : 1.f;
   p.kv_fp8 = fp8_mode;
   p.num_stages8 = pl.stages8;
+  p.seg_cost = pl.tc ? kSegmentCostTc : kSegmentCostMma;
 
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_ptr);
   if (ev_before && cudaEventRecord(reinterpret_cast<cudaEvent_t>(ev_before), stream) != cudaSuccess)

@@ -59,6 +59,7 @@ struct SplitKvParams {
   int kv_fp8;                   // caches hold fp8 e4m3 (tcgen05 kernel): 1 converted to fp16 in shared
                                 // memory, 2 read as fp8 by the tensor core
   int num_stages8;              // tcgen05 kernel, kv_fp8: blocks in the fp8 staging ring
+  int seg_cost;                 // schedule: units a segment start costs a CTA (one more epilogue)
 };
 
 struct MergeParams {

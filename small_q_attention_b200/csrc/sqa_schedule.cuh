@@ -2,9 +2,12 @@
 //
 // One unit is one 16-token page of one KV head of one sequence; the units of
 // (b, kvh) form segment s = b * Hkv + kvh.  All units are laid end to end and
-// cut into gridDim.x equal ranges, one per CTA; each (CTA, segment) overlap is
-// a "piece".  Warp 0 of every CTA derives its range from seq_lens with a warp
-// scan, so the host never synchronises.
+// cut into gridDim.x ranges of equal cost, one per CTA; each (CTA, segment)
+// overlap is a "piece".  The cost of a range is its units plus p.seg_cost for
+// every segment that starts in it: a CTA that crosses into a new segment pays
+// one more piece epilogue and a pipeline refill, so it gets fewer pages.  Warp
+// 0 of every CTA derives its range from seq_lens with a warp scan, so the host
+// never synchronises.
 #pragma once
 
 #include "sqa_internal.h"
@@ -18,7 +21,14 @@ struct SegWalk {
   int pg;         // first page of the current piece within the segment
   int pages;      // pages of sequence b (clamped to the table width)
   int seg_start;  // global unit index of (b, h, page 0)
+  int ne;         // index of this segment among the segments with pages
 };
+
+// Cost position of the unit `off` units into the segment with non-empty index
+// `ne` that starts at unit `seg_start`.
+__device__ __forceinline__ long long unit_cost(const SplitKvParams& p, int seg_start, int ne, int off) {
+  return (long long)seg_start + (long long)p.seg_cost * (ne + 1) + off;
+}
 
 // kSpec: a read before the dependency wait, through L2 only (ld.global.cg), so
 // that no possibly stale line is left in L1 for the reads after the wait.
@@ -36,6 +46,7 @@ __device__ __forceinline__ int seq_pages(const SplitKvParams& p, int b) {
 __device__ __forceinline__ void next_segment(const SplitKvParams& p, SegWalk& w) {
   w.seg_start += w.pages;
   w.pg = 0;
+  ++w.ne;
   if (++w.h == p.hkv) {
     w.h = 0;
     do {
@@ -48,9 +59,10 @@ __device__ __forceinline__ void next_segment(const SplitKvParams& p, SegWalk& w)
 // Shared schedule, filled by warp 0 before the CTA-wide barrier.
 struct Schedule {
   int start, end;      // this CTA's unit range
-  int per_cta;         // units per CTA
+  int per_cta;         // cost per CTA (units + p.seg_cost per segment start)
   int b0, u_b0;        // sequence containing `start` and the units before it
   int pages_b0;        // pages of sequence b0
+  int ne_b0;           // segments with pages before sequence b0
   int abort;           // set by a timed-out wait
 };
 
@@ -94,15 +106,29 @@ __device__ __forceinline__ Schedule compute_schedule(const SplitKvParams& p) {
     if (blockIdx.x == 0 && lane == 0 && flags) atomicOr(p.status, flags);
   }
 
-  const int total = total_pages * p.hkv;
-  const int per = max(1, (total + (int)gridDim.x - 1) / (int)gridDim.x);
-  const int start = min(total, (int)blockIdx.x * per);
-  const int end = min(total, start + per);
+  // cost of sequence b: Hkv segments of (pages + seg_cost) when it has pages
+  const long long seg_cost = p.seg_cost;
+  long long total_cost = 0;
+  int nonempty = 0;
+#pragma unroll
+  for (int c = 0; c < kCachedChunks; ++c) nonempty += __popc(__ballot_sync(0xffffffffu, cached[c] > 0));
+  for (int base = kCachedChunks * 32; base < p.batch; base += 32) {
+    unsigned int unused = 0;
+    nonempty += __popc(__ballot_sync(0xffffffffu, pages_of(base + lane, unused) > 0));
+  }
+  total_cost = ((long long)total_pages + seg_cost * nonempty) * p.hkv;
+  const long long per = max(1LL, (total_cost + gridDim.x - 1) / gridDim.x);
+  const long long x0 = min(total_cost, (long long)blockIdx.x * per);
+  const long long x1 = min(total_cost, x0 + per);
 
-  // Sequence containing unit `start`: first b whose inclusive unit prefix exceeds it.
-  int b0 = p.batch, u_b0 = 0, pages_b0 = 0;
-  if (start < end) {
-    int running = 0;  // units before this 32-sequence block
+  // Locate both ends: the sequence whose cost span holds x, then the head and the
+  // unit offset (cost positions in a segment's first seg_cost map to its start).
+  int start = total_pages * p.hkv, end = total_pages * p.hkv;
+  int b0 = p.batch, u_b0 = 0, pages_b0 = 0, ne_b0 = 0;
+  if (x0 < x1) {
+    long long run_cost = 0;
+    int run_units = 0, run_ne = 0;
+    bool found0 = false;
     for (int base = 0; base < p.batch; base += 32) {
       const int c = base / 32;
       int pg = 0;
@@ -113,31 +139,63 @@ __device__ __forceinline__ Schedule compute_schedule(const SplitKvParams& p) {
         unsigned int unused = 0;
         pg = pages_of(base + lane, unused);
       }
-      const int units = pg * p.hkv;
-      int incl = units;
+      const long long cost = pg > 0 ? (long long)(pg + seg_cost) * p.hkv : 0;
+      long long incl = cost;
+      int incl_u = pg * p.hkv, incl_ne = pg > 0 ? 1 : 0;
 #pragma unroll
       for (int off = 1; off < 32; off <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, incl, off);
-        if (lane >= off) incl += y;
+        const long long y = __shfl_up_sync(0xffffffffu, incl, off);
+        const int yu = __shfl_up_sync(0xffffffffu, incl_u, off);
+        const int yn = __shfl_up_sync(0xffffffffu, incl_ne, off);
+        if (lane >= off) {
+          incl += y;
+          incl_u += yu;
+          incl_ne += yn;
+        }
       }
-      const unsigned hit = __ballot_sync(0xffffffffu, running + incl > start);
-      if (hit) {
-        const int l = __ffs(hit) - 1;
-        b0 = base + l;
-        u_b0 = running + __shfl_sync(0xffffffffu, incl - units, l);
-        pages_b0 = __shfl_sync(0xffffffffu, pg, l);
-        break;
+      // unit position of cost x inside this lane's sequence
+      auto unit_at = [&](long long x) {
+        const long long xr = x - (run_cost + incl - cost);  // cost into this sequence
+        const long long span = pg + seg_cost;
+        const long long h = xr / span;
+        const long long r = xr - h * span;
+        return run_units + (incl_u - pg * p.hkv) + (int)(h * pg + max(r - seg_cost, 0LL));
+      };
+      if (!found0) {
+        const unsigned hit = __ballot_sync(0xffffffffu, run_cost + incl > x0);
+        if (hit) {
+          const int l = __ffs(hit) - 1;
+          const int st = unit_at(x0);
+          start = __shfl_sync(0xffffffffu, st, l);
+          b0 = base + l;
+          u_b0 = run_units + __shfl_sync(0xffffffffu, incl_u - pg * p.hkv, l);
+          pages_b0 = __shfl_sync(0xffffffffu, pg, l);
+          ne_b0 = (run_ne + __shfl_sync(0xffffffffu, incl_ne - (pg > 0 ? 1 : 0), l)) * p.hkv;
+          found0 = true;
+        }
       }
-      running += __shfl_sync(0xffffffffu, incl, 31);
+      if (found0) {
+        const unsigned hit = __ballot_sync(0xffffffffu, run_cost + incl > x1);
+        if (hit) {
+          const int l = __ffs(hit) - 1;
+          const int en = unit_at(x1);
+          end = __shfl_sync(0xffffffffu, en, l);
+          break;
+        }
+      }
+      run_cost += __shfl_sync(0xffffffffu, incl, 31);
+      run_units += __shfl_sync(0xffffffffu, incl_u, 31);
+      run_ne += __shfl_sync(0xffffffffu, incl_ne, 31);
     }
   }
   Schedule s;
   s.start = start;
-  s.end = end;
-  s.per_cta = per;
+  s.end = max(start, end);
+  s.per_cta = (int)per;
   s.b0 = b0;
   s.u_b0 = u_b0;
   s.pages_b0 = pages_b0;
+  s.ne_b0 = ne_b0;
   s.abort = 0;
   return s;
 }
@@ -156,6 +214,7 @@ __device__ __forceinline__ SegWalk first_segment(const SplitKvParams& p, const S
   w.h = off / w.pages;
   w.pg = off - w.h * w.pages;
   w.seg_start = s.u_b0 + w.h * w.pages;
+  w.ne = s.ne_b0 + w.h;
   return w;
 }
 

@@ -2,8 +2,9 @@
 //
 // Work decomposition.  One "unit" is one 16-token page of one KV head of one
 // sequence; the units of (b, kvh) form segment s = b * Hkv + kvh.  All units
-// are laid end to end and cut into gridDim.x equal ranges, one per CTA, so
-// every CTA streams the same number of K/V bytes whatever the mix of lengths
+// are laid end to end and cut into gridDim.x ranges of equal cost (units plus
+// a fixed charge per segment start, sqa_schedule.cuh), one per CTA, so every
+// CTA streams about the same number of K/V bytes whatever the mix of lengths
 // (a ragged batch balances like a uniform one).  A CTA range may end inside a
 // segment or cover several short ones; each (CTA, segment) overlap is a
 // "piece".  A piece that is a whole segment writes the final output directly;
@@ -186,7 +187,7 @@ __device__ void consumer_loop(const SplitKvParams& p, const Schedule& sch, uint8
     const int n = min(sch.end, seg_end) - unit;
     const bool whole = (unit == w.seg_start) && (seg_end <= sch.end);
     if (tid == 0 && unit == w.seg_start && SQA_CHECK(s < p.batch * p.hkv, p.status, 7, s)) {
-      const int last_cta = (seg_end - 1) / sch.per_cta;
+      const int last_cta = (int)(unit_cost(p, w.seg_start, w.ne, w.pages - 1) / sch.per_cta);
       p.seg_info[s] = make_int2((int)blockIdx.x + s, last_cta - (int)blockIdx.x + 1);
     }
 

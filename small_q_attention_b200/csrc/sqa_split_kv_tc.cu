@@ -517,7 +517,7 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
     const int nblk = blocks_of(n);
     const bool whole = (unit == w.seg_start) && (seg_end <= sch.end);
     if (tid == 0 && unit == w.seg_start) {
-      const int last_cta = (seg_end - 1) / sch.per_cta;
+      const int last_cta = (int)(unit_cost(p, w.seg_start, w.ne, w.pages - 1) / sch.per_cta);
       p.seg_info[s] = make_int2((int)blockIdx.x + s, last_cta - (int)blockIdx.x + 1);
     }
     const int len_raw = __ldg(p.seq_lens + w.b);
