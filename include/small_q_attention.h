@@ -130,7 +130,7 @@ typedef struct sqa_args {
    * ([num_pages, 2, ...]); a multiple of 8 (16-byte aligned pages). */
   int64_t page_stride;
   /* Element type of key_cache / value_cache: SQA_KV_SAME (as dtype) or
-   * SQA_KV_FP8_E4M3 (1 byte, with fp16 queries and output; tcgen05 kernel).
+   * SQA_KV_FP8_E4M3 (1 byte, with fp16 or bf16 queries and output; tcgen05 kernel).
    * The tensor core reads the fp8 K/V as they are (kind::f8f6f4); each query
    * row (scaled by a power of two) and each probability enter as the sum of
    * two e4m3 parts, about 8 significant bits (measured max error 0.3 of the

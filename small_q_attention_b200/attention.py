@@ -122,8 +122,8 @@ def _check_inputs(query, key_cache, value_cache, block_tables, seq_lens, page_si
     _cache_page_stride(key_cache, value_cache)
     qd = query.dtype
     kd = key_cache.dtype
-    if qd not in _DTYPES or value_cache.dtype != kd or not (kd == qd or (kd == _FP8 and qd == torch.float16)):
-        raise ValueError("the kernel requires FP16 (or BF16) Q/K/V of one type, or FP16 Q with FP8-E4M3 K/V")
+    if qd not in _DTYPES or value_cache.dtype != kd or not (kd == qd or (kd == _FP8 and _FP8 is not None)):
+        raise ValueError("the kernel requires FP16 (or BF16) Q/K/V of one type, or FP16/BF16 Q with FP8-E4M3 K/V")
     for t in tensors[3:]:
         if t.dtype != torch.int32:
             raise ValueError("block_tables, seq_lens and mask_lens must be int32")
@@ -278,9 +278,10 @@ def small_q_attention(query, key_cache, value_cache, block_tables, seq_lens, pag
     """Causal paged MTP attention; returns ``[batch, q_len, Hq, 128]`` in the input type.
 
     Q/K/V are FP16 (the upstream contract) or BF16 (all three of one type;
-    accumulation is FP32 either way), or FP16 Q with FP8-E4M3 K/V (tcgen05
-    kernel; the fp8 values enter exactly: pass the caches' dequantisation scales
-    as ``sm_scale = k_scale / sqrt(128)`` and ``out_scale = v_scale``).
+    accumulation is FP32 either way), or FP16/BF16 Q with FP8-E4M3 K/V (tcgen05
+    kernel, read as fp8 by the tensor core; Q and the probabilities enter as
+    two e4m3 parts each; pass the caches' dequantisation scales as
+    ``sm_scale = k_scale / sqrt(128)`` and ``out_scale = v_scale``).
 
     ``seq_lens[b]`` is the KV length including the ``q_len`` draft tokens and
     draft row ``qi`` sees tokens ``< seq_lens[b] - q_len + qi + 1``

@@ -197,7 +197,11 @@ int validate(const sqa_args* a) {
   if (a->kv_layout != SQA_KV_NHD && a->kv_layout != SQA_KV_HND) return SQA_ERR_UNSUPPORTED;
   if (a->kv_dtype != SQA_KV_SAME && a->kv_dtype != SQA_KV_FP8_E4M3) return SQA_ERR_UNSUPPORTED;
   // fp8 caches: fp16 queries, tcgen05 kernel
-  if (a->kv_dtype == SQA_KV_FP8_E4M3 && (a->dtype != SQA_DTYPE_F16 || a->kernel == 1)) return SQA_ERR_UNSUPPORTED;
+  // fp8 caches run on the tcgen05 kernel; read as fp8 they take fp16 or bf16 queries,
+  // converted to fp16 in shared memory (-DSQA_FP8_CONVERT) fp16 queries only
+  if (a->kv_dtype == SQA_KV_FP8_E4M3 &&
+      (a->kernel == 1 || (a->dtype != SQA_DTYPE_F16 && !(kFp8Native && a->dtype == SQA_DTYPE_BF16))))
+    return SQA_ERR_UNSUPPORTED;
   // a page must hold 16 x Hkv x 128 elements and start 16-byte aligned (TMA strides)
   const int64_t align_elems = a->kv_dtype == SQA_KV_FP8_E4M3 ? 16 : 8;
   if (a->page_stride < 0 || (a->page_stride > 0 && (a->page_stride < (int64_t)kPageSize * a->num_kv_heads * kHeadDim ||

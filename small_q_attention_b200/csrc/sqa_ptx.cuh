@@ -299,6 +299,16 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   else return pack_half2(lo, hi);
 }
 
+// Two fp16 (BF = false) or bf16 values packed low-first in a 32-bit word -> two floats.
+template <bool BF>
+__device__ __forceinline__ float2 unpack2(uint32_t w) {
+  if constexpr (BF) {
+    return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+  } else {
+    return __half22float2(*reinterpret_cast<const __half2*>(&w));
+  }
+}
+
 // Programmatic dependent launch.  grid_dependency_wait() blocks until the
 // preceding kernel in the stream has completed and its memory is visible (a
 // no-op when the launch had no programmatic dependency); every global read of

@@ -308,8 +308,9 @@ __device__ __forceinline__ void tc_mma_drain(const SplitKvParams& p, const TcSme
 template <bool BF, int KV>
 __device__ void tc_mma_qk(const SplitKvParams& p, const Schedule& sch, const TcSmem& sm, uint32_t tmem,
                           volatile int* abort) {
-  // Q (TMEM) x K_block (K-major); for e4m3 A and B the format fields are 0, as for fp16
-  constexpr uint32_t kIdescQK = mma_idesc_f16(128, kBlockTokens, false, false, BF);
+  // Q (TMEM) x K_block (K-major).  Format field 0 is fp16 for kind::f16 and e4m3 for
+  // kind::f8f6f4 (where 1 would be e5m2): KV 2 is e4m3 whatever the query type.
+  constexpr uint32_t kIdescQK = mma_idesc_f16(128, kBlockTokens, false, false, BF && KV != 2);
   const int NB = p.num_stages;
   SegWalk w = first_segment(p, sch);
   int h = 0;   // CTA block counter
@@ -375,7 +376,8 @@ __device__ void tc_mma_qk(const SplitKvParams& p, const Schedule& sch, const TcS
 template <int R, bool BF, int KV>
 __device__ void tc_mma_pv(const SplitKvParams& p, const Schedule& sch, const TcSmem& sm, uint32_t tmem,
                           volatile int* abort) {
-  constexpr uint32_t kIdescPV = mma_idesc_f16(128, 128, false, true, BF);  // P (TMEM) x V (MN-major)
+  // P (TMEM) x V (MN-major); KV 2: e4m3 whatever the query type (format field 0)
+  constexpr uint32_t kIdescPV = mma_idesc_f16(128, 128, false, true, BF && KV != 2);
   constexpr int kPPR = kBP / R;       // pages of a block per replica
   constexpr int kLanesPR = 128 / R;   // TMEM lanes per replica
   const int NB = p.num_stages;
@@ -474,7 +476,7 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
       float mx = 0.f;
 #pragma unroll
       for (int i = 0; i < 64; ++i) {
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&qv[i >> 5][i & 31]));
+        const float2 f = unpack2<BF>(qv[i >> 5][i & 31]);
         mx = fmaxf(mx, fmaxf(fabsf(f.x), fabsf(f.y)));
       }
       // mx in [2^(x-127), 2^(x-126)) for biased exponent x: 2^e mx in [128, 256) for e = 134 - x
@@ -484,8 +486,8 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
       uint32_t hi[32], lo[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {  // 4 dims per column: words 2i, 2i + 1 of the row
-        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&qv[(2 * i) >> 5][(2 * i) & 31]));
-        const float2 c = __half22float2(*reinterpret_cast<const __half2*>(&qv[(2 * i + 1) >> 5][(2 * i + 1) & 31]));
+        const float2 a = unpack2<BF>(qv[(2 * i) >> 5][(2 * i) & 31]);
+        const float2 c = unpack2<BF>(qv[(2 * i + 1) >> 5][(2 * i + 1) & 31]);
         const float x0 = a.x * sc, x1 = a.y * sc, x2 = c.x * sc, x3 = c.y * sc;
         const uint32_t h01 = pack_e4m3x2(x0, x1), h23 = pack_e4m3x2(x2, x3);
         const float2 d01 = unpack_e4m3x2(h01), d23 = unpack_e4m3x2(h23);
@@ -919,7 +921,10 @@ int split_kv_tc_smem_bytes(int num_blocks, int num_blocks8, bool fp8_native) {
 cudaError_t launch_split_kv_tc(const SplitKvParams& p, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
                                int grid, int smem_bytes, cudaStream_t stream) {
   const bool r4 = kGroup * p.q_len <= 32;
-  if (p.kv_fp8 == 2) {  // fp8 caches read as fp8; fp16 queries only (checked by the caller)
+  if (p.kv_fp8 == 2) {  // fp8 caches read as fp8; fp16 or bf16 queries
+    if (p.bf16)
+      return r4 ? launch_tc<4, true, 2>(p, tm_k, tm_v, grid, smem_bytes, stream)
+                : launch_tc<2, true, 2>(p, tm_k, tm_v, grid, smem_bytes, stream);
     return r4 ? launch_tc<4, false, 2>(p, tm_k, tm_v, grid, smem_bytes, stream)
               : launch_tc<2, false, 2>(p, tm_k, tm_v, grid, smem_bytes, stream);
   }

@@ -16,9 +16,10 @@ the output.
 
 Supported subset (anything else raises ``ValueError``): uniform
 ``q_len_per_req`` in 1..16, page size 16, head dim 128, GQA group 4, fp16 or
-bf16 query/cache/output of one type, float scales, ``window_left=-1``, no
-sinks, no custom mask, no variable query lengths, no nvfp4/fp8 scale-factor
-tensors, one shared page table for K and V.  ``backend`` and ``enable_pdl`` are
+bf16 query and output, a cache of the query's type or fp8-e4m3 (its
+dequantisation scales folded into ``bmm1_scale`` / ``bmm2_scale``, as FlashInfer
+does), float scales, ``window_left=-1``, no sinks, no custom mask, no variable
+query lengths, no nvfp4 scale-factor tensors, one shared page table for K and V.  ``backend`` and ``enable_pdl`` are
 accepted and ignored (the kernels always use programmatic dependent launch).
 """
 

@@ -111,6 +111,38 @@ def test_fp8_contract(sqa):
     args = (c["key_cache"], c["value_cache"], c["block_tables"], c["seq_lens"], 16)
     with pytest.raises(ValueError):  # the warp-level kernel has no fp8 path
         sqa.small_q_attention(c["query"], *args, kernel=1)
-    with pytest.raises(ValueError):  # fp8 caches take fp16 queries
-        sqa.small_q_attention(c["query"].to(torch.bfloat16), *args)
+    with pytest.raises(ValueError):  # fp32 queries are not a path type
+        sqa.small_q_attention(c["query"].float(), *args)
     assert sqa.selected_kernel(c["query"], *args) == 2
+
+
+@pytest.mark.parametrize("q_len,lens,hkv", [(2, [33, 1024], 8), (8, [2048, 8, 9, 300], 2), (16, [16, 31, 4096], 8)])
+def test_fp8_bf16_queries(sqa, q_len, lens, hkv):
+    """BF16 queries (and output) with FP8 K/V: a BF16 model with an FP8 cache."""
+    c = case_fp8(q_len, lens, hkv=hkv, seed=q_len * 31 + len(lens))
+    q = c["query"].to(torch.bfloat16)
+    out = sqa.small_q_attention(q, c["key_cache"], c["value_cache"], c["block_tables"], c["seq_lens"], 16,
+                                check=True)
+    assert out.dtype == torch.bfloat16
+    assert_close(out, oracle(dict(c, query=q.float())))
+
+
+def test_fp8_flashinfer_entry(sqa):
+    """The FlashInfer-compatible entry with an fp8 cache ([pages, 2, Hkv, 16, 128]) and BF16 queries, the
+    dequantisation scales folded into bmm1_scale / bmm2_scale."""
+    from small_q_attention_b200.flashinfer_compat import trtllm_batch_decode_with_kv_cache
+
+    q_len = 4
+    c = case_fp8(q_len, [100, 2000, 8192], seed=13)
+    hnd = lambda t: t.view(torch.uint8).permute(0, 2, 1, 3).contiguous()  # noqa: E731
+    kv = torch.stack([hnd(c["key_cache"]), hnd(c["value_cache"])], dim=1).contiguous().view(F8)
+    b = c["query"].shape[0]
+    query = c["query"].to(torch.bfloat16).reshape(b * q_len, 32, 128)
+    ws = torch.zeros(128 << 20, dtype=torch.uint8, device="cuda")
+    k_scale, v_scale = 0.5, 2.0
+    out = trtllm_batch_decode_with_kv_cache(query, kv, ws, c["block_tables"], c["seq_lens"], max(c["lens"]),
+                                            bmm1_scale=k_scale / math.sqrt(128), bmm2_scale=v_scale,
+                                            kv_layout="HND", q_len_per_req=q_len)
+    assert out.dtype == torch.bfloat16 and out.shape == query.shape
+    ref = oracle(dict(c, query=c["query"].to(torch.bfloat16).float()), k_scale, v_scale)
+    assert_close(out.view(c["query"].shape), ref)
