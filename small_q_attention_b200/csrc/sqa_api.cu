@@ -181,7 +181,7 @@ struct Plan {
   int segments;
   int pieces;
   int stages8 = 0;
-  size_t off_seg, off_lse, off_o, off_timeline = 0, bytes;
+  size_t off_lse, off_o, off_timeline = 0, bytes;
 };
 
 int validate(const sqa_args* a) {
@@ -292,8 +292,7 @@ int make_plan(const sqa_args* a, int device, Plan* plan) {
   pl.grid = (int)grid;
   pl.pieces = pl.grid + pl.segments;  // piece index = cta + segment < grid + segments - 1
 
-  pl.off_seg = kAlign;  // [0, 256): device status word
-  pl.off_lse = align_up(pl.off_seg + (size_t)pl.segments * sizeof(int2));
+  pl.off_lse = kAlign;  // [0, 256): device status word
   pl.off_o = align_up(pl.off_lse + (size_t)pl.pieces * pl.shape.rows_pad * sizeof(float));
   pl.bytes = align_up(pl.off_o + (size_t)pl.pieces * pl.shape.rows_pad * kHeadDim * sizeof(float));
 #ifdef SQA_DEBUG_TIMELINE
@@ -398,7 +397,6 @@ int forward_impl(const sqa_args* a, void* workspace, size_t workspace_bytes, voi
   p.out_lse = a->out_lse;
   p.ws_o = reinterpret_cast<float*>(ws + pl.off_o);
   p.ws_lse = reinterpret_cast<float*>(ws + pl.off_lse);
-  p.seg_info = reinterpret_cast<int2*>(ws + pl.off_seg);
   p.status = reinterpret_cast<unsigned int*>(ws);
   p.batch = a->batch;
   p.q_len = a->q_len;
@@ -431,7 +429,6 @@ int forward_impl(const sqa_args* a, void* workspace, size_t workspace_bytes, voi
   MergeParams m;
   m.parts_o = p.ws_o;
   m.parts_lse = p.ws_lse;
-  m.seg_info = p.seg_info;
   m.seq_lens = a->seq_lens;
   m.out = p.out;
   m.out_o = p.out_o;
@@ -447,6 +444,8 @@ int forward_impl(const sqa_args* a, void* workspace, size_t workspace_bytes, voi
   m.hkv = a->num_kv_heads;
   m.max_pages = a->max_pages;
   m.bf16 = p.bf16;
+  m.split_grid = pl.grid;
+  m.seg_cost = p.seg_cost;
   if (launch_segment_merge(m, pl.shape.rows_pad, stream) != cudaSuccess) return SQA_ERR_CUDA;
   if (!debug_sync(stream, "merge kernel", pl.segments, 0, a)) return SQA_ERR_CUDA;
   return SQA_OK;

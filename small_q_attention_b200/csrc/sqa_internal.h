@@ -45,7 +45,6 @@ struct SplitKvParams {
   float* out_lse;               // partial mode
   float* ws_o;                  // [pieces, rows_pad, 128]
   float* ws_lse;                // [pieces, rows_pad]
-  int2* seg_info;               // [B * Hkv]: (first piece index, piece count)
   unsigned int* status;
   int batch, q_len, hq, hkv, max_pages, num_pages;
   int num_stages;
@@ -65,7 +64,6 @@ struct SplitKvParams {
 struct MergeParams {
   const float* parts_o;         // piece i, row r at parts_o + (i * piece_rows + r) * 128 (+ first offset)
   const float* parts_lse;
-  const int2* seg_info;         // nullptr: every segment has pieces [0, num_parts)
   const int32_t* seq_lens;      // per-call merge: empty sequences are written as 0 / -inf
   unsigned int* status;         // per-call merge: device status word
   unsigned long long* timeline; // -DSQA_DEBUG_TIMELINE: 4 stamps per merge CTA, else nullptr
@@ -77,6 +75,7 @@ struct MergeParams {
   int piece_rows;               // rows per piece (rows_pad for the per-call merge)
   int batch, q_len, hq, hkv, max_pages;
   int bf16;                     // out holds bf16 (else fp16)
+  int split_grid, seg_cost;     // per-call merge: the split-KV launch's schedule (pieces of a segment)
 };
 
 // Launchers (stream-ordered, no allocation).  Return cudaGetLastError().

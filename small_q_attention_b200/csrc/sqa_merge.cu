@@ -10,11 +10,16 @@
 #include "sqa_internal.h"
 #include "sqa_merge_row.cuh"
 #include "sqa_ptx.cuh"
+#include "sqa_schedule.cuh"
 
 namespace sqa {
 namespace {
 
 // Per-call merge: grid (B * Hkv, ceil(4 * q_len / 4)), 4 warps = 4 rows per CTA.
+// Before its dependency wait each warp works out its segment's pieces from
+// seq_lens (an input the split kernel does not write: final before that kernel
+// started) with the split kernel's own schedule; after the wait one round trip
+// brings the partials.
 __global__ void __launch_bounds__(128) sqa_segment_merge_kernel(const MergeParams p) {
   unsigned long long* tl =
       p.timeline ? p.timeline + ((size_t)blockIdx.y * gridDim.x + blockIdx.x) * 4 : nullptr;
@@ -23,11 +28,12 @@ __global__ void __launch_bounds__(128) sqa_segment_merge_kernel(const MergeParam
   // it touches memory, and until then its CTAs take SMs as the split-KV CTAs
   // leave them (and prefetch).
   allow_dependent_launch();
-  grid_dependency_wait();    // the split-KV grid has finished writing the partials
-  if (threadIdx.x == 0) SQA_STAMP(tl, 1);
   const int s = blockIdx.x;
   const int b = s / p.hkv;
   const int h = s - b * p.hkv;
+  const int2 info = segment_pieces(p.seq_lens, p.batch, p.max_pages, p.hkv, p.seg_cost, p.split_grid, b, h);
+  grid_dependency_wait();    // the split-KV grid has finished writing the partials
+  if (threadIdx.x == 0) SQA_STAMP(tl, 1);
   const int rows = kGroup * p.q_len;
   const int row = blockIdx.y * 4 + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -37,10 +43,7 @@ __global__ void __launch_bounds__(128) sqa_segment_merge_kernel(const MergeParam
   float* out_o = p.out_o ? p.out_o + out_row * kHeadDim : nullptr;
   float* out_lse = p.out_lse ? p.out_lse + out_row : nullptr;
 
-  // both loads in flight together
-  const int2 info = p.seg_info[s];
-  const int len = max(__ldg(p.seq_lens + b), 0);
-  if (len == 0) {  // no page was processed for this sequence: nothing is visible
+  if (info.y == 0) {  // no page was processed for this sequence: nothing is visible
     if (out) reinterpret_cast<uint2*>(out)[lane] = make_uint2(0u, 0u);  // +0 in fp16 and bf16
     if (out_o) reinterpret_cast<float4*>(out_o)[lane] = make_float4(0.f, 0.f, 0.f, 0.f);
     if (out_lse && lane == 0) *out_lse = -INFINITY;

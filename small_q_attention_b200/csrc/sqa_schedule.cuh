@@ -21,14 +21,7 @@ struct SegWalk {
   int pg;         // first page of the current piece within the segment
   int pages;      // pages of sequence b (clamped to the table width)
   int seg_start;  // global unit index of (b, h, page 0)
-  int ne;         // index of this segment among the segments with pages
 };
-
-// Cost position of the unit `off` units into the segment with non-empty index
-// `ne` that starts at unit `seg_start`.
-__device__ __forceinline__ long long unit_cost(const SplitKvParams& p, int seg_start, int ne, int off) {
-  return (long long)seg_start + (long long)p.seg_cost * (ne + 1) + off;
-}
 
 // kSpec: a read before the dependency wait, through L2 only (ld.global.cg), so
 // that no possibly stale line is left in L1 for the reads after the wait.
@@ -46,7 +39,6 @@ __device__ __forceinline__ int seq_pages(const SplitKvParams& p, int b) {
 __device__ __forceinline__ void next_segment(const SplitKvParams& p, SegWalk& w) {
   w.seg_start += w.pages;
   w.pg = 0;
-  ++w.ne;
   if (++w.h == p.hkv) {
     w.h = 0;
     do {
@@ -62,7 +54,6 @@ struct Schedule {
   int per_cta;         // cost per CTA (units + p.seg_cost per segment start)
   int b0, u_b0;        // sequence containing `start` and the units before it
   int pages_b0;        // pages of sequence b0
-  int ne_b0;           // segments with pages before sequence b0
   int abort;           // set by a timed-out wait
 };
 
@@ -124,10 +115,10 @@ __device__ __forceinline__ Schedule compute_schedule(const SplitKvParams& p) {
   // Locate both ends: the sequence whose cost span holds x, then the head and the
   // unit offset (cost positions in a segment's first seg_cost map to its start).
   int start = total_pages * p.hkv, end = total_pages * p.hkv;
-  int b0 = p.batch, u_b0 = 0, pages_b0 = 0, ne_b0 = 0;
+  int b0 = p.batch, u_b0 = 0, pages_b0 = 0;
   if (x0 < x1) {
     long long run_cost = 0;
-    int run_units = 0, run_ne = 0;
+    int run_units = 0;
     bool found0 = false;
     for (int base = 0; base < p.batch; base += 32) {
       const int c = base / 32;
@@ -141,16 +132,14 @@ __device__ __forceinline__ Schedule compute_schedule(const SplitKvParams& p) {
       }
       const long long cost = pg > 0 ? (long long)(pg + seg_cost) * p.hkv : 0;
       long long incl = cost;
-      int incl_u = pg * p.hkv, incl_ne = pg > 0 ? 1 : 0;
+      int incl_u = pg * p.hkv;
 #pragma unroll
       for (int off = 1; off < 32; off <<= 1) {
         const long long y = __shfl_up_sync(0xffffffffu, incl, off);
         const int yu = __shfl_up_sync(0xffffffffu, incl_u, off);
-        const int yn = __shfl_up_sync(0xffffffffu, incl_ne, off);
         if (lane >= off) {
           incl += y;
           incl_u += yu;
-          incl_ne += yn;
         }
       }
       // unit position of cost x inside this lane's sequence
@@ -170,7 +159,6 @@ __device__ __forceinline__ Schedule compute_schedule(const SplitKvParams& p) {
           b0 = base + l;
           u_b0 = run_units + __shfl_sync(0xffffffffu, incl_u - pg * p.hkv, l);
           pages_b0 = __shfl_sync(0xffffffffu, pg, l);
-          ne_b0 = (run_ne + __shfl_sync(0xffffffffu, incl_ne - (pg > 0 ? 1 : 0), l)) * p.hkv;
           found0 = true;
         }
       }
@@ -185,7 +173,6 @@ __device__ __forceinline__ Schedule compute_schedule(const SplitKvParams& p) {
       }
       run_cost += __shfl_sync(0xffffffffu, incl, 31);
       run_units += __shfl_sync(0xffffffffu, incl_u, 31);
-      run_ne += __shfl_sync(0xffffffffu, incl_ne, 31);
     }
   }
   Schedule s;
@@ -195,7 +182,6 @@ __device__ __forceinline__ Schedule compute_schedule(const SplitKvParams& p) {
   s.b0 = b0;
   s.u_b0 = u_b0;
   s.pages_b0 = pages_b0;
-  s.ne_b0 = ne_b0;
   s.abort = 0;
   return s;
 }
@@ -214,8 +200,59 @@ __device__ __forceinline__ SegWalk first_segment(const SplitKvParams& p, const S
   w.h = off / w.pages;
   w.pg = off - w.h * w.pages;
   w.seg_start = s.u_b0 + w.h * w.pages;
-  w.ne = s.ne_b0 + w.h;
   return w;
+}
+
+// Whole warp: the pieces of segment (b, h) under the schedule of a split-KV
+// launch of `grid` CTAs — the first piece's workspace slot (first CTA + segment
+// index) and the number of pieces — from the same cost mapping as
+// compute_schedule (every lane gets the result; batch up to 128 reads each
+// length once).  For the merge kernel, which may run this before its
+// dependency wait: seq_lens is an input the split kernel does not write.
+__device__ __forceinline__ int2 segment_pieces(const int32_t* seq_lens, int batch, int max_pages, int hkv,
+                                               int seg_cost, int grid, int b, int h) {
+  constexpr int kCachedChunks = 4;
+  const int lane = threadIdx.x & 31;
+  auto pages_of = [&](int i) {
+    if (i >= batch) return 0;
+    const int len = max(__ldcg(seq_lens + i), 0);
+    return min((len + kPageSize - 1) / kPageSize, max_pages);
+  };
+  int cached[kCachedChunks];
+#pragma unroll
+  for (int c = 0; c < kCachedChunks; ++c) cached[c] = pages_of(c * 32 + lane);
+  long long total_pages = 0, pages_before = 0;
+  int nonempty = 0, nonempty_before = 0, pages_b = 0;
+  for (int base = 0; base < batch; base += 32) {
+    const int c = base / 32;
+    int pg = 0;
+#pragma unroll
+    for (int k = 0; k < kCachedChunks; ++k)
+      if (k == c) pg = cached[k];
+    if (c >= kCachedChunks) pg = pages_of(base + lane);
+    const int i = base + lane;
+    int sum = pg, before = (i < b) ? pg : 0;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      sum += __shfl_xor_sync(0xffffffffu, sum, off);
+      before += __shfl_xor_sync(0xffffffffu, before, off);
+    }
+    total_pages += sum;
+    pages_before += before;
+    nonempty += __popc(__ballot_sync(0xffffffffu, pg > 0));
+    nonempty_before += __popc(__ballot_sync(0xffffffffu, pg > 0 && i < b));
+    const unsigned hit = __ballot_sync(0xffffffffu, i == b);
+    if (hit) pages_b = __shfl_sync(0xffffffffu, pg, __ffs(hit) - 1);
+  }
+  if (pages_b == 0) return make_int2(0, 0);
+  const long long total_cost = (total_pages + (long long)seg_cost * nonempty) * hkv;
+  const long long per = max(1LL, (total_cost + grid - 1) / grid);
+  const int ne = nonempty_before * hkv + h;                            // non-empty segments before (b, h)
+  const long long seg_start = pages_before * hkv + (long long)h * pages_b;
+  const long long first_cost = seg_start + (long long)seg_cost * (ne + 1);
+  const int first_cta = (int)(first_cost / per);
+  const int last_cta = (int)((first_cost + pages_b - 1) / per);
+  return make_int2(first_cta + b * hkv + h, last_cta - first_cta + 1);
 }
 
 // Producer warp, before the dependency wait: L2 prefetches of the first

@@ -186,10 +186,6 @@ __device__ void consumer_loop(const SplitKvParams& p, const Schedule& sch, uint8
     const int seg_end = w.seg_start + w.pages;
     const int n = min(sch.end, seg_end) - unit;
     const bool whole = (unit == w.seg_start) && (seg_end <= sch.end);
-    if (tid == 0 && unit == w.seg_start && SQA_CHECK(s < p.batch * p.hkv, p.status, 7, s)) {
-      const int last_cta = (int)(unit_cost(p, w.seg_start, w.ne, w.pages - 1) / sch.per_cta);
-      p.seg_info[s] = make_int2((int)blockIdx.x + s, last_cta - (int)blockIdx.x + 1);
-    }
 
     const int len_raw = __ldg(p.seq_lens + w.b);
     const int len = min(len_raw, w.pages * kPageSize);

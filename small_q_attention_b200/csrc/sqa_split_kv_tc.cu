@@ -518,10 +518,6 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
     const int n = min(sch.end, seg_end) - unit;
     const int nblk = blocks_of(n);
     const bool whole = (unit == w.seg_start) && (seg_end <= sch.end);
-    if (tid == 0 && unit == w.seg_start) {
-      const int last_cta = (int)(unit_cost(p, w.seg_start, w.ne, w.pages - 1) / sch.per_cta);
-      p.seg_info[s] = make_int2((int)blockIdx.x + s, last_cta - (int)blockIdx.x + 1);
-    }
     const int len_raw = __ldg(p.seq_lens + w.b);
     const int len = min(len_raw, w.pages * kPageSize);
     const int mlen = p.mask_lens ? __ldg(p.mask_lens + w.b) : len_raw;
