@@ -30,19 +30,6 @@ constexpr int kMaxSmemPerCta = 227 * 1024;  // dynamic shared memory limit of on
 constexpr long long kAutoTcUnitsQ2 = 131072;
 constexpr long long kAutoTcUnitsQ4 = 2048;
 constexpr long long kAutoTcUnitsQ8 = 512;
-// fp8 caches: read as fp8 by the tensor core (kind::f8f6f4) unless built with
-// -DSQA_FP8_CONVERT, which converts them to fp16 in shared memory instead (with
-// kFp8OperandBlocks fp16 operand blocks between the converters and the MMAs; the
-// rest of shared memory stages fp8 blocks).
-#ifdef SQA_FP8_CONVERT
-constexpr bool kFp8Native = false;
-#else
-constexpr bool kFp8Native = true;
-#endif
-#ifndef SQA_FP8_OPERAND_BLOCKS
-#define SQA_FP8_OPERAND_BLOCKS 2
-#endif
-constexpr int kFp8OperandBlocks = SQA_FP8_OPERAND_BLOCKS;
 constexpr int kDefaultMinPagesPerCta = 4;
 // Schedule: a segment start costs a CTA as much as this many pages (one more
 // piece epilogue and pipeline refill; measured per kernel on B200).
@@ -95,11 +82,11 @@ EncodeTiledFn encode_fn() {
 // d2 = token (Hkv * 256 B apart); HND has d1 = token (256 B apart), d2 = head
 // (4 KB apart); pages are `page_stride` bytes apart (16 * Hkv * 256 when the
 // cache is one contiguous tensor).
-// fp8 caches (fp8 = 1 or 2): the same map with 1-byte elements and a 128-dim
-// (128-byte) box; 1: no swizzle (the converters read plain rows), 2: 128-byte
-// swizzle (the tensor core reads the rows as K-major K and MN-major V operands).
+// fp8 caches: the same map with 1-byte elements and a 128-dim (128-byte) box,
+// also 128-byte swizzled (the tensor core reads the rows as K-major K and
+// MN-major V operands).
 bool encode_cache_map_uncached(CUtensorMap* map, const void* base, int num_pages, int hkv, bool hnd,
-                               uint64_t page_stride, int fp8) {
+                               uint64_t page_stride, bool fp8) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   const cuuint64_t row = (cuuint64_t)kHeadDim * (fp8 ? 1 : 2);
@@ -110,7 +97,7 @@ bool encode_cache_map_uncached(CUtensorMap* map, const void* base, int num_pages
   const cuuint32_t estr[4] = {1, 1, 1, 1};
   return fn(map, fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base),
             dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-            fp8 == 1 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_SWIZZLE_128B,
             // L2 fills of one head's row: 256 B for 16-bit elements, 128 B for fp8 (a
             // 256-byte fill there would also fetch the neighbouring head's row)
             fp8 ? CU_TENSOR_MAP_L2_PROMOTION_L2_128B : CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -121,12 +108,11 @@ bool encode_cache_map_uncached(CUtensorMap* map, const void* base, int num_pages
 // encoded maps per host thread (a map depends only on base, pages and heads;
 // the element type does not matter to a copy of 2-byte elements).
 bool encode_cache_map(CUtensorMap* map, const void* base, int num_pages, int hkv, bool hnd, uint64_t page_stride,
-                      int fp8) {
+                      bool fp8) {
   struct Entry {
     const void* base;
     int num_pages, hkv;
-    bool hnd;
-    int fp8;
+    bool hnd, fp8;
     uint64_t page_stride;
     CUtensorMap map;
   };
@@ -180,7 +166,6 @@ struct Plan {
   int smem;
   int segments;
   int pieces;
-  int stages8 = 0;
   size_t off_lse, off_o, off_timeline = 0, bytes;
 };
 
@@ -196,12 +181,8 @@ int validate(const sqa_args* a) {
   if (a->dtype != SQA_DTYPE_F16 && a->dtype != SQA_DTYPE_BF16) return SQA_ERR_UNSUPPORTED;
   if (a->kv_layout != SQA_KV_NHD && a->kv_layout != SQA_KV_HND) return SQA_ERR_UNSUPPORTED;
   if (a->kv_dtype != SQA_KV_SAME && a->kv_dtype != SQA_KV_FP8_E4M3) return SQA_ERR_UNSUPPORTED;
-  // fp8 caches: fp16 queries, tcgen05 kernel
-  // fp8 caches run on the tcgen05 kernel; read as fp8 they take fp16 or bf16 queries,
-  // converted to fp16 in shared memory (-DSQA_FP8_CONVERT) fp16 queries only
-  if (a->kv_dtype == SQA_KV_FP8_E4M3 &&
-      (a->kernel == 1 || (a->dtype != SQA_DTYPE_F16 && !(kFp8Native && a->dtype == SQA_DTYPE_BF16))))
-    return SQA_ERR_UNSUPPORTED;
+  // fp8 caches run on the tcgen05 kernel (fp16 or bf16 queries)
+  if (a->kv_dtype == SQA_KV_FP8_E4M3 && a->kernel == 1) return SQA_ERR_UNSUPPORTED;
   // a page must hold 16 x Hkv x 128 elements and start 16-byte aligned (TMA strides)
   const int64_t align_elems = a->kv_dtype == SQA_KV_FP8_E4M3 ? 16 : 8;
   if (a->page_stride < 0 || (a->page_stride > 0 && (a->page_stride < (int64_t)kPageSize * a->num_kv_heads * kHeadDim ||
@@ -245,7 +226,7 @@ int make_plan(const sqa_args* a, int device, Plan* plan) {
   // every q_len but has the longer per-CTA latency chain (TMEM, asynchronous MMA
   // completions, replica merge); the warp-level kernel wins small launches.
   if (a->kv_dtype == SQA_KV_FP8_E4M3) {
-    pl.tc = true;  // the converters live in the tcgen05 kernel
+    pl.tc = true;  // the fp8 products live in the tcgen05 kernel
   } else if (a->kernel == 0) {
     if (a->q_len >= 9) pl.tc = true;
     else if (a->q_len >= 5) pl.tc = units_upper > kAutoTcUnitsQ8;
@@ -255,27 +236,15 @@ int make_plan(const sqa_args* a, int device, Plan* plan) {
     pl.tc = a->kernel == 2;
   }
   int ctas_per_sm = kCtasPerSm;
-  if (pl.tc && a->kv_dtype == SQA_KV_FP8_E4M3 && kFp8Native) {
-    // fp8 read as fp8: a ring of 16 KB blocks (K pages | V pages) in up to 227 KB
+  if (pl.tc) {
+    // one CTA per SM: a ring of 4-page blocks (32 KB for 16-bit caches, 16 KB for
+    // fp8: K pages | V pages) in up to 227 KB of shared memory
+    const bool fp8 = a->kv_dtype == SQA_KV_FP8_E4M3;
     ctas_per_sm = 1;
-    const int fixed = split_kv_tc_smem_bytes(0, 0, true);
-    pl.stages = (kMaxSmemPerCta - fixed) / (split_kv_tc_block_bytes(true) + 16);
+    const int fixed = split_kv_tc_smem_bytes(0, fp8);
+    pl.stages = (kMaxSmemPerCta - fixed) / (split_kv_tc_block_bytes(fp8) + 16);
     if (pl.stages > kMaxStages) pl.stages = kMaxStages;
-    pl.smem = split_kv_tc_smem_bytes(pl.stages, 0, true);
-  } else if (pl.tc && a->kv_dtype == SQA_KV_FP8_E4M3) {
-    // fp8: two fp16 operand blocks; the rest of 227 KB stages fp8 blocks (the bytes in flight)
-    ctas_per_sm = 1;
-    pl.stages = kFp8OperandBlocks;
-    const int fixed = split_kv_tc_smem_bytes(pl.stages, 0);
-    pl.stages8 = (kMaxSmemPerCta - fixed) / (split_kv_tc_block_bytes() / 2 + 16);
-    if (pl.stages8 > kMaxStages) pl.stages8 = kMaxStages;
-    pl.smem = split_kv_tc_smem_bytes(pl.stages, pl.stages8);
-  } else if (pl.tc) {  // one CTA per SM: a ring of 4-page blocks in up to 227 KB of shared memory
-    ctas_per_sm = 1;
-    const int fixed = split_kv_tc_smem_bytes(0);
-    pl.stages = (kMaxSmemPerCta - fixed) / (split_kv_tc_block_bytes() + 16);
-    if (pl.stages > kMaxStages) pl.stages = kMaxStages;
-    pl.smem = split_kv_tc_smem_bytes(pl.stages);
+    pl.smem = split_kv_tc_smem_bytes(pl.stages, fp8);
   } else {
     const int fixed = split_kv_smem_bytes(pl.shape, 0);
     pl.stages = (kSmemPerCta - fixed) / (kStageBytes + 24);
@@ -381,9 +350,8 @@ int forward_impl(const sqa_args* a, void* workspace, size_t workspace_bytes, voi
   const bool hnd = a->kv_layout == SQA_KV_HND;
   const bool fp8 = a->kv_dtype == SQA_KV_FP8_E4M3;
   const uint64_t page_stride = page_stride_bytes(a->page_stride, a->num_kv_heads, fp8 ? 1 : 2);
-  const int fp8_mode = fp8 ? (kFp8Native ? 2 : 1) : 0;
-  if (!encode_cache_map(&tm_k, a->key_cache, a->num_pages, a->num_kv_heads, hnd, page_stride, fp8_mode) ||
-      !encode_cache_map(&tm_v, a->value_cache, a->num_pages, a->num_kv_heads, hnd, page_stride, fp8_mode))
+  if (!encode_cache_map(&tm_k, a->key_cache, a->num_pages, a->num_kv_heads, hnd, page_stride, fp8) ||
+      !encode_cache_map(&tm_v, a->value_cache, a->num_pages, a->num_kv_heads, hnd, page_stride, fp8))
     return SQA_ERR_CUDA;
 
   uint8_t* ws = static_cast<uint8_t*>(workspace);
@@ -412,8 +380,7 @@ int forward_impl(const sqa_args* a, void* workspace, size_t workspace_bytes, voi
   p.bf16 = a->dtype == SQA_DTYPE_BF16;
   p.hnd = hnd;
   p.out_scale = a->out_scale != 0.f ? a->out_scale : 1.f;
-  p.kv_fp8 = fp8_mode;
-  p.num_stages8 = pl.stages8;
+  p.kv_fp8 = fp8;
   p.seg_cost = pl.tc ? kSegmentCostTc : kSegmentCostMma;
 
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_ptr);

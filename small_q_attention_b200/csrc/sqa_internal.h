@@ -55,9 +55,7 @@ struct SplitKvParams {
   int bf16;                     // q / caches / out hold bf16 (else fp16) bits
   int hnd;                      // caches are [P, Hkv, 16, 128] (else [P, 16, Hkv, 128])
   float out_scale;              // multiplies every output row (1 = plain attention)
-  int kv_fp8;                   // caches hold fp8 e4m3 (tcgen05 kernel): 1 converted to fp16 in shared
-                                // memory, 2 read as fp8 by the tensor core
-  int num_stages8;              // tcgen05 kernel, kv_fp8: blocks in the fp8 staging ring
+  int kv_fp8;                   // caches hold fp8 e4m3, read as fp8 by the tensor core (tcgen05 kernel)
   int seg_cost;                 // schedule: units a segment start costs a CTA (one more epilogue)
 };
 
@@ -90,7 +88,7 @@ int split_kv_smem_bytes(const WarpShape& ws, int num_stages);
 // The tcgen05 / tensor-memory variant of the split-KV kernel (any q_len <= 16).
 cudaError_t launch_split_kv_tc(const SplitKvParams& p, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
                                int grid, int smem_bytes, cudaStream_t stream);
-int split_kv_tc_smem_bytes(int num_blocks, int num_blocks8 = 0, bool fp8_native = false);
-int split_kv_tc_block_bytes(bool fp8_native = false);
+int split_kv_tc_smem_bytes(int num_blocks, bool fp8 = false);
+int split_kv_tc_block_bytes(bool fp8 = false);
 
 }  // namespace sqa

@@ -27,6 +27,9 @@
 // * Two MMA warps, one issuing the QK products and one the PV products, each
 //   converged and issuing through elect.sync: a PV whose P is ready never
 //   waits behind a QK whose pages are still in flight.
+// * fp8 caches (template mode KV = 2): 16 KB blocks of 128-byte swizzled fp8
+//   rows read by kind::f8f6f4 products; Q and P enter as two e4m3 parts each
+//   (high + low), so eight QK and four PV products per block as for fp16.
 //
 // Pipelines (mbarriers; every wait bounded):
 //   ring   full[NB] / empty[NB]   producer -> QK issuer; released by the commit after PV
@@ -59,10 +62,6 @@ static_assert(kColS + kNumS * 64 <= 512, "S slots must fit in TMEM");
 constexpr int kSlotCols = kBlockTokens;         // fp32 S of a block; its fp16 P takes the first half
 constexpr int kSoftmaxWarps = 4;
 constexpr int kThreadsTc = (kSoftmaxWarps + 3) * 32;  // softmax x4, QK issuer, PV issuer, producer
-#ifndef SQA_TC_CONVERT_WARPS
-#define SQA_TC_CONVERT_WARPS 4
-#endif
-constexpr int kConvertWarps = SQA_TC_CONVERT_WARPS;   // fp8 caches: fp8 -> fp16 converters (4: K and V, 8: 4 each)
 constexpr int kBlockBytes8 = kBP * 4096;              // fp8 block: K pages | V pages, 2 KB each
 constexpr int kMergeCols = 64;                  // dims merged per pass
 constexpr int kMergeStride = kMergeCols + 1;    // floats per merge row (conflict-free columns)
@@ -72,32 +71,27 @@ constexpr float kRescaleLog2 = 8.f;
 constexpr float kLn2 = 0.6931471805599453f;
 
 struct TcSmem {
-  uint8_t* ring;    // fp16 operand blocks (the TMA target, or the converters' output for fp8 caches)
-  uint8_t* stage8;  // fp8 caches: the TMA target
+  uint8_t* ring;    // operand blocks, the TMA target
   float* merge;
   float2* ml;
-  uint64_t *full, *empty, *full8, *empty8, *s_full, *p_full, *pv_done, *q_ready, *mma_done;
+  uint64_t *full, *empty, *s_full, *p_full, *pv_done, *q_ready, *mma_done;
   uint32_t* tmem_base;
   Schedule* sch;
 };
 
-// KV: 0 = 16-bit caches; 1 = fp8 caches converted to fp16 in shared memory;
-// 2 = fp8 caches read by the tensor core as fp8 (kind::f8f6f4).
+// KV: 0 = 16-bit caches; 2 = fp8 caches read by the tensor core as fp8 (kind::f8f6f4).
 template <int KV>
 __host__ __device__ constexpr int ring_block_bytes() { return KV == 2 ? kBlockBytes8 : kBlockBytes; }
 
-__device__ __forceinline__ TcSmem carve(uint8_t* smem, int nb, int nb8, int ring_bytes) {
+__device__ __forceinline__ TcSmem carve(uint8_t* smem, int nb, int ring_bytes) {
   TcSmem t;
   t.ring = smem;
-  t.stage8 = smem + (size_t)nb * ring_bytes;
-  t.merge = reinterpret_cast<float*>(t.stage8 + (size_t)nb8 * kBlockBytes8);
+  t.merge = reinterpret_cast<float*>(smem + (size_t)nb * ring_bytes);
   t.ml = reinterpret_cast<float2*>(reinterpret_cast<uint8_t*>(t.merge) + kMergeBytes);
   uint64_t* b = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(t.ml) + kMlBytes);
   t.full = b;
   t.empty = t.full + nb;
-  t.full8 = t.empty + nb;
-  t.empty8 = t.full8 + nb8;
-  t.s_full = t.empty8 + nb8;
+  t.s_full = t.empty + nb;
   t.p_full = t.s_full + kNumS;
   t.pv_done = t.p_full + kNumS;
   t.q_ready = t.pv_done + kNumS;
@@ -110,18 +104,16 @@ __device__ __forceinline__ TcSmem carve(uint8_t* smem, int nb, int nb8, int ring
 __device__ __forceinline__ int blocks_of(int n) { return (n + kBP - 1) / kBP; }
 
 // ------------------------------------------------------------------ producer (whole warp)
-// KV 1: fp8 caches land in the staging ring (full8 / empty8), one 2 KB box per page
-// per tensor; KV 2: the same fp8 boxes (128-byte swizzled) land in the operand ring;
-// KV 0: fp16 halves land in the operand ring (full / empty).
+// KV 2: fp8 boxes (128 dims = 128 bytes, swizzled), one per page per tensor;
+// KV 0: two 64-dim fp16 halves per page per tensor; both into the operand ring.
 template <int KV>
 __device__ void tc_producer(const SplitKvParams& p, const Schedule& sch, const CUtensorMap* tm_k,
                             const CUtensorMap* tm_v, const TcSmem& sm, volatile int* abort) {
-  constexpr bool F8 = KV == 1;
   const int lane = threadIdx.x & 31;
   const uint64_t policy = l2_policy_evict_first();
-  const int NB = F8 ? p.num_stages8 : p.num_stages;
-  uint64_t* const full = F8 ? sm.full8 : sm.full;
-  uint64_t* const empty = F8 ? sm.empty8 : sm.empty;
+  const int NB = p.num_stages;
+  uint64_t* const full = sm.full;
+  uint64_t* const empty = sm.empty;
   SegWalk w = first_segment(p, sch);
   int slot = 0;
   uint32_t phase = 0;
@@ -170,9 +162,9 @@ __device__ void tc_producer(const SplitKvParams& p, const Schedule& sch, const C
             // NHD map: (dim, head, token, page); HND map: (dim, token, head, page)
             const int c1 = p.hnd ? 0 : w.h;
             const int c2 = p.hnd ? w.h : 0;
-            if constexpr (KV != 0) {
+            if constexpr (KV == 2) {
               mbar_arrive_expect_tx(f, np * 4096);
-              const uint32_t base = smem_u32((F8 ? sm.stage8 : sm.ring) + (size_t)slot * kBlockBytes8);
+              const uint32_t base = smem_u32(sm.ring + (size_t)slot * kBlockBytes8);
               for (int j = 0; j < np; ++j) {  // 128 fp8 dims x 16 tokens = 2 KB per tensor
                 tma_load_4d(base + j * 2048, tm_k, f, 0, c1, c2, pages[j], policy);
                 tma_load_4d(base + kBlockBytes8 / 2 + j * 2048, tm_v, f, 0, c1, c2, pages[j], policy);
@@ -208,83 +200,6 @@ __device__ void tc_producer(const SplitKvParams& p, const Schedule& sch, const C
       const int last = k + NB * ((issued - 1 - k) / NB);
       if (!mbar_drain(smem_u32(full + k), (uint32_t)(last / NB) & 1u, 100000000ull)) atomicOr(p.status, 1u);
     }
-  }
-}
-
-// ------------------------------------------------------------------ fp8 -> fp16 converters (4 warps)
-// fp8 caches: each 64-token block of K and V arrives in the staging ring as
-// plain 128-byte token rows (128 fp8 dims); the converters write it into the
-// operand ring in exactly the layout the fp16 TMA path produces (two 64-dim
-// halves, 128-byte rows, 128-byte swizzle), so the MMA code is unchanged.
-// e4m3 -> fp16 is exact.  Thread t takes token row t / 8, dims 16 (t % 8) ..
-// +15 of every page and tensor: 16 B read, 32 B written (two swizzled chunks).
-__device__ void tc_convert(const SplitKvParams& p, const Schedule& sch, const TcSmem& sm, volatile int* abort) {
-  const int tt = threadIdx.x - (kSoftmaxWarps + 3) * 32;  // 0 .. 32 * kConvertWarps - 1
-  const int t = tt & 127;
-  // with 8 warps the first four convert K, the others V; with 4, each converts both
-  const int tv0 = kConvertWarps == 8 ? (tt >> 7) : 0;
-  const int tv1 = kConvertWarps == 8 ? tv0 + 1 : 2;
-  const int lane = threadIdx.x & 31;
-  const int r = t >> 3;      // token row within a page
-  const int c = t & 7;       // 16-dim chunk of the fp8 row
-  const int half = c >> 2;   // 0: dims 0-63 (lo region), 1: dims 64-127 (hi region)
-  const uint32_t off0 = (uint32_t)(r * 128 + ((((2 * c) & 7) ^ (r & 7)) << 4));
-  const uint32_t off1 = (uint32_t)(r * 128 + ((((2 * c + 1) & 7) ^ (r & 7)) << 4));
-  const int NB = p.num_stages, NB8 = p.num_stages8;
-  SegWalk w = first_segment(p, sch);
-  int g = 0;
-  int unit = sch.start;
-  while (unit < sch.end) {
-    const int seg_end = w.seg_start + w.pages;
-    const int n = min(sch.end, seg_end) - unit;
-    const int nblk = blocks_of(n);
-    for (int k = 0; k < nblk; ++k, ++g) {
-      const int np = min(kBP, n - k * kBP);
-      const int s8 = g % NB8, sc = g % NB;
-      mbar_wait_bounded(smem_u32(sm.full8 + s8), (uint32_t)(g / NB8) & 1u, abort, p.status, 12, g);
-      mbar_wait_bounded(smem_u32(sm.empty + sc), ((uint32_t)(g / NB) & 1u) ^ 1u, abort, p.status, 13, g);
-      // 32-bit shared-window addresses (measured 1.6x faster than generic pointers here)
-      const uint32_t src = smem_u32(sm.stage8) + (uint32_t)(s8 * kBlockBytes8 + r * 128 + c * 16);
-      const uint32_t dst = smem_u32(sm.ring) + (uint32_t)(sc * kBlockBytes + half * kRegionBytes);
-      // every load of the block first (one shared-memory round trip), then convert and store
-      uint32_t words[kBP][2][4];
-#pragma unroll
-      for (int j = 0; j < kBP; ++j) {
-#pragma unroll
-        for (int tv = 0; tv < 2; ++tv) {  // K, then V
-          if (j < np && tv >= tv0 && tv < tv1) lds_v4(words[j][tv], src + tv * (kBlockBytes8 / 2) + j * 2048);
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < kBP; ++j) {
-        if (j >= np) break;
-#pragma unroll
-        for (int tv = 0; tv < 2; ++tv) {
-          if (tv < tv0 || tv >= tv1) continue;
-          uint32_t h[8];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const uint32_t wd = words[j][tv][i];
-            const __half2_raw lo = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(wd & 0xffffu), __NV_E4M3);
-            const __half2_raw hi = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(wd >> 16), __NV_E4M3);
-            h[2 * i] = (uint32_t)lo.x | ((uint32_t)lo.y << 16);
-            h[2 * i + 1] = (uint32_t)hi.x | ((uint32_t)hi.y << 16);
-          }
-          const uint32_t d = dst + tv * 2 * kRegionBytes + j * 2048;
-          sts_v4(d + off0, h[0], h[1], h[2], h[3]);
-          sts_v4(d + off1, h[4], h[5], h[6], h[7]);
-        }
-      }
-      fence_proxy_async_smem();  // generic writes, read next by the tensor core
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(smem_u32(sm.full + sc));    // operand block ready (one arrival per warp)
-        mbar_arrive(smem_u32(sm.empty8 + s8));  // staging block free
-      }
-    }
-    unit += n;
-    if (unit >= seg_end) next_segment(p, w);
-    else w.pg += n;
   }
 }
 
@@ -764,13 +679,12 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
 }
 
 template <int R, bool BF, int KV>
-__global__ void __launch_bounds__(kThreadsTc + (KV == 1 ? kConvertWarps * 32 : 0), 1)
+__global__ void __launch_bounds__(kThreadsTc, 1)
     sqa_split_kv_tc_kernel(const SplitKvParams p, const __grid_constant__ CUtensorMap tm_k,
                            const __grid_constant__ CUtensorMap tm_v) {
-  constexpr bool F8 = KV == 1;  // fp8 caches through the converter warps
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const TcSmem sm = carve(smem, p.num_stages, F8 ? p.num_stages8 : 0, ring_block_bytes<KV>());
+  const TcSmem sm = carve(smem, p.num_stages, ring_block_bytes<KV>());
   const int warp = threadIdx.x >> 5;
   constexpr int kMmaWarp = kSoftmaxWarps;         // QK issuer; owns the TMEM allocation
   constexpr int kPvWarp = kSoftmaxWarps + 1;
@@ -786,14 +700,8 @@ __global__ void __launch_bounds__(kThreadsTc + (KV == 1 ? kConvertWarps * 32 : 0
     if (tl) tl[5] = clock64();
 #endif
     for (int i = 0; i < p.num_stages; ++i) {
-      mbar_init(smem_u32(sm.full + i), F8 ? kConvertWarps : 1);  // TMA bytes, or the converters
+      mbar_init(smem_u32(sm.full + i), 1);  // the producer's arrival + the TMA bytes
       mbar_init(smem_u32(sm.empty + i), 1);
-    }
-    if (F8) {
-      for (int i = 0; i < p.num_stages8; ++i) {
-        mbar_init(smem_u32(sm.full8 + i), 1);
-        mbar_init(smem_u32(sm.empty8 + i), kConvertWarps);
-      }
     }
     for (int i = 0; i < kNumS; ++i) {
       mbar_init(smem_u32(sm.s_full + i), 1);
@@ -813,7 +721,7 @@ __global__ void __launch_bounds__(kThreadsTc + (KV == 1 ? kConvertWarps * 32 : 0
   // The PV issuer has nothing to do before the first P: it prefetches this
   // CTA's first pages into L2 before the dependency wait (hints only), off the
   // start-up path of the other warps.
-  if (warp == kPvWarp) prefetch_start<KV != 0>(p, &tm_k, &tm_v, (F8 ? p.num_stages8 : p.num_stages) * kBP);
+  if (warp == kPvWarp) prefetch_start<KV != 0>(p, &tm_k, &tm_v, p.num_stages * kBP);
 #endif
   grid_dependency_wait();
   allow_dependent_launch();
@@ -849,8 +757,6 @@ __global__ void __launch_bounds__(kThreadsTc + (KV == 1 ? kConvertWarps * 32 : 0
 
   if (warp == kProducerWarp) {
     tc_producer<KV>(p, s, &tm_k, &tm_v, sm, abort);
-  } else if (warp > kProducerWarp) {
-    if constexpr (F8) tc_convert(p, s, sm, abort);
   } else if (warp == kMmaWarp) {
     tc_mma_qk<BF, KV>(p, s, sm, tmem, abort);
   } else if (warp == kPvWarp) {
@@ -892,7 +798,7 @@ cudaError_t launch_tc(const SplitKvParams& p, const CUtensorMap& tm_k, const CUt
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kThreadsTc + (KV == 1 ? kConvertWarps * 32 : 0));
+  cfg.blockDim = dim3(kThreadsTc);
   cfg.dynamicSmemBytes = smem_bytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -907,26 +813,22 @@ cudaError_t launch_tc(const SplitKvParams& p, const CUtensorMap& tm_k, const CUt
 
 }  // namespace
 
-int split_kv_tc_block_bytes(bool fp8_native) { return fp8_native ? kBlockBytes8 : kBlockBytes; }
+int split_kv_tc_block_bytes(bool fp8) { return fp8 ? kBlockBytes8 : kBlockBytes; }
 
-int split_kv_tc_smem_bytes(int num_blocks, int num_blocks8, bool fp8_native) {
-  return 1024 + num_blocks * split_kv_tc_block_bytes(fp8_native) + num_blocks8 * kBlockBytes8 + kMergeBytes +
-         kMlBytes + (2 * num_blocks + 2 * num_blocks8 + 3 * kNumS + 3) * 8 + 8 + 64;
+int split_kv_tc_smem_bytes(int num_blocks, bool fp8) {
+  return 1024 + num_blocks * split_kv_tc_block_bytes(fp8) + kMergeBytes + kMlBytes +
+         (2 * num_blocks + 3 * kNumS + 3) * 8 + 8 + 64;
 }
 
 cudaError_t launch_split_kv_tc(const SplitKvParams& p, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
                                int grid, int smem_bytes, cudaStream_t stream) {
   const bool r4 = kGroup * p.q_len <= 32;
-  if (p.kv_fp8 == 2) {  // fp8 caches read as fp8; fp16 or bf16 queries
+  if (p.kv_fp8) {  // fp8 caches read as fp8; fp16 or bf16 queries
     if (p.bf16)
       return r4 ? launch_tc<4, true, 2>(p, tm_k, tm_v, grid, smem_bytes, stream)
                 : launch_tc<2, true, 2>(p, tm_k, tm_v, grid, smem_bytes, stream);
     return r4 ? launch_tc<4, false, 2>(p, tm_k, tm_v, grid, smem_bytes, stream)
               : launch_tc<2, false, 2>(p, tm_k, tm_v, grid, smem_bytes, stream);
-  }
-  if (p.kv_fp8) {  // fp8 caches converted to fp16 in shared memory
-    return r4 ? launch_tc<4, false, 1>(p, tm_k, tm_v, grid, smem_bytes, stream)
-              : launch_tc<2, false, 1>(p, tm_k, tm_v, grid, smem_bytes, stream);
   }
   if (p.bf16)
     return r4 ? launch_tc<4, true, 0>(p, tm_k, tm_v, grid, smem_bytes, stream)
