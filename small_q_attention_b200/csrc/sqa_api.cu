@@ -31,6 +31,10 @@ constexpr long long kAutoTcUnitsQ2 = 131072;
 constexpr long long kAutoTcUnitsQ4 = 2048;
 constexpr long long kAutoTcUnitsQ8 = 512;
 constexpr int kDefaultMinPagesPerCta = 4;
+// fp8 caches: 8-page blocks when a CTA's range is at least this many pages x KV
+// heads (measured on B200: 5-6% faster at q16 x 16 x 32K and on cfg5, 4-6% slower
+// on calls of ~100 pages per CTA).
+constexpr long long kFp8LongRangeUnits = 400;
 // Schedule: a segment start costs a CTA as much as this many pages (one more
 // piece epilogue and pipeline refill; measured per kernel on B200).
 #ifndef SQA_SEGMENT_COST_TC
@@ -164,6 +168,7 @@ struct Plan {
   int grid;
   int stages;
   int smem;
+  int kv_fp8 = 0;  // fp8 caches: 2 = 4-page blocks, 3 = 8-page blocks
   int segments;
   int pieces;
   size_t off_lse, off_o, off_timeline = 0, bytes;
@@ -235,22 +240,7 @@ int make_plan(const sqa_args* a, int device, Plan* plan) {
   } else {
     pl.tc = a->kernel == 2;
   }
-  int ctas_per_sm = kCtasPerSm;
-  if (pl.tc) {
-    // one CTA per SM: a ring of 4-page blocks (32 KB for 16-bit caches, 16 KB for
-    // fp8: K pages | V pages) in up to 227 KB of shared memory
-    const bool fp8 = a->kv_dtype == SQA_KV_FP8_E4M3;
-    ctas_per_sm = 1;
-    const int fixed = split_kv_tc_smem_bytes(0, fp8);
-    pl.stages = (kMaxSmemPerCta - fixed) / (split_kv_tc_block_bytes(fp8) + 16);
-    if (pl.stages > kMaxStages) pl.stages = kMaxStages;
-    pl.smem = split_kv_tc_smem_bytes(pl.stages, fp8);
-  } else {
-    const int fixed = split_kv_smem_bytes(pl.shape, 0);
-    pl.stages = (kSmemPerCta - fixed) / (kStageBytes + 24);
-    if (pl.stages > kMaxStages) pl.stages = kMaxStages;
-    pl.smem = split_kv_smem_bytes(pl.shape, pl.stages);
-  }
+  const int ctas_per_sm = pl.tc ? 1 : kCtasPerSm;  // tcgen05: one CTA per SM (all of TMEM)
   const int min_pages = a->min_pages_per_cta > 0 ? a->min_pages_per_cta : kDefaultMinPagesPerCta;
   long long grid = a->num_ctas > 0 ? a->num_ctas : (long long)sms * ctas_per_sm;
   if (a->num_ctas <= 0) {
@@ -259,6 +249,21 @@ int make_plan(const sqa_args* a, int device, Plan* plan) {
   }
   if (grid < 1) grid = 1;
   pl.grid = (int)grid;
+  if (pl.tc) {
+    // a ring of blocks in up to 227 KB of shared memory: 32 KB (16-bit caches, 4
+    // pages), fp8 caches 16 KB (4 pages) or, for long per-CTA ranges, 32 KB (8 pages)
+    if (a->kv_dtype == SQA_KV_FP8_E4M3)
+      pl.kv_fp8 = units_upper >= (long long)kFp8LongRangeUnits * pl.grid ? 3 : 2;
+    const int fixed = split_kv_tc_smem_bytes(0, pl.kv_fp8);
+    pl.stages = (kMaxSmemPerCta - fixed) / (split_kv_tc_block_bytes(pl.kv_fp8) + 16);
+    if (pl.stages > kMaxStages) pl.stages = kMaxStages;
+    pl.smem = split_kv_tc_smem_bytes(pl.stages, pl.kv_fp8);
+  } else {
+    const int fixed = split_kv_smem_bytes(pl.shape, 0);
+    pl.stages = (kSmemPerCta - fixed) / (kStageBytes + 24);
+    if (pl.stages > kMaxStages) pl.stages = kMaxStages;
+    pl.smem = split_kv_smem_bytes(pl.shape, pl.stages);
+  }
   pl.pieces = pl.grid + pl.segments;  // piece index = cta + segment < grid + segments - 1
 
   pl.off_lse = kAlign;  // [0, 256): device status word
@@ -380,7 +385,7 @@ int forward_impl(const sqa_args* a, void* workspace, size_t workspace_bytes, voi
   p.bf16 = a->dtype == SQA_DTYPE_BF16;
   p.hnd = hnd;
   p.out_scale = a->out_scale != 0.f ? a->out_scale : 1.f;
-  p.kv_fp8 = fp8;
+  p.kv_fp8 = pl.kv_fp8;
   p.seg_cost = pl.tc ? kSegmentCostTc : kSegmentCostMma;
 
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_ptr);

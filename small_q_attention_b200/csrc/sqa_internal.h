@@ -55,7 +55,8 @@ struct SplitKvParams {
   int bf16;                     // q / caches / out hold bf16 (else fp16) bits
   int hnd;                      // caches are [P, Hkv, 16, 128] (else [P, 16, Hkv, 128])
   float out_scale;              // multiplies every output row (1 = plain attention)
-  int kv_fp8;                   // caches hold fp8 e4m3, read as fp8 by the tensor core (tcgen05 kernel)
+  int kv_fp8;                   // caches hold fp8 e4m3, read as fp8 by the tensor core (tcgen05 kernel):
+                                // 2 in blocks of 4 pages, 3 in blocks of 8 pages
   int seg_cost;                 // schedule: units a segment start costs a CTA (one more epilogue)
 };
 
@@ -88,7 +89,7 @@ int split_kv_smem_bytes(const WarpShape& ws, int num_stages);
 // The tcgen05 / tensor-memory variant of the split-KV kernel (any q_len <= 16).
 cudaError_t launch_split_kv_tc(const SplitKvParams& p, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
                                int grid, int smem_bytes, cudaStream_t stream);
-int split_kv_tc_smem_bytes(int num_blocks, bool fp8 = false);
-int split_kv_tc_block_bytes(bool fp8 = false);
+int split_kv_tc_smem_bytes(int num_blocks, int kv_fp8 = 0);
+int split_kv_tc_block_bytes(int kv_fp8 = 0);
 
 }  // namespace sqa

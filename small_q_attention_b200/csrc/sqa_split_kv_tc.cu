@@ -62,7 +62,25 @@ static_assert(kColS + kNumS * 64 <= 512, "S slots must fit in TMEM");
 constexpr int kSlotCols = kBlockTokens;         // fp32 S of a block; its fp16 P takes the first half
 constexpr int kSoftmaxWarps = 4;
 constexpr int kThreadsTc = (kSoftmaxWarps + 3) * 32;  // softmax x4, QK issuer, PV issuer, producer
-constexpr int kBlockBytes8 = kBP * 4096;              // fp8 block: K pages | V pages, 2 KB each
+
+// Block shape per cache mode.  KV 0 (16-bit): 4 pages (64 tokens) per 32 KB ring
+// block (K lo | K hi | V lo | V hi), four 64-column S slots.  fp8 caches, K pages
+// then V pages, 2 KB each: KV 2, 4 pages per 16 KB block and four 64-column S
+// slots; KV 3, 8 pages per 32 KB block and two 128-column S slots (the same TMEM
+// and tokens in flight; the QK products run at N = 128, where the tensor core is
+// most efficient, and the softmax's per-block overheads cover twice the tokens:
+// the better shape for long per-CTA ranges, the 4-page one for short calls).
+template <int KV>
+struct TcShape {
+  static constexpr bool kFp8 = KV >= 2;
+  static constexpr int kPages = KV == 3 ? 8 : kBP;
+  static constexpr int kTokens = kPages * kPageSize;
+  static constexpr int kSlots = KV == 3 ? 2 : kNumS;
+  static constexpr int kSlotCols = kTokens;
+  static constexpr int kRing = kFp8 ? kPages * 4096 : kBlockBytes;  // bytes per ring block
+  static constexpr int kVOffset = kFp8 ? kPages * 2048 : 2 * kRegionBytes;  // V within a block
+  static_assert(kColS + kSlots * kSlotCols <= 512, "S slots must fit in TMEM");
+};
 constexpr int kMergeCols = 64;                  // dims merged per pass
 constexpr int kMergeStride = kMergeCols + 1;    // floats per merge row (conflict-free columns)
 constexpr int kMergeBytes = 128 * kMergeStride * 4;  // one row per TMEM lane
@@ -79,9 +97,8 @@ struct TcSmem {
   Schedule* sch;
 };
 
-// KV: 0 = 16-bit caches; 2 = fp8 caches read by the tensor core as fp8 (kind::f8f6f4).
-template <int KV>
-__host__ __device__ constexpr int ring_block_bytes() { return KV == 2 ? kBlockBytes8 : kBlockBytes; }
+// KV: 0 = 16-bit caches; 2, 3 = fp8 caches read by the tensor core as fp8
+// (kind::f8f6f4) in 4- or 8-page blocks.
 
 __device__ __forceinline__ TcSmem carve(uint8_t* smem, int nb, int ring_bytes) {
   TcSmem t;
@@ -101,7 +118,8 @@ __device__ __forceinline__ TcSmem carve(uint8_t* smem, int nb, int ring_bytes) {
   return t;
 }
 
-__device__ __forceinline__ int blocks_of(int n) { return (n + kBP - 1) / kBP; }
+template <int KV>
+__device__ __forceinline__ int blocks_of(int n) { return (n + TcShape<KV>::kPages - 1) / TcShape<KV>::kPages; }
 
 // ------------------------------------------------------------------ producer (whole warp)
 // KV 2: fp8 boxes (128 dims = 128 bytes, swizzled), one per page per tensor;
@@ -134,7 +152,7 @@ __device__ void tc_producer(const SplitKvParams& p, const Schedule& sch, const C
     const int unit_next = unit + n;  // the next piece, for the look-ahead at this piece's last chunk
     SegWalk wn = w;
     if (unit_next < sch.end) next_segment(p, wn);
-    for (int c0 = 0; c0 < n; c0 += 32) {  // 32 is a multiple of kBP: blocks never straddle chunks
+    for (int c0 = 0; c0 < n; c0 += 32) {  // 32 is a multiple of the block: blocks never straddle chunks
       const int cnt = min(32, n - c0);
       int ids_next = 0;
       if (c0 + 32 < n) {
@@ -143,11 +161,12 @@ __device__ void tc_producer(const SplitKvParams& p, const Schedule& sch, const C
         const int n2 = min(sch.end, wn.seg_start + wn.pages) - unit_next;
         ids_next = (lane < n2) ? __ldg(p.block_tables + (size_t)wn.b * p.max_pages + wn.pg + lane) : 0;
       }
-      for (int jb = 0; jb < cnt; jb += kBP) {
-        const int np = min(kBP, cnt - jb);
-        int pages[kBP];
+      constexpr int kPg = TcShape<KV>::kPages;
+      for (int jb = 0; jb < cnt; jb += kPg) {
+        const int np = min(kPg, cnt - jb);
+        int pages[kPg];
 #pragma unroll
-        for (int j = 0; j < kBP; ++j) {
+        for (int j = 0; j < kPg; ++j) {
           pages[j] = __shfl_sync(0xffffffffu, ids, min(jb + j, 31));
           if (j < np && (pages[j] < 0 || pages[j] >= p.num_pages)) {
             bad_page = 1;
@@ -162,12 +181,12 @@ __device__ void tc_producer(const SplitKvParams& p, const Schedule& sch, const C
             // NHD map: (dim, head, token, page); HND map: (dim, token, head, page)
             const int c1 = p.hnd ? 0 : w.h;
             const int c2 = p.hnd ? w.h : 0;
-            if constexpr (KV == 2) {
+            if constexpr (TcShape<KV>::kFp8) {
               mbar_arrive_expect_tx(f, np * 4096);
-              const uint32_t base = smem_u32(sm.ring + (size_t)slot * kBlockBytes8);
+              const uint32_t base = smem_u32(sm.ring + (size_t)slot * TcShape<KV>::kRing);
               for (int j = 0; j < np; ++j) {  // 128 fp8 dims x 16 tokens = 2 KB per tensor
                 tma_load_4d(base + j * 2048, tm_k, f, 0, c1, c2, pages[j], policy);
-                tma_load_4d(base + kBlockBytes8 / 2 + j * 2048, tm_v, f, 0, c1, c2, pages[j], policy);
+                tma_load_4d(base + TcShape<KV>::kVOffset + j * 2048, tm_v, f, 0, c1, c2, pages[j], policy);
               }
             } else {
               mbar_arrive_expect_tx(f, np * kStageBytes);
@@ -225,7 +244,8 @@ __device__ void tc_mma_qk(const SplitKvParams& p, const Schedule& sch, const TcS
                           volatile int* abort) {
   // Q (TMEM) x K_block (K-major).  Format field 0 is fp16 for kind::f16 and e4m3 for
   // kind::f8f6f4 (where 1 would be e5m2): KV 2 is e4m3 whatever the query type.
-  constexpr uint32_t kIdescQK = mma_idesc_f16(128, kBlockTokens, false, false, BF && KV != 2);
+  using Sh = TcShape<KV>;
+  constexpr uint32_t kIdescQK = mma_idesc_f16(128, Sh::kTokens, false, false, BF && !Sh::kFp8);
   const int NB = p.num_stages;
   SegWalk w = first_segment(p, sch);
   int h = 0;   // CTA block counter
@@ -234,13 +254,13 @@ __device__ void tc_mma_qk(const SplitKvParams& p, const Schedule& sch, const TcS
   while (unit < sch.end) {
     const int seg_end = w.seg_start + w.pages;
     const int n = min(sch.end, seg_end) - unit;
-    const int nblk = blocks_of(n);
+    const int nblk = blocks_of<KV>(n);
     // Q of piece pc is in Q slot pc % 2 (written one piece ahead by the softmax warps)
     mbar_wait_bounded(smem_u32(sm.q_ready + (pc & 1)), (uint32_t)(pc >> 1) & 1u, abort, p.status, 4, pc);
     const uint32_t q_col = tmem + kColQ + (pc & 1) * 64;
     for (int k = 0; k < nblk; ++k, ++h) {
-      if (h >= kNumS)
-        mbar_wait_bounded(smem_u32(sm.pv_done + (h % kNumS)), (uint32_t)((h - kNumS) / kNumS) & 1u, abort,
+      if (h >= Sh::kSlots)
+        mbar_wait_bounded(smem_u32(sm.pv_done + (h % Sh::kSlots)), (uint32_t)((h - Sh::kSlots) / Sh::kSlots) & 1u, abort,
                           p.status, 11, h);
       const int slot = h % NB;
       mbar_wait_bounded(smem_u32(sm.full + slot), (uint32_t)(h / NB) & 1u, abort, p.status, 5, h);
@@ -252,10 +272,10 @@ __device__ void tc_mma_qk(const SplitKvParams& p, const Schedule& sch, const TcS
       }
       const uint64_t t_qk = SQA_T0();
       if (elect_one()) {
-        const uint32_t d = tmem + kColS + (h % kNumS) * kSlotCols;
-        if constexpr (KV == 2) {
-          // K: 64 token rows of 128 fp8 dims (128 B, swizzled), 8-row groups 1 KB apart
-          const uint32_t k_base = smem_u32(sm.ring + (size_t)slot * kBlockBytes8);
+        const uint32_t d = tmem + kColS + (h % Sh::kSlots) * Sh::kSlotCols;
+        if constexpr (Sh::kFp8) {
+          // K: 64 or 128 token rows of 128 fp8 dims (128 B, swizzled), 8-row groups 1 KB apart
+          const uint32_t k_base = smem_u32(sm.ring + (size_t)slot * Sh::kRing);
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {  // high part, then low part; 32 dims (32 B) per step
             const uint64_t b = smem_desc_sw128(k_base + (kk & 3) * 32u, 16, 1024);
@@ -269,7 +289,7 @@ __device__ void tc_mma_qk(const SplitKvParams& p, const Schedule& sch, const TcS
             tc_mma_ts(d, q_col + kk * 8, b, kIdescQK, kk > 0 ? 1u : 0u);
           }
         }
-        tc_commit(smem_u32(sm.s_full + (h % kNumS)));
+        tc_commit(smem_u32(sm.s_full + (h % Sh::kSlots)));
       }
       __syncwarp();
       SQA_WAIT_ACCOUNT(12, t_qk);
@@ -292,8 +312,9 @@ template <int R, bool BF, int KV>
 __device__ void tc_mma_pv(const SplitKvParams& p, const Schedule& sch, const TcSmem& sm, uint32_t tmem,
                           volatile int* abort) {
   // P (TMEM) x V (MN-major); KV 2: e4m3 whatever the query type (format field 0)
-  constexpr uint32_t kIdescPV = mma_idesc_f16(128, 128, false, true, BF && KV != 2);
-  constexpr int kPPR = kBP / R;       // pages of a block per replica
+  constexpr uint32_t kIdescPV = mma_idesc_f16(128, 128, false, true, BF && !TcShape<KV>::kFp8);
+  using Sh = TcShape<KV>;
+  constexpr int kPPR = kBP / R;       // KV 0: pages of a block per replica
   constexpr int kLanesPR = 128 / R;   // TMEM lanes per replica
   const int NB = p.num_stages;
   SegWalk w = first_segment(p, sch);
@@ -302,27 +323,29 @@ __device__ void tc_mma_pv(const SplitKvParams& p, const Schedule& sch, const TcS
   while (unit < sch.end) {
     const int seg_end = w.seg_start + w.pages;
     const int n = min(sch.end, seg_end) - unit;
-    const int nblk = blocks_of(n);
+    const int nblk = blocks_of<KV>(n);
     for (int k = 0; k < nblk; ++k, ++g) {
       const int slot = g % NB;
-      const int np = min(kBP, n - k * kBP);
-      mbar_wait_bounded(smem_u32(sm.p_full + (g % kNumS)), (uint32_t)(g / kNumS) & 1u, abort, p.status, 6, g);
+      const int np = min(Sh::kPages, n - k * Sh::kPages);
+      mbar_wait_bounded(smem_u32(sm.p_full + (g % Sh::kSlots)), (uint32_t)(g / Sh::kSlots) & 1u, abort, p.status, 6,
+                        g);
       __syncwarp();
       tc_fence_after();
       const uint64_t t_pv = SQA_T0();
       if (elect_one()) {
-        const uint32_t p_col = tmem + kColS + (g % kNumS) * kSlotCols;
-        if constexpr (KV == 2) {
-          // V: 64 token rows of 128 fp8 dims, one 128-byte MN atom wide; 8-row groups 1 KB apart
-          const uint32_t v_base = smem_u32(sm.ring + (size_t)slot * kBlockBytes8 + kBlockBytes8 / 2);
-          const int halves = np > 2 ? 2 : 1;  // 32 tokens per product; absent pages hold zero V
+        const uint32_t p_col = tmem + kColS + (g % Sh::kSlots) * Sh::kSlotCols;
+        if constexpr (Sh::kFp8) {
+          // V: the block's token rows of 128 fp8 dims, one 128-byte MN atom wide; 8-row groups
+          // 1 KB apart; P high part in the slot's first kTokens / 4 columns, low part next
+          const uint32_t v_base = smem_u32(sm.ring + (size_t)slot * Sh::kRing + Sh::kVOffset);
+          const int quarters = (np + 1) / 2;  // 32 tokens per product; absent pages hold zero V
 #pragma unroll
           for (int part = 0; part < 2; ++part) {
-            for (int hf = 0; hf < halves; ++hf) {
-              const uint64_t b = smem_desc_sw128(v_base + hf * 4096, kBlockBytes8, 1024);
+            for (int qt = 0; qt < quarters; ++qt) {
+              const uint64_t b = smem_desc_sw128(v_base + qt * 4096, Sh::kRing, 1024);
               // the piece's first product overwrites O
-              tc_mma_ts_f8(tmem + kColO, p_col + part * 16 + hf * 8, b, kIdescPV,
-                           (k > 0 || part > 0 || hf > 0) ? 1u : 0u);
+              tc_mma_ts_f8(tmem + kColO, p_col + part * (Sh::kTokens / 4) + qt * 8, b, kIdescPV,
+                           (k > 0 || part > 0 || qt > 0) ? 1u : 0u);
             }
           }
         } else {
@@ -339,7 +362,7 @@ __device__ void tc_mma_pv(const SplitKvParams& p, const Schedule& sch, const TcS
           }
         }
         tc_commit(smem_u32(sm.empty + slot));              // the block's ring slot may be refilled
-        tc_commit(smem_u32(sm.pv_done + (g % kNumS)));     // S/P slot free, O up to date
+        tc_commit(smem_u32(sm.pv_done + (g % Sh::kSlots)));  // S/P slot free, O up to date
       }
       __syncwarp();
       SQA_WAIT_ACCOUNT(13, t_pv);
@@ -362,7 +385,8 @@ template <int R, bool BF, int KV>
 __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const TcSmem& sm, uint32_t tmem,
                            volatile int* abort) {
   constexpr int kLanesPR = 128 / R;          // lanes (rows) per replica
-  constexpr int kTok = kBlockTokens / R;     // tokens of a block per replica
+  using Sh = TcShape<KV>;
+  constexpr int kTok = Sh::kTokens / R;      // tokens of a block per replica
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int tid = threadIdx.x;               // 0 .. 127
@@ -387,7 +411,7 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
       qv[c >> 3][4 * (c & 7) + 3] = v.w;
     }
     float qinv = 1.f;  // KV 2: 2^-e of this row
-    if constexpr (KV == 2) {
+    if constexpr (Sh::kFp8) {
       float mx = 0.f;
 #pragma unroll
       for (int i = 0; i < 64; ++i) {
@@ -431,7 +455,7 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
     const int s = w.b * p.hkv + w.h;
     const int seg_end = w.seg_start + w.pages;
     const int n = min(sch.end, seg_end) - unit;
-    const int nblk = blocks_of(n);
+    const int nblk = blocks_of<KV>(n);
     const bool whole = (unit == w.seg_start) && (seg_end <= sch.end);
     const int len_raw = __ldg(p.seq_lens + w.b);
     const int len = min(len_raw, w.pages * kPageSize);
@@ -460,17 +484,23 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
     float m_used = -INFINITY, l = 0.f;
     for (int k = 0; k < nblk; ++k) {
       const int g = gb0 + k;
-      const int np = min(kBP, n - k * kBP);
-      const int tok0 = (w.pg + k * kBP) * kPageSize + tok_lo;  // first token of this replica's columns
+      const int np = min(Sh::kPages, n - k * Sh::kPages);
+      const int tok0 = (w.pg + k * Sh::kPages) * kPageSize + tok_lo;  // first token of this replica's columns
       const int valid = np * kPageSize - tok_lo;                 // valid columns of this replica (may be <= 0)
-      mbar_wait_bounded(smem_u32(sm.s_full + (g % kNumS)), (uint32_t)(g / kNumS) & 1u, abort, p.status, 7, g);
+      mbar_wait_bounded(smem_u32(sm.s_full + (g % Sh::kSlots)), (uint32_t)(g / Sh::kSlots) & 1u, abort, p.status, 7,
+                        g);
       tc_fence_after();
       if (g == 0 && tid == 0 && p.timeline) SQA_CLK(p.timeline + (size_t)blockIdx.x * 32, 14);
       const uint64_t t_sm = SQA_T0();
-      const uint32_t slot_col = tl + kColS + (g % kNumS) * kSlotCols;
+      const uint32_t slot_col = tl + kColS + (g % Sh::kSlots) * Sh::kSlotCols;
       uint32_t sraw[kTok];
-      if constexpr (kTok == 16) tmem_ld16(slot_col + tok_lo, sraw);
-      else tmem_ld32(slot_col + tok_lo, sraw);
+      if constexpr (kTok == 16) {
+        tmem_ld16(slot_col + tok_lo, sraw);
+      } else {
+#pragma unroll
+        for (int c = 0; c < kTok; c += 32)
+          tmem_ld32(slot_col + tok_lo + c, *reinterpret_cast<uint32_t(*)[32]>(sraw + c));
+      }
       tmem_wait_ld();
       // Scores stay unscaled until the exponent: max(c * s) = c * max(s) for c > 0.
       // mask columns past the piece (stale data), the causal tail and the sequence end
@@ -491,7 +521,7 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
         m_used = m_new;  // the piece's first PV of this replica overwrites its O rows
       } else if (__any_sync(0xffffffffu, need)) {
         // O must be stable: wait for PV(g - 1), then rescale this warp's rows in TMEM
-        mbar_wait_bounded(smem_u32(sm.pv_done + ((g - 1) % kNumS)), (uint32_t)((g - 1) / kNumS) & 1u, abort,
+        mbar_wait_bounded(smem_u32(sm.pv_done + ((g - 1) % Sh::kSlots)), (uint32_t)((g - 1) / Sh::kSlots) & 1u, abort,
                           p.status, 8, g);
         tc_fence_after();
         const float alpha = need ? ex2(m_used - m_new) : 1.f;
@@ -513,9 +543,9 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
       // p = 2^(c*s - m): one FFMA and one ex2 per score
       const float nbase = active ? -((m_used == -INFINITY) ? 0.f : m_used) : -INFINITY;
       float ls[2] = {0.f, 0.f};
-      if constexpr (KV == 2) {
-        // P as e4m3 high and low parts over all 64 tokens of the block (columns
-        // 0-15 and 16-31 of the S slot, 4 tokens per column), zero outside this
+      if constexpr (Sh::kFp8) {
+        // P as e4m3 high and low parts over all tokens of the block (the slot's first
+        // kTokens / 4 columns and the next, 4 tokens per column), zero outside this
         // replica's tokens so that the PV products need no lane mask
         constexpr int kW = kTok / 4;  // columns of this replica per part
         uint32_t ph[kW], pl[kW];
@@ -532,13 +562,24 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
           ph[t] = h01 | (h23 << 16);
           pl[t] = pack_e4m3x2(p0 - d01.x, p1 - d01.y) | (pack_e4m3x2(p2 - d23.x, p3 - d23.y) << 16);
         }
-        uint32_t pw[32];
+        constexpr int kPartCols = Sh::kTokens / 4;  // 16 or 32
+        if constexpr (kPartCols == 16) {
+          uint32_t pw[32];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          pw[i] = (i / kW == rep) ? ph[i % kW] : 0u;
-          pw[16 + i] = (i / kW == rep) ? pl[i % kW] : 0u;
+          for (int i = 0; i < 16; ++i) {
+            pw[i] = (i / kW == rep) ? ph[i % kW] : 0u;
+            pw[16 + i] = (i / kW == rep) ? pl[i % kW] : 0u;
+          }
+          tmem_st32(slot_col, pw);
+        } else {
+          uint32_t pw[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) pw[i] = (i / kW == rep) ? ph[i % kW] : 0u;
+          tmem_st32(slot_col, pw);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) pw[i] = (i / kW == rep) ? pl[i % kW] : 0u;
+          tmem_st32(slot_col + 32, pw);
         }
-        tmem_st32(slot_col, pw);
       } else {
         // P as fp16 / bf16 pairs over this replica's columns in the first half of the S slot
         uint32_t pk[kTok / 2];
@@ -554,12 +595,12 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
       }
       l += ls[0] + ls[1];
       tmem_wait_st();
-      const int btok = (w.pg + k * kBP) * kPageSize;
-      if (KV == 2 && (btok + np * kPageSize > len || np < kBP) && warp == 0) {
+      const int btok = (w.pg + k * Sh::kPages) * kPageSize;
+      if (Sh::kFp8 && (btok + np * kPageSize > len || np < Sh::kPages) && warp == 0) {
         // fp8 V rows (128 B, swizzled within the row only) of tokens at or past the
         // sequence end, and of the absent pages a 32-token product still reads: zero
-        uint8_t* vreg = sm.ring + (size_t)(g % NB) * kBlockBytes8 + kBlockBytes8 / 2;
-        const int pages_read = np > 2 ? kBP : 2;
+        uint8_t* vreg = sm.ring + (size_t)(g % NB) * Sh::kRing + Sh::kVOffset;
+        const int pages_read = (np + 1) / 2 * 2;  // whole 32-token quarters
         for (int j = 0; j < pages_read; ++j) {
           const int first = (j < np) ? max(len - (btok + j * kPageSize), 0) : 0;
           if (first >= kPageSize) continue;
@@ -569,7 +610,7 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
         }
         fence_proxy_async_smem();
       }
-      if (KV != 2 && btok + np * kPageSize > len && warp == 0) {
+      if (!Sh::kFp8 && btok + np * kPageSize > len && warp == 0) {
         // tokens at or past the sequence end: zero their V rows (the pool may hold NaN there)
         uint8_t* vreg = sm.ring + (size_t)(g % NB) * kBlockBytes + 2 * kRegionBytes;
         for (int j = 0; j < np; ++j) {
@@ -585,7 +626,7 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(sm.p_full + (g % kNumS)));
+      if (lane == 0) mbar_arrive(smem_u32(sm.p_full + (g % Sh::kSlots)));
       SQA_WAIT_ACCOUNT(14, t_sm);
       (void)t_sm;
     }
@@ -594,7 +635,8 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
     const uint64_t t_ep = SQA_T0();
     const int gl = gb0 + nblk - 1;
     sm.ml[rep * kLanesPR + lrow] = make_float2(m_used, l);
-    mbar_wait_bounded(smem_u32(sm.pv_done + (gl % kNumS)), (uint32_t)(gl / kNumS) & 1u, abort, p.status, 10, gl);
+    mbar_wait_bounded(smem_u32(sm.pv_done + (gl % Sh::kSlots)), (uint32_t)(gl / Sh::kSlots) & 1u, abort, p.status, 10,
+                      gl);
     tc_fence_after();
     named_bar_sync(1, kSoftmaxWarps * 32);
     float mx = -INFINITY;
@@ -684,7 +726,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
                            const __grid_constant__ CUtensorMap tm_v) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const TcSmem sm = carve(smem, p.num_stages, ring_block_bytes<KV>());
+  const TcSmem sm = carve(smem, p.num_stages, TcShape<KV>::kRing);
   const int warp = threadIdx.x >> 5;
   constexpr int kMmaWarp = kSoftmaxWarps;         // QK issuer; owns the TMEM allocation
   constexpr int kPvWarp = kSoftmaxWarps + 1;
@@ -721,7 +763,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
   // The PV issuer has nothing to do before the first P: it prefetches this
   // CTA's first pages into L2 before the dependency wait (hints only), off the
   // start-up path of the other warps.
-  if (warp == kPvWarp) prefetch_start<KV != 0>(p, &tm_k, &tm_v, p.num_stages * kBP);
+  if (warp == kPvWarp) prefetch_start<KV != 0>(p, &tm_k, &tm_v, p.num_stages * TcShape<KV>::kPages);
 #endif
   grid_dependency_wait();
   allow_dependent_launch();
@@ -813,17 +855,24 @@ cudaError_t launch_tc(const SplitKvParams& p, const CUtensorMap& tm_k, const CUt
 
 }  // namespace
 
-int split_kv_tc_block_bytes(bool fp8) { return fp8 ? kBlockBytes8 : kBlockBytes; }
+int split_kv_tc_block_bytes(int kv_fp8) { return kv_fp8 == 3 ? 8 * 4096 : kv_fp8 ? 4 * 4096 : kBlockBytes; }
 
-int split_kv_tc_smem_bytes(int num_blocks, bool fp8) {
-  return 1024 + num_blocks * split_kv_tc_block_bytes(fp8) + kMergeBytes + kMlBytes +
+int split_kv_tc_smem_bytes(int num_blocks, int kv_fp8) {
+  return 1024 + num_blocks * split_kv_tc_block_bytes(kv_fp8) + kMergeBytes + kMlBytes +
          (2 * num_blocks + 3 * kNumS + 3) * 8 + 8 + 64;
 }
 
 cudaError_t launch_split_kv_tc(const SplitKvParams& p, const CUtensorMap& tm_k, const CUtensorMap& tm_v,
                                int grid, int smem_bytes, cudaStream_t stream) {
   const bool r4 = kGroup * p.q_len <= 32;
-  if (p.kv_fp8) {  // fp8 caches read as fp8; fp16 or bf16 queries
+  if (p.kv_fp8 == 3) {  // fp8 caches read as fp8, 8-page blocks; fp16 or bf16 queries
+    if (p.bf16)
+      return r4 ? launch_tc<4, true, 3>(p, tm_k, tm_v, grid, smem_bytes, stream)
+                : launch_tc<2, true, 3>(p, tm_k, tm_v, grid, smem_bytes, stream);
+    return r4 ? launch_tc<4, false, 3>(p, tm_k, tm_v, grid, smem_bytes, stream)
+              : launch_tc<2, false, 3>(p, tm_k, tm_v, grid, smem_bytes, stream);
+  }
+  if (p.kv_fp8) {  // fp8 caches read as fp8, 4-page blocks
     if (p.bf16)
       return r4 ? launch_tc<4, true, 2>(p, tm_k, tm_v, grid, smem_bytes, stream)
                 : launch_tc<2, true, 2>(p, tm_k, tm_v, grid, smem_bytes, stream);

@@ -146,3 +146,14 @@ def test_fp8_flashinfer_entry(sqa):
     assert out.dtype == torch.bfloat16 and out.shape == query.shape
     ref = oracle(dict(c, query=c["query"].to(torch.bfloat16).float()), k_scale, v_scale)
     assert_close(out.view(c["query"].shape), ref)
+
+
+@pytest.mark.parametrize("q_len", [4, 16])
+@pytest.mark.parametrize("num_ctas", [5, 17, 64])
+def test_fp8_block_shapes(sqa, q_len, num_ctas):
+    """Both fp8 block shapes: 8-page blocks when a CTA's range is long (few CTAs here),
+    4-page blocks otherwise; partial blocks and piece boundaries in both."""
+    c = case_fp8(q_len, [3000, 5000, 700, 37], hkv=8, seed=q_len + num_ctas)
+    out = sqa.small_q_attention(c["query"], c["key_cache"], c["value_cache"], c["block_tables"], c["seq_lens"], 16,
+                                num_ctas=num_ctas, min_pages_per_cta=1, check=True)
+    assert_close(out, oracle(c))
