@@ -26,8 +26,8 @@
  * be 16-byte aligned.
  *
  * Nothing here allocates device memory: the caller passes a workspace of at
- * least sqa_workspace_bytes() bytes (fp32 split-KV partials, the per-segment
- * merge table and a device status word).  Every entry point is asynchronous on
+ * least sqa_workspace_bytes() bytes (fp32 split-KV partials and a device
+ * status word).  Every entry point is asynchronous on
  * the given stream and returns a status code; no C++ exception crosses the ABI.
  */
 #ifndef SMALL_Q_ATTENTION_H_
