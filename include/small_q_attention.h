@@ -155,8 +155,8 @@ SQA_API size_t sqa_workspace_bytes(const sqa_args* args, int device, int* status
  * Replaces small_q_attention_v3(...) (csrc/small_q_attention_ext.cu:1132-1210),
  * which the upstream binds as forward_v3 (:1384) and wraps in
  * small_q_attention.cuda.forward_v3 (src/small_q_attention/cuda.py:177-214).
- * Launches the split-KV partial kernel and, when a sequence was split over
- * several CTAs, the log-sum-exp merge kernel.  No device allocation, no host
+ * Launches the split-KV partial kernel and the log-sum-exp merge kernel (which
+ * only combines sequences split over several CTAs).  No device allocation, no host
  * synchronisation. */
 SQA_API int sqa_forward(const sqa_args* args, void* workspace, size_t workspace_bytes, void* stream);
 
