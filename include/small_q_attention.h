@@ -105,7 +105,7 @@ typedef struct sqa_args {
   int32_t num_ctas;
   int32_t min_pages_per_cta;
   /* Kernel choice: 0 = auto (tcgen05 for q_len >= 9, for q_len 5..8 above 512
-   * page-units, for q_len 3..4 from 2048 and for q_len <= 2 from 131072
+   * page-units, for q_len 3..4 from 2048 and for q_len <= 2 from 12288
    * page-units, where a page-unit is one page of one KV head, bounded by
    * max_seq_len or max_pages; warp-level otherwise),
    * 1 = warp-level mma.sync kernel, 2 = tcgen05 / tensor-memory kernel.

@@ -25,9 +25,9 @@ constexpr int kSmemPerCta = kSmemPerSm / kCtasPerSm - 1024;
 constexpr int kMaxSmemPerCta = 227 * 1024;  // dynamic shared memory limit of one CTA on sm_100
 // Auto kernel choice thresholds on the launch's upper bound of units (pages x KV
 // heads), from the 36-case matrix measured on B200 at 1965 MHz: the tcgen05
-// kernel from 131072 units for q_len <= 2, from 2048 for q_len 3..4, above 512
+// kernel from 12288 units for q_len <= 2, from 2048 for q_len 3..4, above 512
 // for q_len 5..8, always for q_len >= 9.
-constexpr long long kAutoTcUnitsQ2 = 131072;
+constexpr long long kAutoTcUnitsQ2 = 12288;
 constexpr long long kAutoTcUnitsQ4 = 2048;
 constexpr long long kAutoTcUnitsQ8 = 512;
 constexpr int kDefaultMinPagesPerCta = 4;
@@ -186,6 +186,8 @@ int validate(const sqa_args* a) {
   if (a->dtype != SQA_DTYPE_F16 && a->dtype != SQA_DTYPE_BF16) return SQA_ERR_UNSUPPORTED;
   if (a->kv_layout != SQA_KV_NHD && a->kv_layout != SQA_KV_HND) return SQA_ERR_UNSUPPORTED;
   if (a->kv_dtype != SQA_KV_SAME && a->kv_dtype != SQA_KV_FP8_E4M3) return SQA_ERR_UNSUPPORTED;
+  // the device schedule counts pages x KV heads in 32 bits
+  if ((long long)a->batch * a->max_pages * a->num_kv_heads > (1LL << 30)) return SQA_ERR_UNSUPPORTED;
   // fp8 caches run on the tcgen05 kernel (fp16 or bf16 queries)
   if (a->kv_dtype == SQA_KV_FP8_E4M3 && a->kernel == 1) return SQA_ERR_UNSUPPORTED;
   // a page must hold 16 x Hkv x 128 elements and start 16-byte aligned (TMA strides)

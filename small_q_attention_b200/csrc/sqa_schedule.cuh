@@ -15,6 +15,13 @@
 
 namespace sqa {
 
+// The charge for a segment start, only when the average range is at least 64
+// units: on calls of a few pages per CTA any charge rounds the busiest CTA's
+// share up by a page or more, which costs more than the extra epilogue.
+__device__ __forceinline__ int segment_cost(int seg_cost, long long total_units, int grid) {
+  return total_units >= 64LL * grid ? seg_cost : 0;
+}
+
 struct SegWalk {
   int b;          // sequence
   int h;          // KV head
@@ -97,28 +104,35 @@ __device__ __forceinline__ Schedule compute_schedule(const SplitKvParams& p) {
     if (blockIdx.x == 0 && lane == 0 && flags) atomicOr(p.status, flags);
   }
 
-  // cost of sequence b: Hkv segments of (pages + seg_cost) when it has pages
-  const long long seg_cost = p.seg_cost;
-  long long total_cost = 0;
+  // cost of sequence b: Hkv segments of (pages + seg_cost) when it has pages (32-bit:
+  // the host bounds batch x max_pages x Hkv)
+  const int total_units = total_pages * p.hkv;
+  const int seg_cost = (int)segment_cost(p.seg_cost, total_units, gridDim.x);
   int nonempty = 0;
+  if (seg_cost > 0) {
 #pragma unroll
-  for (int c = 0; c < kCachedChunks; ++c) nonempty += __popc(__ballot_sync(0xffffffffu, cached[c] > 0));
-  for (int base = kCachedChunks * 32; base < p.batch; base += 32) {
-    unsigned int unused = 0;
-    nonempty += __popc(__ballot_sync(0xffffffffu, pages_of(base + lane, unused) > 0));
+    for (int c = 0; c < kCachedChunks; ++c) nonempty += __popc(__ballot_sync(0xffffffffu, cached[c] > 0));
+    for (int base = kCachedChunks * 32; base < p.batch; base += 32) {
+      unsigned int unused = 0;
+      nonempty += __popc(__ballot_sync(0xffffffffu, pages_of(base + lane, unused) > 0));
+    }
   }
-  total_cost = ((long long)total_pages + seg_cost * nonempty) * p.hkv;
-  const long long per = max(1LL, (total_cost + gridDim.x - 1) / gridDim.x);
-  const long long x0 = min(total_cost, (long long)blockIdx.x * per);
-  const long long x1 = min(total_cost, x0 + per);
+  const int total_cost = total_units + seg_cost * nonempty * p.hkv;
+  const int per = max(1, (total_cost + (int)gridDim.x - 1) / (int)gridDim.x);
+  const int x0 = min(total_cost, (int)blockIdx.x * per);
+  const int x1 = min(total_cost, x0 + per);
 
   // Locate both ends: the sequence whose cost span holds x, then the head and the
-  // unit offset (cost positions in a segment's first seg_cost map to its start).
-  int start = total_pages * p.hkv, end = total_pages * p.hkv;
+  // unit offset (cost positions in a segment's first seg_cost map to its start;
+  // with seg_cost 0 cost and units coincide).
+  int start = total_units, end = total_units;
   int b0 = p.batch, u_b0 = 0, pages_b0 = 0;
+  if (seg_cost == 0) {
+    start = x0;
+    end = x1;
+  }
   if (x0 < x1) {
-    long long run_cost = 0;
-    int run_units = 0;
+    int run_cost = 0, run_units = 0;
     bool found0 = false;
     for (int base = 0; base < p.batch; base += 32) {
       const int c = base / 32;
@@ -130,44 +144,43 @@ __device__ __forceinline__ Schedule compute_schedule(const SplitKvParams& p) {
         unsigned int unused = 0;
         pg = pages_of(base + lane, unused);
       }
-      const long long cost = pg > 0 ? (long long)(pg + seg_cost) * p.hkv : 0;
-      long long incl = cost;
-      int incl_u = pg * p.hkv;
+      const int units = pg * p.hkv;
+      const int cost = pg > 0 ? (pg + seg_cost) * p.hkv : 0;
+      int incl = cost, incl_u = units;
 #pragma unroll
       for (int off = 1; off < 32; off <<= 1) {
-        const long long y = __shfl_up_sync(0xffffffffu, incl, off);
+        const int y = __shfl_up_sync(0xffffffffu, incl, off);
         const int yu = __shfl_up_sync(0xffffffffu, incl_u, off);
         if (lane >= off) {
           incl += y;
           incl_u += yu;
         }
       }
-      // unit position of cost x inside this lane's sequence
-      auto unit_at = [&](long long x) {
-        const long long xr = x - (run_cost + incl - cost);  // cost into this sequence
-        const long long span = pg + seg_cost;
-        const long long h = xr / span;
-        const long long r = xr - h * span;
-        return run_units + (incl_u - pg * p.hkv) + (int)(h * pg + max(r - seg_cost, 0LL));
+      // unit position of cost x inside lane l's sequence (evaluated by every lane for lane l)
+      auto unit_at = [&](int x, int l) {
+        const int xr = x - run_cost - __shfl_sync(0xffffffffu, incl - cost, l);  // cost into sequence
+        const int pgl = __shfl_sync(0xffffffffu, pg, l);
+        const int span = pgl + seg_cost;
+        const int h = xr / span;
+        const int r = xr - h * span;
+        return run_units + __shfl_sync(0xffffffffu, incl_u - units, l) + h * pgl + max(r - seg_cost, 0);
       };
       if (!found0) {
         const unsigned hit = __ballot_sync(0xffffffffu, run_cost + incl > x0);
         if (hit) {
           const int l = __ffs(hit) - 1;
-          const int st = unit_at(x0);
-          start = __shfl_sync(0xffffffffu, st, l);
+          if (seg_cost > 0) start = unit_at(x0, l);
           b0 = base + l;
-          u_b0 = run_units + __shfl_sync(0xffffffffu, incl_u - pg * p.hkv, l);
+          u_b0 = run_units + __shfl_sync(0xffffffffu, incl_u - units, l);
           pages_b0 = __shfl_sync(0xffffffffu, pg, l);
           found0 = true;
+          if (seg_cost == 0) break;  // end = x1 already
         }
       }
       if (found0) {
         const unsigned hit = __ballot_sync(0xffffffffu, run_cost + incl > x1);
         if (hit) {
-          const int l = __ffs(hit) - 1;
-          const int en = unit_at(x1);
-          end = __shfl_sync(0xffffffffu, en, l);
+          end = unit_at(x1, __ffs(hit) - 1);
           break;
         }
       }
@@ -245,13 +258,14 @@ __device__ __forceinline__ int2 segment_pieces(const int32_t* seq_lens, int batc
     if (hit) pages_b = __shfl_sync(0xffffffffu, pg, __ffs(hit) - 1);
   }
   if (pages_b == 0) return make_int2(0, 0);
-  const long long total_cost = (total_pages + (long long)seg_cost * nonempty) * hkv;
-  const long long per = max(1LL, (total_cost + grid - 1) / grid);
+  const int c = segment_cost(seg_cost, total_pages * hkv, grid);
+  const int total_cost = (int)total_pages * hkv + c * nonempty * hkv;
+  const int per = max(1, (total_cost + grid - 1) / grid);
   const int ne = nonempty_before * hkv + h;                            // non-empty segments before (b, h)
-  const long long seg_start = pages_before * hkv + (long long)h * pages_b;
-  const long long first_cost = seg_start + (long long)seg_cost * (ne + 1);
-  const int first_cta = (int)(first_cost / per);
-  const int last_cta = (int)((first_cost + pages_b - 1) / per);
+  const int seg_start = (int)pages_before * hkv + h * pages_b;
+  const int first_cost = seg_start + c * (ne + 1);
+  const int first_cta = first_cost / per;
+  const int last_cta = (first_cost + pages_b - 1) / per;
   return make_int2(first_cta + b * hkv + h, last_cta - first_cta + 1);
 }
 
