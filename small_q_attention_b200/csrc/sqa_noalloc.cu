@@ -26,7 +26,7 @@ namespace {
 constexpr int kMaxDevices = 64;
 constexpr size_t kStatusBytes = 256;  // the device status word lives at offset 0
 
-__device__ __align__(256) unsigned char g_noalloc_scratch[SQA_NOALLOC_SCRATCH_BYTES];
+static __device__ __align__(256) unsigned char g_noalloc_scratch[SQA_NOALLOC_SCRATCH_BYTES];
 
 std::mutex g_mu;
 void* g_scratch_addr[kMaxDevices] = {nullptr};
@@ -57,8 +57,8 @@ extern "C" SQA_API int sqa_forward_noalloc(const sqa_args* args, void* stream) {
   st = scratch_address(device, &scratch);
   if (st != SQA_OK) return st;
   // The array keeps the previous call's contents; only the sticky status word
-  // must start at zero (the merge table and partials are written before they
-  // are read within a call).
+  // must start at zero (the split partials are written before they are read
+  // within a call).
   if (cudaMemsetAsync(scratch, 0, kStatusBytes, static_cast<cudaStream_t>(stream)) != cudaSuccess)
     return SQA_ERR_CUDA;
   return sqa_forward(args, scratch, SQA_NOALLOC_SCRATCH_BYTES, stream);
