@@ -455,9 +455,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       prefetch_tensormap(&tm_v);
     }
     __syncwarp();
-#ifndef SQA_NO_START_PREFETCH
     prefetch_start<false>(p, &tm_k, &tm_v, p.num_stages);
-#endif
   }
   // Everything above writes only shared memory and reads the inputs only as
   // prefetch hints; the inputs and the workspace may still be in use by the

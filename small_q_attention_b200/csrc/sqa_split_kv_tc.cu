@@ -759,12 +759,10 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     prefetch_tensormap(&tm_k);
     prefetch_tensormap(&tm_v);
   }
-#ifndef SQA_NO_START_PREFETCH
   // The PV issuer has nothing to do before the first P: it prefetches this
   // CTA's first pages into L2 before the dependency wait (hints only), off the
   // start-up path of the other warps.
   if (warp == kPvWarp) prefetch_start<KV != 0>(p, &tm_k, &tm_v, p.num_stages * TcShape<KV>::kPages);
-#endif
   grid_dependency_wait();
   allow_dependent_launch();
   if (threadIdx.x == 0) {
