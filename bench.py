@@ -16,17 +16,25 @@ Reported:
                  query, page table and lengths copied from pinned host memory
                  and the output copied back every step (the KV cache is the
                  serving state and stays resident);
-* ``roofline``   the split-KV kernel alone: algorithmic bytes / its mean
-                 CUDA-event duration, against the measured HBM copy bandwidth;
+* ``roofline``   the split-KV kernel: algorithmic bytes / its mean duration
+                 between CUDA events recorded as graph nodes around each of its
+                 launches in a replay of the same K calls (and, beside it, with
+                 eager launches), against the measured HBM copy bandwidth;
+                 ``frac_step`` is the whole step (split + merge) against the same peak;
 * ``cpu_baseline`` the CPU oracle (numpy restatement of the upstream reference)
-                 on the host cores, on a bounded sample of the same workload.
+                 on the host cores, on a bounded sample of the same workload;
+* ``sharded``    cfg3 (KV-head shards), cfg4 (LPT batch shards) and cfg5
+                 (long-context split + merge) at this N, strong scaling, device leg;
+* ``matrix``     (N=1) the 36-case matrix and the five named configs: graph p50
+                 and the upstream's eager per-call p50, TB/s, fraction of peak,
+                 the kernel chosen.
 
 ``--impl reference`` times the upstream algorithm on the CPU (the oracle port:
 the upstream reference is a Python/torch CPU function that does not travel to
 the GPU box) on the same workload; rank 0 only.
 
 ``--matrix PATH`` instead writes one JSONL row per case of the 36-case matrix
-and the five named configurations (µs/call p50, TB/s, fraction of peak).
+and the five named configurations (slower, 1 s of clock settle per case).
 """
 
 from __future__ import annotations
@@ -59,9 +67,6 @@ def _peaks():
 
 
 KERNEL_NAMES = {1: "sqa_split_kv_kernel", 2: "sqa_split_kv_tc_kernel"}
-DTYPES = {}  # filled lazily (torch is imported inside the run functions)
-
-
 def _as_dtype(c, name):
     """A workload dict with its Q/K/V cast to ``name`` ("f16" leaves it as generated)."""
     if name == "f16":
@@ -276,89 +281,105 @@ def _rank_cases(name, world, rank, device, n_rep):
     raise ValueError(name)
 
 
-def run_ours(args):
-    import ctypes
+class DeviceArm:
+    """One rank's inputs for a workload and the operator call on them (the C ABI,
+    arguments packed once per replica, as a serving loop holds them)."""
 
-    import torch
+    def __init__(self, name, args, world, rank, device, dist, lib):
+        import ctypes
 
-    import small_q_attention_b200 as sqa
-    from small_q_attention_b200 import _native
-    from small_q_attention_b200.attention import _fill_args
-    from small_q_attention_b200.sharding import gather_partials, long_context_attention
+        import torch
 
-    world, rank, local = _dist()
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
-    dist = _init_pg(world, "nccl")
-    lib = _native.library()
-    peak_gbs, peak_src = _peaks()
-    name = args.workload
-    longctx = name == "cfg5"
+        from small_q_attention_b200 import _native
+        from small_q_attention_b200.attention import _fill_args
 
-    reps, bytes_rank, bytes_job = _rank_cases(name, world, rank, device, REPLICAS)
-    max_len = max(max(r["lens"]) for r in reps)
-    ws_bytes = 0
-    cargs, outs, lses = [], [], []
-    for r in reps:
-        a = _fill_args(r["query"], r["key_cache"], r["value_cache"], r["block_tables"], r["seq_lens"],
-                       r.get("mask_lens"), max_len, 0, 0, args.kernel)
-        if longctx:
-            o = torch.empty(r["query"].shape, dtype=torch.float32, device=device)
-            l = torch.empty(r["query"].shape[:3], dtype=torch.float32, device=device)
-            a.out_partial, a.out_lse = o.data_ptr(), l.data_ptr()
-            lses.append(l)
-        else:
-            o = torch.empty_like(r["query"])
-            a.out = o.data_ptr()
-        outs.append(o)
-        cargs.append(a)
-        st = ctypes.c_int(0)
-        ws_bytes = max(ws_bytes, lib.sqa_workspace_bytes(ctypes.byref(a), local, ctypes.byref(st)))
-        _native.check(st.value, "sqa_workspace_bytes")
-    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=device)
-    merged = torch.empty(reps[0]["query"].shape, dtype=torch.float16, device=device)
-    kernel_id = lib.sqa_selected_kernel(ctypes.byref(cargs[0]), local)  # what kernel=args.kernel resolves to
-    if kernel_id < 0:
-        _native.check(-kernel_id, "sqa_selected_kernel")
+        self.name, self.world, self.rank, self.dist, self.lib = name, world, rank, dist, lib
+        self.longctx = name == "cfg5"
+        self.reps, self.bytes_rank, self.bytes_job = _rank_cases(name, world, rank, device, REPLICAS)
+        self.max_len = max(max(r["lens"]) for r in self.reps)
+        self.cargs, self.outs, self.lses = [], [], []
+        ws_bytes = 0
+        for r in self.reps:
+            a = _fill_args(r["query"], r["key_cache"], r["value_cache"], r["block_tables"], r["seq_lens"],
+                           r.get("mask_lens"), self.max_len, 0, 0, args.kernel)
+            if self.longctx:
+                o = torch.empty(r["query"].shape, dtype=torch.float32, device=device)
+                l = torch.empty(r["query"].shape[:3], dtype=torch.float32, device=device)
+                a.out_partial, a.out_lse = o.data_ptr(), l.data_ptr()
+                self.lses.append(l)
+            else:
+                o = torch.empty_like(r["query"])
+                a.out = o.data_ptr()
+            self.outs.append(o)
+            self.cargs.append(a)
+            st = ctypes.c_int(0)
+            ws_bytes = max(ws_bytes, lib.sqa_workspace_bytes(ctypes.byref(a), device.index, ctypes.byref(st)))
+            _native.check(st.value, "sqa_workspace_bytes")
+        self.ws_bytes = ws_bytes
+        self.ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=device)
+        self.merged = torch.empty(self.reps[0]["query"].shape, dtype=torch.float16, device=device)
+        self.kernel_id = lib.sqa_selected_kernel(ctypes.byref(self.cargs[0]), device.index)
+        if self.kernel_id < 0:
+            _native.check(-self.kernel_id, "sqa_selected_kernel")
+        # our kernels per step: split-KV + per-call merge (+ the cross-rank merge in long-context mode)
+        self.launches_per_step = 3 if self.longctx else 2
 
-    def call(i, stream, ev0=None, ev1=None):
-        a = cargs[i % REPLICAS]
+    def call(self, i, stream, ev0=None, ev1=None):
+        import ctypes
+
+        import small_q_attention_b200 as sqa
+        from small_q_attention_b200 import _native
+        from small_q_attention_b200.sharding import gather_partials
+
+        lib, a = self.lib, self.cargs[i % REPLICAS]
         if ev0 is None:
-            code = lib.sqa_forward(ctypes.byref(a), ctypes.c_void_p(ws.data_ptr()), ctypes.c_size_t(ws_bytes),
-                                   ctypes.c_void_p(stream))
+            code = lib.sqa_forward(ctypes.byref(a), ctypes.c_void_p(self.ws.data_ptr()),
+                                   ctypes.c_size_t(self.ws_bytes), ctypes.c_void_p(stream))
         else:
-            code = lib.sqa_forward_timed(ctypes.byref(a), ctypes.c_void_p(ws.data_ptr()),
-                                         ctypes.c_size_t(ws_bytes), ctypes.c_void_p(stream),
+            code = lib.sqa_forward_timed(ctypes.byref(a), ctypes.c_void_p(self.ws.data_ptr()),
+                                         ctypes.c_size_t(self.ws_bytes), ctypes.c_void_p(stream),
                                          ctypes.c_void_p(ev0), ctypes.c_void_p(ev1))
         _native.check(code, "sqa_forward")
-        if longctx:  # the exchange step: gather every rank's (O, LSE), merge on every rank
+        if self.longctx:  # the exchange step: gather every rank's (O, LSE), merge
             j = i % REPLICAS
-            if dist is not None:
-                parts_o, parts_lse = gather_partials(outs[j], lses[j])
+            if self.dist is not None:
+                parts_o, parts_lse = gather_partials(self.outs[j], self.lses[j])
             else:
-                parts_o, parts_lse = outs[j][None], lses[j][None]
-            sqa.merge_partials(parts_o, parts_lse, out=merged)
+                parts_o, parts_lse = self.outs[j][None], self.lses[j][None]
+            sqa.merge_partials(parts_o, parts_lse, out=self.merged)
 
+
+def measure_device(arm, args, device, with_clocks=True):
+    """Device throughput of K steps replayed from one CUDA graph (inputs resident),
+    the max over ranks; then the split-KV kernel's own duration, inside a replay
+    of the same K calls (events as graph nodes) and eagerly (an event pair per launch)."""
+    import torch
+
+    K, W, dist = args.steps, args.warmup, arm.dist
     stream = torch.cuda.Stream(device)
     sh = stream.cuda_stream
-    K, W = args.steps, args.warmup
-
-    # --- warm-up (eager), then capture exactly K steps in one graph
     with torch.cuda.stream(stream):
         for i in range(W):
-            call(i, sh)
+            arm.call(i, sh)
     stream.synchronize()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
         for i in range(K):
-            call(i, torch.cuda.current_stream().cuda_stream)
+            arm.call(i, torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
-    graph.replay()  # warm the graph itself
-    torch.cuda.synchronize()
+    # warm replays (untimed) so that the timed replay starts at the clock of a busy GPU
+    t_warm = time.perf_counter()
+    while True:
+        graph.replay()
+        torch.cuda.synchronize()
+        if time.perf_counter() - t_warm > 0.05:
+            break
 
-    # --- timed region: K steps, barrier + synchronize on both sides
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
+    clocks = ClockSampler(device.index) if with_clocks else None
+    if clocks:
+        clocks.__enter__()
+    try:
         if dist is not None:
             dist.barrier()
         torch.cuda.synchronize()
@@ -369,26 +390,59 @@ def run_ours(args):
         torch.cuda.synchronize()
         if dist is not None:
             dist.barrier()
+    finally:
+        if clocks:
+            clocks.__exit__()
     t_ms = _max_over_ranks(start.elapsed_time(end), dist, device)
-    value_tbs = K * bytes_job / (t_ms * 1e-3) / 1e12
-    del graph  # holds NCCL work in the long-context mode: release before the group
+    del graph  # holds NCCL work in the long-context mode: release it before the group
 
-    # --- roofline: the split-KV kernel alone, one event pair per launch (this rank)
+    # the split-KV kernel inside a replay of the same K calls: its launches bracketed by
+    # event-record nodes (which also order the kernel after the previous call's merge)
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
     for e0, e1 in evs:  # create the underlying CUDA events
         e0.record(stream)
         e1.record(stream)
     torch.cuda.synchronize()
+    kern_graph_ms = None
+    try:
+        g2 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g2, stream=stream):
+            for i, (e0, e1) in enumerate(evs):
+                arm.call(i, torch.cuda.current_stream().cuda_stream, e0.cuda_event, e1.cuda_event)
+        torch.cuda.synchronize()
+        g2.replay()
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            g2.replay()
+        torch.cuda.synchronize()
+        kern_graph_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs)
+        del g2
+    except Exception as e:  # event nodes not capturable here: the eager figure stands alone
+        print(f"bench: in-graph kernel timing unavailable ({e})", file=sys.stderr)
+    # the same kernel launched eagerly, one event pair per launch
     with torch.cuda.stream(stream):
         for i, (e0, e1) in enumerate(evs):
-            call(i, sh, e0.cuda_event, e1.cuda_event)
+            arm.call(i, sh, e0.cuda_event, e1.cuda_event)
     torch.cuda.synchronize()
-    kern_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs)
-    kern_bytes = bytes_rank + (2 * 16 * 32 * 128 * 2 if longctx else 0)
-    achieved_gbs = kern_bytes / (kern_ms * 1e-3) / 1e9
+    kern_eager_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs)
+    return {"t_ms": t_ms, "kern_graph_ms": kern_graph_ms, "kern_eager_ms": kern_eager_ms,
+            "clocks": clocks.summary() if clocks else None}
 
-    # --- e2e through the public API with host buffers: the step's small inputs
-    # (Q, page table, lengths) go up in one pinned copy, the output comes back
+
+def measure_e2e(arm, args, device):
+    """The metric end to end through the public Python API with host buffers: each
+    step's query, page table and lengths go up from pinned host memory in one
+    packed copy and the output comes back (the KV cache is serving state and
+    stays resident).  pipelined: the H2D copy runs on a copy stream and may
+    overlap the previous step's kernel, the D2H read on a second copy stream after
+    the step's kernel (a serving loop's pipeline); serial: all on one stream."""
+    import torch
+
+    import small_q_attention_b200 as sqa
+    from small_q_attention_b200.sharding import long_context_attention
+
+    K, W, dist = args.steps, args.warmup, arm.dist
+    reps, longctx = arm.reps, arm.longctx
     small = ("query", "block_tables", "seq_lens") + (("mask_lens",) if longctx else ())
 
     def _packed(r, pin):
@@ -414,71 +468,140 @@ def run_ours(args):
     h2d = host_in[0].numel()
     d2h = host_out.numel() * host_out.element_size()
     e2e_out = [torch.empty_like(r["query"]) for r in reps]
-
-    # A serving loop's pipeline: each step's H2D copy runs on a copy stream and may
-    # overlap the previous step's kernel; the step's D2H read runs on a second copy
-    # stream after its kernel.  Every step's copies are inside the timed region.
+    stream = torch.cuda.Stream(device)
     s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
     ev_in = [torch.cuda.Event() for _ in range(REPLICAS)]
     ev_done = [torch.cuda.Event() for _ in range(REPLICAS)]
     ev_out = [torch.cuda.Event() for _ in range(REPLICAS)]
+    pipelined = args.e2e_mode == "pipelined"
+    set_stream = torch.cuda.set_stream
 
-    def e2e_step(i):
+    def attend(j):
+        d = dev_in[j][1]
+        if longctx:
+            return long_context_attention(d["query"], reps[j]["key_cache"], reps[j]["value_cache"],
+                                          d["block_tables"], d["seq_lens"], d["mask_lens"], 16, out=e2e_out[j],
+                                          workspace=arm.ws)
+        return sqa.small_q_attention(d["query"], reps[j]["key_cache"], reps[j]["value_cache"], d["block_tables"],
+                                     d["seq_lens"], 16, arm.max_len, out=e2e_out[j], workspace=arm.ws,
+                                     kernel=args.kernel)
+
+    def step(i):
         j = i % REPLICAS
-        s_in.wait_event(ev_done[j])  # the kernel that last read dev_in[j] has finished
-        with torch.cuda.stream(s_in):
+        if not pipelined:  # `stream` is current
             dev_in[j][0].copy_(host_in[j], non_blocking=True)
-            ev_in[j].record(s_in)
+            host_out.copy_(attend(j), non_blocking=True)
+            return
+        s_in.wait_event(ev_done[j])  # the kernel that last read dev_in[j] has finished
+        set_stream(s_in)
+        dev_in[j][0].copy_(host_in[j], non_blocking=True)
+        ev_in[j].record(s_in)
+        set_stream(stream)
         stream.wait_event(ev_in[j])
         stream.wait_event(ev_out[j])  # the D2H that last read e2e_out[j] has finished
-        d = dev_in[j][1]
-        # `stream` is the current stream for the whole loop (set once below)
-        if longctx:
-            o = long_context_attention(d["query"], reps[j]["key_cache"], reps[j]["value_cache"],
-                                       d["block_tables"], d["seq_lens"], d["mask_lens"], 16, out=e2e_out[j],
-                                       workspace=ws)
-        else:
-            o = sqa.small_q_attention(d["query"], reps[j]["key_cache"], reps[j]["value_cache"],
-                                      d["block_tables"], d["seq_lens"], 16, max_len, out=e2e_out[j],
-                                      workspace=ws, kernel=args.kernel)
+        o = attend(j)
         ev_done[j].record(stream)
         s_out.wait_event(ev_done[j])
-        with torch.cuda.stream(s_out):
-            host_out.copy_(o, non_blocking=True)
-            ev_out[j].record(s_out)
+        set_stream(s_out)
+        host_out.copy_(o, non_blocking=True)
+        ev_out[j].record(s_out)
+        set_stream(stream)
 
-    with torch.cuda.stream(stream):
+    prev = torch.cuda.current_stream(device)
+    set_stream(stream)
+    try:
         for i in range(W):
-            e2e_step(i)
-    torch.cuda.synchronize()
-    if dist is not None:
-        dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
+            step(i)
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
         s_in.wait_stream(stream)
         for i in range(K):
-            e2e_step(i)
+            step(i)
         for ev in ev_out:
             stream.wait_event(ev)
         e1.record(stream)
-    torch.cuda.synchronize()
+        torch.cuda.synchronize()
+    finally:
+        set_stream(prev)
     e2e_ms = _max_over_ranks(e0.elapsed_time(e1), dist, device)
-    e2e_tbs = K * bytes_job / (e2e_ms * 1e-3) / 1e12
+    return {"e2e_ms": e2e_ms, "h2d": h2d, "d2h": d2h}
+
+
+def _sharded_line(arm, res, args, peak_gbs):
+    K = args.steps
+    return {"workload": WORKLOADS[arm.name], "value": round(K * arm.bytes_job / (res["t_ms"] * 1e-3) / 1e12, 4),
+            "unit": "TB/s", "us_per_call": round(res["t_ms"] / K * 1e3, 3),
+            "algorithmic_bytes_per_call": arm.bytes_job,
+            "scaling": "strong", "kernel": KERNEL_NAMES[arm.kernel_id],
+            "per_gpu_frac": round(K * arm.bytes_job / (res["t_ms"] * 1e-3) / 1e9 / arm.world / peak_gbs, 4)}
+
+
+def run_ours(args):
+    import torch
+
+    from small_q_attention_b200 import _native
+
+    world, rank, local = _dist()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    dist = _init_pg(world, "nccl")
+    lib = _native.library()
+    peak_gbs, peak_src = _peaks()
+    name = args.workload
+    K, W = args.steps, args.warmup
+
+    arm = DeviceArm(name, args, world, rank, device, dist, lib)
+    res = measure_device(arm, args, device)
+    t_ms = res["t_ms"]
+    value_tbs = K * arm.bytes_job / (t_ms * 1e-3) / 1e12
+    kern_bytes = arm.bytes_rank + (2 * 16 * 32 * 128 * 2 if arm.longctx else 0)
+    kern_ms = res["kern_graph_ms"] if res["kern_graph_ms"] is not None else res["kern_eager_ms"]
+    achieved_gbs = kern_bytes / (kern_ms * 1e-3) / 1e9
+    eager_gbs = kern_bytes / (res["kern_eager_ms"] * 1e-3) / 1e9
+    e2e = measure_e2e(arm, args, device)
+    e2e_tbs = K * arm.bytes_job / (e2e["e2e_ms"] * 1e-3) / 1e12
+    launches = arm.launches_per_step * K
+    main_desc = dict(kernel_id=arm.kernel_id, max_len=arm.max_len, q=arm.reps[0]["query"],
+                     cache_mb=REPLICAS * arm.reps[0]["key_cache"].numel() * 4 / 1e6, bytes_job=arm.bytes_job)
+    del arm
+    torch.cuda.empty_cache()
+
+    # the sharded configurations at this N (strong scaling), the device leg only
+    sharded = {}
+    if not args.no_sharded:
+        for sub in ("cfg3", "cfg4", "cfg5"):
+            if sub == name:
+                continue
+            sarm = DeviceArm(sub, args, world, rank, device, dist, lib)
+            sres = measure_device(sarm, args, device, with_clocks=False)
+            sharded[sub] = _sharded_line(sarm, sres, args, peak_gbs)
+            del sarm
+            torch.cuda.empty_cache()
+
+    # --- the 36-case matrix and the named configs (N=1 only: it would hold every GPU)
+    matrix = None
+    if world == 1 and not args.no_matrix:
+        matrix = matrix_rows(args, settle=args.settle_line, replica_mb=args.matrix_replica_mb, verbose=False)
 
     # --- CPU baseline: the oracle on a bounded sample (rank 0, N=1, the cfg2 line only)
     cpu = None
     if rank == 0 and world == 1 and name == "cfg2" and not args.no_cpu_baseline:
-        times = time_oracle(reps[0], args.cpu_seconds)
+        from small_q_attention_b200.workloads import make_config
+
+        c0 = make_config("cfg2", seed=0, device=device)
+        times = time_oracle(c0, args.cpu_seconds)
         t = statistics.median(times)
-        cpu = {"value": bytes_rank / t / 1e12, "unit": "TB/s", "cores": _cpu_cores(), "kind": "port",
+        cpu = {"value": _case_bytes(c0) / t / 1e12, "unit": "TB/s", "cores": _cpu_cores(), "kind": "port",
                "sample": f"{len(times)} whole cfg2 calls (B=4,q=4,kv=8192) of the numpy oracle, "
                          f"median {t * 1e3:.1f} ms/call, {_cpu_model()}"}
 
     if dist is not None:
         dist.barrier()
     if rank == 0:
-        q = reps[0]["query"]
+        q = main_desc["q"]
         line = {
             "metric": METRIC, "value": round(value_tbs, 4), "unit": "TB/s", "n_gpus": world, "steps": K,
             "warmup": W, "ms_per_step": round(t_ms / K, 6), "higher_is_better": True,
@@ -487,25 +610,41 @@ def run_ours(args):
             "config": {"workload": WORKLOADS[name],
                        "global_batch": (q.shape[0] * world if name == "cfg2" else
                                         {"cfg3": 16, "cfg4": 64, "cfg5": 1}[name]),
-                       "seq_len": max_len if name != "cfg5" else 262144, "q_len": int(q.shape[1]),
+                       "seq_len": main_desc["max_len"] if name != "cfg5" else 262144, "q_len": int(q.shape[1]),
                        "parallelism": {"cfg2": f"batch-shard x{world}", "cfg3": f"kv-head-shard x{world}",
                                        "cfg4": f"batch-shard (LPT) x{world}",
                                        "cfg5": f"kv-range split x{world} + NCCL all-gather"}[name],
                        "l2": f"inputs rotated over {REPLICAS} replicas per GPU "
-                             f"({REPLICAS * reps[0]['key_cache'].numel() * 4 / 1e6:.0f} MB > 126 MB L2)",
+                             f"({main_desc['cache_mb']:.0f} MB > 126 MB L2)",
                        "us_per_call": round(t_ms / K * 1e3, 3),
-                       "algorithmic_bytes_per_call": bytes_job},
+                       "algorithmic_bytes_per_call": main_desc["bytes_job"]},
             "roofline": {"bound": "hbm", "achieved": round(achieved_gbs, 1), "peak": peak_gbs, "unit": "GB/s",
                          "frac": round(achieved_gbs / peak_gbs, 4), "peak_source": f"{peak_src} hbm_gbs (burst)",
-                         "traffic": _traffic(name, kernel_id) if world == 1 else None,
-                         "kernel": KERNEL_NAMES[kernel_id],
-                         "kernel_us": round(kern_ms * 1e3, 3), "rank": 0},
+                         "traffic": _traffic(name, main_desc["kernel_id"]) if world == 1 else None,
+                         "kernel": KERNEL_NAMES[main_desc["kernel_id"]],
+                         "kernel_us": round(kern_ms * 1e3, 3),
+                         "kernel_timing": ("CUDA events recorded as graph nodes around the split-KV launch of each "
+                                           "of the K calls, one graph replay (rank 0)"
+                                           if res["kern_graph_ms"] is not None else
+                                           "eager launches, one CUDA event pair per launch (rank 0)"),
+                         "kernel_us_eager": round(res["kern_eager_ms"] * 1e3, 3),
+                         "frac_eager": round(eager_gbs / peak_gbs, 4),
+                         "frac_step": round(value_tbs * 1e3 / world / peak_gbs, 4),
+                         "frac_step_def": "algorithmic bytes per GPU / ms_per_step (split-KV + merge kernels, "
+                                          "back to back in the timed graph) / peak",
+                         "rank": 0},
             "cpu_baseline": cpu,
-            "e2e": {"value": round(e2e_tbs, 4), "unit": "TB/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "us_per_step": round(e2e_ms / K * 1e3, 3)},
-            "clocks": clocks.summary(),
-            "gpu_launches": (3 if longctx else 2) * K,
+            "e2e": {"value": round(e2e_tbs, 4), "unit": "TB/s", "h2d_bytes_per_step": e2e["h2d"],
+                    "d2h_bytes_per_step": e2e["d2h"], "us_per_step": round(e2e["e2e_ms"] / K * 1e3, 3),
+                    "mode": args.e2e_mode,
+                    "api": "small_q_attention_b200.small_q_attention (torch extension over the C ABI)"},
+            "clocks": res["clocks"],
+            "gpu_launches": launches,
         }
+        if sharded:
+            line["sharded"] = sharded
+        if matrix is not None:
+            line["matrix"] = matrix
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.barrier()
@@ -581,49 +720,57 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
-def run_matrix(args):
-    """Per-case p50 µs/call and TB/s over the 36-case matrix and the named configs."""
+def _matrix_cases(only=None):
+    from small_q_attention_b200.workloads import CONFIGS, matrix_cases
+
+    cases = [(f"q{c['q_len']}_kv{c['kv_len']}_b{c['batch']}", c) for c in matrix_cases()]
+    cases += [(n, None) for n in CONFIGS]
+    if only:  # config names, "q<N>" for a q_len, or case labels like q16_kv8192_b16
+        cases = [(n, c) for n, c in cases if n in only or (c and f"q{c['q_len']}" in only)]
+    return cases
+
+
+def matrix_rows(args, settle: float = 1.0, replica_mb: float = 400.0, verbose: bool = True):
+    """Per case of the 36-cell matrix and the five named configs, through the public API:
+
+    * ``p50_us``: CUDA graph of >= 20 back-to-back calls rotating over enough distinct
+      input replicas (>= ``replica_mb`` of K/V) that no call finds its pages in L2;
+      median over 5 replays; ``tb_s`` / ``roofline_frac`` from it;
+    * ``eager_p50_us``: the upstream's protocol (``scripts/run_gpu_matrix.py:63-81``):
+      5 warm-up calls, then 15 calls on the same inputs, a CUDA event pair around each
+      call and a synchronise after it, median -- comparable cell for cell with the
+      upstream's published per-call latencies (the same inputs every call, so small
+      cases may be served from L2, as the upstream's were).
+    """
     import torch
 
     import small_q_attention_b200 as sqa
-    from small_q_attention_b200.workloads import CONFIGS, make_case, make_config, matrix_cases
+    from small_q_attention_b200.workloads import make_case, make_config
 
     torch.cuda.set_device(0)
-    DTYPES.update({"f16": torch.float16, "bf16": torch.bfloat16})
     peak_gbs, peak_src = _peaks()
     rows = []
-    # one explicit workspace, large enough for every case (16 KV-head segments x 64 rows worst case)
-    ws = torch.zeros(64 << 20, dtype=torch.uint8, device="cuda")
-    cases = [("matrix", c) for c in matrix_cases()] + [(n, None) for n in CONFIGS]
-    if args.only:  # config names, "q<N>" for a q_len, or case labels like q16_kv8192_b16
-        def label_of(n, c):
-            return n if c is None else f"q{c['q_len']}_kv{c['kv_len']}_b{c['batch']}"
-        cases = [(n, c) for n, c in cases
-                 if label_of(n, c) in args.only or (c and f"q{c['q_len']}" in args.only)]
-    for name, c in cases:
+    ws = torch.zeros(64 << 20, dtype=torch.uint8, device="cuda")  # one workspace for every case
+
+    def make(name, c, seed):
         if c is None:
-            first = _as_dtype(make_config(name, seed=0), args.dtype)
-            label = name
-        else:
-            first = _as_dtype(make_case(c["batch"], c["q_len"], [c["kv_len"]] * c["batch"], pool_factor=1.0,
-                                        page_mode=args.page_mode, seed=0), args.dtype)
-            label = f"q{c['q_len']}_kv{c['kv_len']}_b{c['batch']}"
+            return _as_dtype(make_config(name, seed=seed), args.dtype)
+        return _as_dtype(make_case(c["batch"], c["q_len"], [c["kv_len"]] * c["batch"], pool_factor=1.0,
+                                   page_mode=args.page_mode, seed=seed), args.dtype)
+
+    for label, c in _matrix_cases(args.only):
+        first = make(label, c, 0)
         nb = _case_bytes(first)
-        # distinct input copies so that consecutive calls never find K/V in L2:
-        # at least 2 and enough for >= 400 MB of caches in rotation (at most 64)
         cache_bytes = first["key_cache"].numel() * first["key_cache"].element_size() * 2
-        n_rep = max(2, min(64, math.ceil(400e6 / max(1, cache_bytes))))
-        inst = [first]
-        for s_ in range(1, n_rep):
-            if c is None:
-                inst.append(_as_dtype(make_config(name, seed=s_), args.dtype))
-            else:
-                inst.append(_as_dtype(make_case(c["batch"], c["q_len"], [c["kv_len"]] * c["batch"], pool_factor=1.0,
-                                                page_mode=args.page_mode, seed=s_), args.dtype))
+        n_rep = max(2, min(64, math.ceil(replica_mb * 1e6 / max(1, cache_bytes))))
+        inst = [first] + [make(label, c, s_) for s_ in range(1, n_rep)]
         outs = [torch.empty_like(x["query"]) for x in inst]
         fn = lambda i: sqa.small_q_attention(  # noqa: E731
             inst[i]["query"], inst[i]["key_cache"], inst[i]["value_cache"], inst[i]["block_tables"],
             inst[i]["seq_lens"], 16, max(inst[i]["lens"]), out=outs[i], workspace=ws, kernel=args.kernel)
+        kernel_id = sqa.selected_kernel(inst[0]["query"], inst[0]["key_cache"], inst[0]["value_cache"],
+                                        inst[0]["block_tables"], inst[0]["seq_lens"], 16, max(inst[0]["lens"]),
+                                        kernel=args.kernel)
         for i in range(5):
             fn(i % len(inst))
         torch.cuda.synchronize()
@@ -638,7 +785,7 @@ def run_matrix(args):
         # A burst of heavy cases leaves the SM clock low for up to ~2 s afterwards
         # (measured: ~1.1 GHz with no throttle reason reported); let it recover so
         # every case is timed at the same clock, and record the clock per case.
-        time.sleep(args.settle)
+        time.sleep(settle)
         g.replay()
         torch.cuda.synchronize()
         samples = []
@@ -650,24 +797,45 @@ def run_matrix(args):
                 e1.record()
                 torch.cuda.synchronize()
                 samples.append(e0.elapsed_time(e1) * 1e3 / reps)
+            # the upstream's per-call protocol on replica 0
+            for _ in range(5):
+                fn(0)
+            torch.cuda.synchronize()
+            eager = []
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            for _ in range(15):
+                e0.record()
+                fn(0)
+                e1.record()
+                e1.synchronize()
+                eager.append(e0.elapsed_time(e1) * 1e3)
         us = statistics.median(samples)
+        eager_us = statistics.median(eager)
         bits = sqa.read_device_status(ws.data_ptr(), clear=True)
         if bits:
             detail = int(ws[4:8].view(torch.int32).item())
             raise RuntimeError(f"{label}: device status bits {bits:#x}, detail {detail:#010x}")
+        cs = clocks.summary()
         row = {"case": label, "q_len": inst[0]["query"].shape[1], "batch": inst[0]["query"].shape[0],
                "kv_len_max": max(inst[0]["lens"]), "page_mode": args.page_mode if c else "random",
-               "p50_us": round(us, 3), "min_us": round(min(samples), 3), "alg_bytes": nb,
-               "tb_s": round(nb / (us * 1e-6) / 1e12, 4),
-               "roofline_frac": round(nb / (us * 1e-6) / 1e9 / peak_gbs, 4), "peak_gbs": peak_gbs,
-               "peak_source": peak_src, "n_gpus": 1, "replicas": n_rep, "kernel": args.kernel,
-               "sm_mhz": clocks.summary()["sm_mhz"], "clock_reasons": clocks.summary()["reasons"],
-               "dtype": args.dtype,
-               "timing": f"CUDA graph of {reps} back-to-back calls over rotating replicas, median of 5"}
+               "kernel": KERNEL_NAMES[kernel_id], "p50_us": round(us, 3), "min_us": round(min(samples), 3),
+               "alg_bytes": nb, "tb_s": round(nb / (us * 1e-6) / 1e12, 4),
+               "roofline_frac": round(nb / (us * 1e-6) / 1e9 / peak_gbs, 4),
+               "eager_p50_us": round(eager_us, 3), "eager_tb_s": round(nb / (eager_us * 1e-6) / 1e12, 4),
+               "peak_gbs": peak_gbs, "peak_source": peak_src, "replicas": n_rep, "sm_mhz": cs["sm_mhz"],
+               "clock_reasons": cs["reasons"], "dtype": args.dtype}
+        if verbose:
+            row["timing"] = (f"p50: CUDA graph of {reps} back-to-back calls over rotating replicas, median of 5; "
+                             "eager: upstream per-call protocol, median of 15")
+            print(json.dumps(row), flush=True)
         rows.append(row)
-        print(json.dumps(row), flush=True)
         del g, inst, outs
         torch.cuda.empty_cache()
+    return rows
+
+
+def run_matrix(args):
+    rows = matrix_rows(args, settle=args.settle, replica_mb=args.matrix_replica_mb)
     if args.matrix:
         Path(args.matrix).parent.mkdir(parents=True, exist_ok=True)
         Path(args.matrix).write_text("".join(json.dumps(r) + "\n" for r in rows))
@@ -694,6 +862,14 @@ def main():
                     help="matrix: seconds of idle before timing each case (clock recovery)")
     ap.add_argument("--kernel", type=int, default=0, choices=(0, 1, 2),
                     help="0 auto, 1 warp-level mma.sync kernel, 2 tcgen05 kernel")
+    ap.add_argument("--e2e-mode", default="pipelined", choices=("pipelined", "serial"),
+                    help="e2e: copies on their own streams overlapping the kernels, or all on one stream")
+    ap.add_argument("--no-matrix", action="store_true", help="leave the matrix out of the N=1 line")
+    ap.add_argument("--no-sharded", action="store_true", help="leave the cfg3/cfg4/cfg5 sub-results out")
+    ap.add_argument("--settle-line", type=float, default=0.2,
+                    help="matrix inside the driver line: seconds of idle before each case")
+    ap.add_argument("--matrix-replica-mb", type=float, default=400.0,
+                    help="matrix: MB of distinct K/V replicas rotated per case (>= 126 MB L2)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

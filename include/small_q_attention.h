@@ -162,8 +162,10 @@ SQA_API int sqa_forward(const sqa_args* args, void* workspace, size_t workspace_
 
 /* sqa_forward that also records the caller's CUDA events (cudaEvent_t, may be
  * NULL) on `stream` immediately before and after the split-KV kernel launch,
- * so the dominant kernel can be timed with events on its own stream.  Does
- * the same work as sqa_forward.  No upstream counterpart (measurement hook). */
+ * so the dominant kernel can be timed with events on its own stream.  Under
+ * stream capture the records become event-record nodes of the graph
+ * (cudaEventRecordExternal), timing the kernel inside each replay.  Does the
+ * same work as sqa_forward.  No upstream counterpart (measurement hook). */
 SQA_API int sqa_forward_timed(const sqa_args* args, void* workspace, size_t workspace_bytes, void* stream,
                               void* event_before, void* event_after);
 
@@ -203,16 +205,25 @@ SQA_API int sqa_workspace_init(void* workspace, size_t workspace_bytes, void* st
  * synchronise the device) in the middle of a decode step.
  * - Every GPU that loads the library holds the array until the process exits.
  * - The first call with a device current looks up the array's device address
- *   on that device; make that first call before any stream capture.
+ *   on that device; make that first call before any stream capture.  The
+ *   address is kept for the device's primary context: calls after
+ *   cudaDeviceReset, or under another context, are not supported.
  * - Shapes whose sqa_workspace_bytes() exceeds SQA_NOALLOC_SCRATCH_BYTES are
  *   rejected with SQA_ERR_WORKSPACE_TOO_SMALL.
  * - All calls share the one array: calls that overlap on the GPU (other
  *   streams, other threads) race and must be serialised by the caller.
- * - The device status bits are cleared at the start of every call and are not
- *   reported; host-side validation is the same as sqa_forward's.
+ * - The device status bits are cleared at the start of every call; read the
+ *   last call's bits with sqa_noalloc_read_device_status.  Host-side
+ *   validation is the same as sqa_forward's.
  * No counterpart in the reference (its launcher allocates scratch per call
  * with torch::empty, csrc/small_q_attention_ext.cu:1183-1185). */
 SQA_API int sqa_forward_noalloc(const sqa_args* args, void* stream);
+
+/* sqa_read_device_status for the scratch array of sqa_forward_noalloc on the
+ * current device: the SQA_DEV_* bits of the last call (sticky until cleared;
+ * every sqa_forward_noalloc call clears them first).  Synchronises `stream`.
+ * No counterpart in the reference. */
+SQA_API int sqa_noalloc_read_device_status(uint32_t* device_bits, int clear, void* stream);
 
 /* ---- Cache append: the step before attention in MTP decoding ----
  * Writes the K/V of the q_len new tokens of every sequence into their page

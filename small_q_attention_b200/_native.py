@@ -47,6 +47,7 @@ EXPORTED_SYMBOLS = (
     "sqa_forward",
     "sqa_forward_timed",
     "sqa_forward_noalloc",
+    "sqa_noalloc_read_device_status",
     "sqa_merge_partials",
     "sqa_read_device_status",
     "sqa_workspace_init",
@@ -142,6 +143,8 @@ def library(path: Path | None = None):
         lib.sqa_forward_timed.restype = ctypes.c_int
         lib.sqa_forward_noalloc.argtypes = [ctypes.POINTER(SqaArgs), vp]
         lib.sqa_forward_noalloc.restype = ctypes.c_int
+        lib.sqa_noalloc_read_device_status.argtypes = [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int, vp]
+        lib.sqa_noalloc_read_device_status.restype = ctypes.c_int
         lib.sqa_merge_partials.argtypes = [vp, vp, i32, i64, vp, vp, vp, vp]
         lib.sqa_merge_partials.restype = ctypes.c_int
         lib.sqa_read_device_status.argtypes = [vp, ctypes.POINTER(ctypes.c_uint32), ctypes.c_int, vp]
@@ -159,6 +162,35 @@ def library(path: Path | None = None):
         if path is None:
             _lib = lib
         return lib
+
+
+_ext = None
+
+
+def torch_ext():
+    """Load (once) and return the torch extension module ``_sqa_torch`` (the direct
+    entry of the Python operator, and the ``torch.ops.sqa_b200`` operators); it
+    links the same ``libsqa_b200.so``.  Raises if it is missing: no fallback."""
+    global _ext
+    if _ext is not None:
+        return _ext
+    with _lock:
+        if _ext is None:
+            import importlib.util
+            import sysconfig
+
+            import torch  # noqa: F401  (the extension needs torch's libraries loaded first)
+
+            path = LIB_PATH.parent / ("_sqa_torch" + (sysconfig.get_config_var("EXT_SUFFIX") or ".so"))
+            if not path.exists():
+                raise RuntimeError(f"torch extension {path} is missing; build it with "
+                                   "`python -m small_q_attention_b200.build`")
+            library()  # the C ABI it calls (same file, loaded once)
+            spec = importlib.util.spec_from_file_location("_sqa_torch", path)
+            mod = importlib.util.module_from_spec(spec)
+            spec.loader.exec_module(mod)
+            _ext = mod
+    return _ext
 
 
 def status_string(code: int) -> str:

@@ -10,12 +10,19 @@ stream (the upstream launches on the legacy default stream,
 ``csrc/small_q_attention_ext.cu:1187``), never synchronises the host, and
 reuses one workspace per (device, stream) instead of allocating fp32 scratch
 on every call (``ext.cu:1183-1185``).
+
+The operator itself runs through the torch extension (``csrc/sqa_torch_op.cpp``):
+its contract checks, argument packing, workspace lookup and launches are C++,
+so a call costs a few microseconds of host time; the same code is registered as
+``torch.ops.sqa_b200.small_q_attention`` / ``small_q_attention_partial`` for
+``torch.compile``.  The ctypes helpers below (``_check_inputs``,
+``_fill_args``) serve the C-ABI-level entry points (plan/run wrapper, merge,
+tests).
 """
 
 from __future__ import annotations
 
 import ctypes
-import threading
 
 import torch
 
@@ -28,8 +35,6 @@ MAX_Q_LEN = 16
 
 _DTYPES = (torch.float16, torch.bfloat16)
 _FP8 = getattr(torch, "float8_e4m3fn", None)
-_ws_lock = threading.Lock()
-_workspaces: dict[tuple[int, int], torch.Tensor] = {}
 
 
 _raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
@@ -173,42 +178,6 @@ def _fill_args(query, key_cache, value_cache, block_tables, seq_lens, mask_lens,
         _native.KV_FP8_E4M3 if key_cache.dtype == _FP8 else _native.KV_SAME)
 
 
-_need_cache: dict[tuple, int] = {}
-
-
-def _workspace_need(args: _native.SqaArgs, device_index: int) -> int:
-    key = (device_index, args.batch, args.q_len, args.num_kv_heads, args.num_pages, args.max_pages,
-           args.max_seq_len, args.num_ctas, args.min_pages_per_cta, args.kernel)
-    need = _need_cache.get(key)
-    if need is None:
-        st = ctypes.c_int(0)
-        need = int(_native.library().sqa_workspace_bytes(ctypes.byref(args), device_index, ctypes.byref(st)))
-        _native.check(st.value, "sqa_workspace_bytes")
-        _need_cache[key] = need
-    return need
-
-
-def workspace_for(args: _native.SqaArgs, device: torch.device, workspace: torch.Tensor | None = None):
-    """Return (pointer, bytes) of the workspace for ``args``.
-
-    A caller's ``workspace`` is used as given (``sqa_forward`` rejects one that
-    is too small).  With ``workspace=None`` one uint8 buffer per (device,
-    stream) is kept and grown on demand; its status word starts zeroed.
-    """
-    if workspace is not None:
-        if workspace.device != device or not workspace.is_contiguous():
-            raise ValueError("workspace must be a contiguous tensor on the query's device")
-        return workspace.data_ptr(), workspace.numel() * workspace.element_size()
-    need = _workspace_need(args, device.index)
-    key = (device.index, _stream_handle(device))
-    with _ws_lock:
-        ws = _workspaces.get(key)
-        if ws is None or ws.numel() < need:
-            ws = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device=device)
-            _workspaces[key] = ws
-    return ws.data_ptr(), ws.numel()
-
-
 def selected_kernel(query, key_cache, value_cache, block_tables, seq_lens, page_size,
                     max_seq_len: int = 0, *, num_ctas: int = 0, min_pages_per_cta: int = 0,
                     kernel: int = 0, kv_layout: str = "NHD") -> int:
@@ -258,19 +227,6 @@ def _raise_device_bits(bits: int) -> None:
         raise RuntimeError("a bounded device wait timed out; the output is not valid")
 
 
-def _run(args, device, workspace, check):
-    ws_ptr, ws_bytes = workspace_for(args, device, workspace)
-    stream = _stream_handle(device)
-    with _on_device(device):
-        code = _native.library().sqa_forward(ctypes.byref(args), ctypes.c_void_p(ws_ptr),
-                                            ctypes.c_size_t(ws_bytes), ctypes.c_void_p(stream))
-        if code == _native.SQA_ERR_WORKSPACE_TOO_SMALL and workspace is not None:
-            raise ValueError(f"workspace too small: need {_workspace_need(args, device.index)} bytes")
-        _native.check(code, "sqa_forward")
-        if check:
-            _raise_device_bits(read_device_status(ws_ptr, clear=True, device=device))
-
-
 def small_q_attention(query, key_cache, value_cache, block_tables, seq_lens, page_size: int,
                       max_seq_len: int = 0, *, out=None, workspace=None, num_ctas: int = 0,
                       min_pages_per_cta: int = 0, kernel: int = 0, check: bool = False,
@@ -296,16 +252,15 @@ def small_q_attention(query, key_cache, value_cache, block_tables, seq_lens, pag
     ``[pages, Hkv, 16, 128]``; ``sm_scale`` (default ``128**-0.5``) scales q.k and
     ``out_scale`` every output row (FlashInfer's ``bmm1_scale`` / ``bmm2_scale``).
     """
-    _check_inputs(query, key_cache, value_cache, block_tables, seq_lens, page_size, kv_layout=kv_layout)
-    if out is None:
-        out = torch.empty_like(query)
-    elif out.shape != query.shape or out.dtype != query.dtype or not out.is_contiguous() or out.device != query.device:
-        raise ValueError("out must be a contiguous tensor shaped and typed like query")
-    args = _fill_args(query, key_cache, value_cache, block_tables, seq_lens, None, max_seq_len,
-                      num_ctas, min_pages_per_cta, kernel, kv_layout, sm_scale, out_scale)
-    args.out = out.data_ptr()
-    _run(args, query.device, workspace, check)
-    return out
+    if not _cuda_available():
+        raise RuntimeError("CUDA is required for the small-q attention kernel")
+    try:
+        return _native.torch_ext().forward(
+            query, key_cache, value_cache, block_tables, seq_lens, page_size, max_seq_len, out, workspace,
+            num_ctas, min_pages_per_cta, kernel, check, _layout_code(kv_layout),
+            0.0 if sm_scale is None else sm_scale, out_scale)
+    except TypeError as e:  # a non-tensor where a tensor belongs (pybind11's argument check)
+        raise ValueError(f"all inputs must be CUDA tensors ({e})") from None
 
 
 def small_q_attention_partial(query, key_cache, value_cache, block_tables, seq_lens, page_size: int,
@@ -322,21 +277,15 @@ def small_q_attention_partial(query, key_cache, value_cache, block_tables, seq_l
     ``LSE`` the natural-log log-sum-exp ``[B, q_len, Hq]`` (-inf for a row
     that sees no key here).  Combine shards with :func:`merge_partials`.
     """
-    _check_inputs(query, key_cache, value_cache, block_tables, seq_lens, page_size, mask_lens, kv_layout)
-    if out is None:
-        out = torch.empty(query.shape, dtype=torch.float32, device=query.device)
-    if out_lse is None:
-        out_lse = torch.empty(query.shape[:3], dtype=torch.float32, device=query.device)
-    if out.dtype != torch.float32 or out.shape != query.shape or not out.is_contiguous():
-        raise ValueError("out must be a contiguous fp32 tensor shaped like query")
-    if out_lse.dtype != torch.float32 or out_lse.shape != query.shape[:3] or not out_lse.is_contiguous():
-        raise ValueError("out_lse must be a contiguous fp32 tensor [batch, q_len, Hq]")
-    args = _fill_args(query, key_cache, value_cache, block_tables, seq_lens, mask_lens, max_seq_len,
-                      num_ctas, min_pages_per_cta, kernel, kv_layout, sm_scale, out_scale)
-    args.out_partial = out.data_ptr()
-    args.out_lse = out_lse.data_ptr()
-    _run(args, query.device, workspace, check)
-    return out, out_lse
+    if not _cuda_available():
+        raise RuntimeError("CUDA is required for the small-q attention kernel")
+    try:
+        return _native.torch_ext().forward_partial(
+            query, key_cache, value_cache, block_tables, seq_lens, page_size, mask_lens, max_seq_len, out, out_lse,
+            workspace, num_ctas, min_pages_per_cta, kernel, check, _layout_code(kv_layout),
+            0.0 if sm_scale is None else sm_scale, out_scale)
+    except TypeError as e:
+        raise ValueError(f"all inputs must be CUDA tensors ({e})") from None
 
 
 def merge_partials(parts_o, parts_lse, *, out=None, out_dtype=torch.float16, return_lse: bool = False):

@@ -1,10 +1,15 @@
-"""Build the in-tree native library ``_lib/libsqa_b200.so`` with nvcc for sm_100a.
+"""Build the in-tree native libraries for sm_100a.
 
-The library is a plain C-ABI shared object (``include/small_q_attention.h``):
-no torch types cross it, so it builds without torch and is loaded with
-ctypes.  ``python -m small_q_attention_b200.build`` (or
-``__graft_entry__.build()``) rebuilds it when a source is newer than the
-library.
+* ``_lib/libsqa_b200.so`` (nvcc): every kernel and the plain C ABI
+  (``include/small_q_attention.h``); no torch types cross it, so it builds
+  without torch and is loaded with ctypes.
+* ``_lib/_sqa_torch<ext>`` (g++ against torch's headers): the torch extension
+  over that C ABI -- the ``torch.ops.sqa_b200`` operators and the direct entry
+  the Python operator calls.  It computes nothing itself and links
+  ``libsqa_b200.so`` from its own directory.
+
+``python -m small_q_attention_b200.build`` (or ``__graft_entry__.build()``)
+rebuilds each one when a source is newer than it.
 """
 
 from __future__ import annotations
@@ -13,6 +18,7 @@ import os
 import shutil
 import subprocess
 import sys
+import sysconfig
 from pathlib import Path
 
 PKG = Path(__file__).resolve().parent
@@ -49,6 +55,47 @@ def is_stale() -> bool:
     return any(p.stat().st_mtime > built for p in _inputs())
 
 
+TORCH_EXT_SOURCE = CSRC / "sqa_torch_op.cpp"
+TORCH_EXT_PATH = LIB_DIR / ("_sqa_torch" + (sysconfig.get_config_var("EXT_SUFFIX") or ".so"))
+
+
+def torch_ext_is_stale() -> bool:
+    if not TORCH_EXT_PATH.exists():
+        return True
+    built = TORCH_EXT_PATH.stat().st_mtime
+    deps = [TORCH_EXT_SOURCE, ROOT / "include" / "small_q_attention.h", Path(__file__)]
+    return any(p.stat().st_mtime > built for p in deps)
+
+
+def build_torch_ext(force: bool = False, verbose: bool = False) -> Path:
+    """Compile the torch extension (host code only) if missing or stale; return its path."""
+    if not force and not torch_ext_is_stale():
+        return TORCH_EXT_PATH
+    import torch
+    from torch.utils import cpp_extension as ce
+
+    cuda_home = ce.CUDA_HOME or "/usr/local/cuda"
+    torch_lib = Path(torch.__file__).resolve().parent / "lib"
+    includes = [Path(torch.__file__).resolve().parent / "include",
+                Path(torch.__file__).resolve().parent / "include" / "torch" / "csrc" / "api" / "include",
+                Path(cuda_home) / "include", Path(sysconfig.get_paths()["include"])]
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    tmp = TORCH_EXT_PATH.with_name(TORCH_EXT_PATH.name + ".tmp")
+    cmd = [os.environ.get("CXX", "g++"), "-std=c++17", "-O2", "-shared", "-fPIC", "-fvisibility=hidden",
+           f"-D_GLIBCXX_USE_CXX11_ABI={abi}", "-DTORCH_API_INCLUDE_EXTENSION_H", "-DTORCH_EXTENSION_NAME=_sqa_torch",
+           *[f"-I{p}" for p in includes], "-I", str(ROOT / "include"), str(TORCH_EXT_SOURCE), "-o", str(tmp),
+           f"-L{torch_lib}", "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_cuda", "-ltorch_python",
+           f"-L{Path(cuda_home) / 'lib64'}", "-lcudart", f"-L{LIB_DIR}", "-lsqa_b200",
+           "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{torch_lib}"]
+    if verbose:
+        print(" ".join(cmd), file=sys.stderr)
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"g++ failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
+    os.replace(tmp, TORCH_EXT_PATH)
+    return TORCH_EXT_PATH
+
+
 def build(force: bool = False, verbose: bool = False, extra_flags=None) -> Path:
     """Compile the native library if missing or stale; return its path."""
     if not force and not is_stale():
@@ -66,5 +113,11 @@ def build(force: bool = False, verbose: bool = False, extra_flags=None) -> Path:
     return LIB_PATH
 
 
+def build_all(force: bool = False, verbose: bool = False) -> list[Path]:
+    """Both libraries: the kernels' C ABI first, then the torch extension that links it."""
+    return [build(force=force, verbose=verbose), build_torch_ext(force=force, verbose=verbose)]
+
+
 if __name__ == "__main__":
-    print(build(force="--force" in sys.argv, verbose=True))
+    for path in build_all(force="--force" in sys.argv, verbose=True):
+        print(path)

@@ -14,7 +14,7 @@
 namespace sqa {
 namespace {
 
-constexpr int kAbiVersion = 107;
+constexpr int kAbiVersion = 108;
 constexpr size_t kAlign = 256;
 constexpr int kMaxDevices = 64;
 constexpr int kCtasPerSm = 2;
@@ -186,8 +186,12 @@ int validate(const sqa_args* a) {
   if (a->dtype != SQA_DTYPE_F16 && a->dtype != SQA_DTYPE_BF16) return SQA_ERR_UNSUPPORTED;
   if (a->kv_layout != SQA_KV_NHD && a->kv_layout != SQA_KV_HND) return SQA_ERR_UNSUPPORTED;
   if (a->kv_dtype != SQA_KV_SAME && a->kv_dtype != SQA_KV_FP8_E4M3) return SQA_ERR_UNSUPPORTED;
-  // the device schedule counts pages x KV heads in 32 bits
-  if ((long long)a->batch * a->max_pages * a->num_kv_heads > (1LL << 30)) return SQA_ERR_UNSUPPORTED;
+  // The device schedule counts cost in 32 bits: every page x KV head plus the
+  // charge of every segment start (at most the larger kernel's), so that the
+  // total, a CTA's range ends and their sums stay below 2^31.
+  const int max_seg_cost = kSegmentCostTc > kSegmentCostMma ? kSegmentCostTc : kSegmentCostMma;
+  if ((long long)a->batch * a->num_kv_heads * ((long long)a->max_pages + max_seg_cost) > (1LL << 30))
+    return SQA_ERR_UNSUPPORTED;
   // fp8 caches run on the tcgen05 kernel (fp16 or bf16 queries)
   if (a->kv_dtype == SQA_KV_FP8_E4M3 && a->kernel == 1) return SQA_ERR_UNSUPPORTED;
   // a page must hold 16 x Hkv x 128 elements and start 16-byte aligned (TMA strides)
@@ -391,13 +395,21 @@ int forward_impl(const sqa_args* a, void* workspace, size_t workspace_bytes, voi
   p.seg_cost = pl.tc ? kSegmentCostTc : kSegmentCostMma;
 
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_ptr);
-  if (ev_before && cudaEventRecord(reinterpret_cast<cudaEvent_t>(ev_before), stream) != cudaSuccess)
+  // Timing events: under stream capture they become event-record nodes of the
+  // graph (cudaEventRecordExternal), so the kernel is timed inside a replay.
+  unsigned int ev_flags = cudaEventRecordDefault;
+  if (ev_before || ev_after) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess) return SQA_ERR_CUDA;
+    if (cs == cudaStreamCaptureStatusActive) ev_flags = cudaEventRecordExternal;
+  }
+  if (ev_before && cudaEventRecordWithFlags(reinterpret_cast<cudaEvent_t>(ev_before), stream, ev_flags) != cudaSuccess)
     return SQA_ERR_CUDA;
   const cudaError_t launched = pl.tc ? launch_split_kv_tc(p, tm_k, tm_v, pl.grid, pl.smem, stream)
                                     : launch_split_kv(p, tm_k, tm_v, pl.grid, pl.smem, stream);
   if (launched != cudaSuccess) return SQA_ERR_CUDA;
   if (!debug_sync(stream, "split-KV kernel", pl.grid, pl.smem, a)) return SQA_ERR_CUDA;
-  if (ev_after && cudaEventRecord(reinterpret_cast<cudaEvent_t>(ev_after), stream) != cudaSuccess)
+  if (ev_after && cudaEventRecordWithFlags(reinterpret_cast<cudaEvent_t>(ev_after), stream, ev_flags) != cudaSuccess)
     return SQA_ERR_CUDA;
 
   MergeParams m;

@@ -105,7 +105,7 @@ __device__ __forceinline__ Schedule compute_schedule(const SplitKvParams& p) {
   }
 
   // cost of sequence b: Hkv segments of (pages + seg_cost) when it has pages (32-bit:
-  // the host bounds batch x max_pages x Hkv)
+  // the host bounds batch x Hkv x (max_pages + seg_cost) by 2^30)
   const int total_units = total_pages * p.hkv;
   const int seg_cost = (int)segment_cost(p.seg_cost, total_units, gridDim.x);
   int nonempty = 0;

@@ -42,7 +42,7 @@ def test_every_declared_symbol_is_exported(lib):
 
 
 def test_abi_version_and_status_strings(lib):
-    assert lib.sqa_abi_version() == 107
+    assert lib.sqa_abi_version() == 108
     for code in range(6):
         assert lib.sqa_status_string(code).decode()
     assert lib.sqa_status_string(99).decode() == "unknown status"
@@ -144,3 +144,28 @@ def test_struct_layouts_match_the_header(tmp_path):
         assert got[(cname, "size")] == ctypes.sizeof(cls)
         for name, _ in cls._fields_:
             assert got[(cname, name)] == getattr(cls, name).offset, (cname, name)
+
+
+def test_torch_extension_registers_the_operators():
+    """The torch extension loads without a GPU, registers torch.ops.sqa_b200.*, and
+    its Meta kernels give the output shapes (what torch.compile traces with); a
+    CPU tensor is rejected with the upstream's ValueError before any launch."""
+    import torch
+
+    from small_q_attention_b200 import _native, build
+
+    build.build_torch_ext()  # no-op when up to date
+    ext = _native.torch_ext()
+    assert ext.abi_version() == 108
+    q = torch.empty(2, 4, 32, 128, dtype=torch.float16, device="meta")
+    k = torch.empty(64, 16, 8, 128, dtype=torch.float16, device="meta")
+    bt = torch.empty(2, 32, dtype=torch.int32, device="meta")
+    sl = torch.empty(2, dtype=torch.int32, device="meta")
+    out = torch.ops.sqa_b200.small_q_attention(q, k, k, bt, sl, 16)
+    assert out.shape == q.shape and out.dtype == torch.float16
+    o, lse = torch.ops.sqa_b200.small_q_attention_partial(q, k, k, bt, sl, 16, mask_lens=sl)
+    assert o.shape == q.shape and o.dtype == torch.float32 and lse.shape == (2, 4, 32)
+    cpu = [torch.zeros(2, 4, 32, 128, dtype=torch.float16), torch.zeros(64, 16, 8, 128, dtype=torch.float16)]
+    with pytest.raises(ValueError, match="CUDA tensors"):
+        ext.forward(cpu[0], cpu[1], cpu[1], torch.zeros(2, 32, dtype=torch.int32),
+                    torch.zeros(2, dtype=torch.int32), 16, 0, None, None, 0, 0, 0, False, 0, 0.0, 1.0)
