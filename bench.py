@@ -717,7 +717,74 @@ def run_reference(args):
                                    f"reference.py:10-74 ({_cpu_model()}, torch {torch.__version__})"},
         "e2e": {"value": v, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    ref_gpu = None
+    if not args.no_ref_gpu:
+        ref_gpu = time_reference_gpu(args, [WORKLOAD])
+    if ref_gpu:
+        line["reference_gpu_kernel"] = ref_gpu[0]
     print(json.dumps(line), flush=True)
+    if args.ref_gpu_matrix:
+        rows = time_reference_gpu(args, [n for n, _ in _matrix_cases(args.only)])
+        Path(args.ref_gpu_matrix).parent.mkdir(parents=True, exist_ok=True)
+        Path(args.ref_gpu_matrix).write_text("".join(json.dumps(r) + "\n" for r in rows))
+
+
+def time_reference_gpu(args, labels):
+    """The upstream's own GPU path on this box: ``forward_v3`` of its CUDA extension
+    (``csrc/small_q_attention_ext.cu:1132-1210``, built unmodified for sm_100a by
+    ``oracle/build_ref_gpu.py``), chunk_keys 512 and max_seq_len given, as its
+    matrix runs it (``scripts/run_gpu_matrix.py:116``), timed with its own protocol
+    (``scripts/run_gpu_matrix.py:63-81``: 5 warm-up calls, 15 calls on the same
+    inputs, a CUDA event pair and a synchronise around each, median).  A same-box
+    comparator reported beside the CPU reference; None when the extension is not
+    built or there is no GPU.  q_len 16 is outside its contract (``cuda.py:206-207``)."""
+    try:
+        import torch
+
+        from oracle import build_ref_gpu
+
+        if not torch.cuda.is_available() or build_ref_gpu.built_module_path() is None:
+            return None
+        mod = build_ref_gpu.load_module()
+    except Exception as e:  # the comparator is optional: report why it is missing
+        print(f"bench: upstream GPU extension unavailable ({e})", file=sys.stderr)
+        return None
+    from small_q_attention_b200.workloads import CONFIGS, make_case, make_config
+
+    torch.cuda.set_device(0)
+    rows = []
+    for label in labels:
+        if label in CONFIGS:
+            c = make_config(label, seed=0)
+        else:
+            q, kv, b = (int(x) for x in label.replace("q", "").replace("kv", "").replace("b", "").split("_"))
+            c = make_case(b, q, [kv] * b, pool_factor=1.0, seed=0)
+        q_len = c["query"].shape[1]
+        if q_len not in (2, 4, 8):
+            rows.append({"case": label, "unsupported": "q_len outside the upstream contract (2, 4, 8)"})
+            continue
+        args_ = (c["query"], c["key_cache"], c["value_cache"], c["block_tables"], c["seq_lens"], 16, 512,
+                 max(c["lens"]))
+        for _ in range(5):
+            mod.forward_v3(*args_)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        samples = []
+        for _ in range(15):
+            e0.record()
+            mod.forward_v3(*args_)
+            e1.record()
+            e1.synchronize()
+            samples.append(e0.elapsed_time(e1) * 1e3)
+        us = statistics.median(samples)
+        nb = _case_bytes(c)
+        rows.append({"case": label, "impl": "upstream forward_v3 (ext.cu:1132-1210), sm_100a build, chunk_keys 512",
+                     "p50_us": round(us, 3), "tb_s": round(nb / (us * 1e-6) / 1e12, 4), "alg_bytes": nb,
+                     "protocol": "scripts/run_gpu_matrix.py:63-81 (same inputs, event pair + sync per call, "
+                                 "median of 15)"})
+        del c
+        torch.cuda.empty_cache()
+    return rows
 
 
 def _matrix_cases(only=None):
@@ -868,6 +935,10 @@ def main():
     ap.add_argument("--no-sharded", action="store_true", help="leave the cfg3/cfg4/cfg5 sub-results out")
     ap.add_argument("--settle-line", type=float, default=0.2,
                     help="matrix inside the driver line: seconds of idle before each case")
+    ap.add_argument("--no-ref-gpu", action="store_true",
+                    help="--impl reference: leave out the upstream GPU kernel beside the CPU reference")
+    ap.add_argument("--ref-gpu-matrix", type=str, default=None,
+                    help="--impl reference: also time the upstream GPU kernel on every matrix case, JSONL here")
     ap.add_argument("--matrix-replica-mb", type=float, default=400.0,
                     help="matrix: MB of distinct K/V replicas rotated per case (>= 126 MB L2)")
     args = ap.parse_args()

@@ -55,6 +55,27 @@ def is_stale() -> bool:
     return any(p.stat().st_mtime > built for p in _inputs())
 
 
+def shared_runtime_cxx() -> str:
+    """A C++ compiler that links the shared libstdc++ (the one torch uses).
+
+    A compiler that only finds libstdc++.a would put a private copy of the C++
+    runtime into the extension; C++ exceptions thrown there and rethrown by
+    torch's error translation then cross two runtimes, which is undefined
+    behaviour (it crashed in the unwinder on a CUDA host).  $CXX is taken when
+    it qualifies, else the first g++ / c++ on PATH that does."""
+    seen = []
+    for cand in (os.environ.get("CXX"), "g++", "c++", "/usr/bin/g++"):
+        exe = shutil.which(cand) if cand else None
+        if not exe or exe in seen:
+            continue
+        seen.append(exe)
+        res = subprocess.run([exe, "-print-file-name=libstdc++.so"], capture_output=True, text=True)
+        found = res.stdout.strip()
+        if res.returncode == 0 and os.path.isabs(found) and Path(found).exists():
+            return exe
+    raise RuntimeError(f"no C++ compiler on this host links the shared libstdc++ (tried {seen})")
+
+
 TORCH_EXT_SOURCE = CSRC / "sqa_torch_op.cpp"
 TORCH_EXT_PATH = LIB_DIR / ("_sqa_torch" + (sysconfig.get_config_var("EXT_SUFFIX") or ".so"))
 
@@ -81,7 +102,7 @@ def build_torch_ext(force: bool = False, verbose: bool = False) -> Path:
                 Path(cuda_home) / "include", Path(sysconfig.get_paths()["include"])]
     abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
     tmp = TORCH_EXT_PATH.with_name(TORCH_EXT_PATH.name + ".tmp")
-    cmd = [os.environ.get("CXX", "g++"), "-std=c++17", "-O2", "-shared", "-fPIC", "-fvisibility=hidden",
+    cmd = [shared_runtime_cxx(), "-std=c++17", "-O2", "-g", "-shared", "-fPIC", "-fvisibility=hidden",
            f"-D_GLIBCXX_USE_CXX11_ABI={abi}", "-DTORCH_API_INCLUDE_EXTENSION_H", "-DTORCH_EXTENSION_NAME=_sqa_torch",
            *[f"-I{p}" for p in includes], "-I", str(ROOT / "include"), str(TORCH_EXT_SOURCE), "-o", str(tmp),
            f"-L{torch_lib}", "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_cuda", "-ltorch_python",

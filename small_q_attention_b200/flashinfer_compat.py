@@ -1,4 +1,4 @@
-"""FlashInfer-compatible entry point for speculative-decoding (MTP) attention.
+"""FlashInfer-compatible entry points for speculative-decoding (MTP) attention.
 
 ``trtllm_batch_decode_with_kv_cache`` mirrors the signature of FlashInfer's
 ``flashinfer.decode.trtllm_batch_decode_with_kv_cache`` (FlashInfer 0.6) —
@@ -21,6 +21,19 @@ dequantisation scales folded into ``bmm1_scale`` / ``bmm2_scale``, as FlashInfer
 does), float scales, ``window_left=-1``, no sinks, no custom mask, no variable
 query lengths, no nvfp4 scale-factor tensors, one shared page table for K and V.  ``backend`` and ``enable_pdl`` are
 accepted and ignored (the kernels always use programmatic dependent launch).
+
+``BatchDecodeWithPagedKVCacheWrapper`` mirrors FlashInfer's decode wrapper
+(``flashinfer.decode.BatchDecodeWithPagedKVCacheWrapper``, 0.6 / 0.7) as the
+upstream drives it for MTP (``scripts/compare_flashinfer_paths.py:104-121``,
+``docs/pr3859_comment_draft.md:19-23``): ``plan(indptr, indices, last_page_len,
+..., q_len_per_req=q)`` once per batch, then ``run(q, paged_kv_cache)`` per
+step.  The CSR page layout (``indptr`` [batch + 1], ``indices`` the pages of
+every request back to back, ``last_page_len`` [batch] in 1..page_size) is
+turned into this path's padded page table and lengths once, in ``plan``; the
+draft rows follow the same causal rule (row ``qi`` of a request sees the
+tokens before ``kv_len - q_len + qi + 1``).  Same supported subset as above;
+``pos_encoding_mode`` must be "NONE", no logits soft cap, no rope scaling, no
+``return_lse``.
 """
 
 from __future__ import annotations
@@ -29,11 +42,11 @@ import torch
 
 from .attention import small_q_attention
 
-__all__ = ["trtllm_batch_decode_with_kv_cache"]
+__all__ = ["trtllm_batch_decode_with_kv_cache", "BatchDecodeWithPagedKVCacheWrapper", "csr_to_block_table"]
 
 
 def _unsupported(what: str):
-    raise ValueError(f"trtllm_batch_decode_with_kv_cache: {what} is not supported by small_q_attention_b200")
+    raise ValueError(f"{what} is not supported by small_q_attention_b200's FlashInfer-compatible entry points")
 
 
 def trtllm_batch_decode_with_kv_cache(
@@ -116,3 +129,125 @@ def trtllm_batch_decode_with_kv_cache(
     res = small_q_attention(q4, k_cache, v_cache, block_tables, seq_lens, 16, max_seq_len, out=out4, workspace=ws,
                             kv_layout=kv_layout, sm_scale=float(bmm1_scale), out_scale=float(bmm2_scale))
     return res.view(query.shape)
+
+
+def csr_to_block_table(indptr, indices, last_page_len, page_size: int = 16):
+    """FlashInfer's CSR page layout -> ``(block_tables [batch, max_pages] int32,
+    seq_lens [batch] int32)`` on the indices' device.  A request with ``n > 0``
+    pages holds ``(n - 1) * page_size + last_page_len`` tokens; one with none, 0.
+    Table entries past a request's pages are 0 (never read: the kernels stop at
+    the length)."""
+    indptr = indptr.to(device=indices.device, dtype=torch.int64)
+    last = last_page_len.to(device=indices.device, dtype=torch.int64)
+    counts = indptr[1:] - indptr[:-1]
+    if (counts < 0).any():
+        raise ValueError("indptr must be non-decreasing")
+    batch = counts.numel()
+    max_pages = max(int(counts.max()) if batch else 0, 1)
+    j = torch.arange(max_pages, device=indices.device, dtype=torch.int64)
+    valid = j[None, :] < counts[:, None]
+    idx = (indptr[:-1, None] + j[None, :]).clamp(max=max(indices.numel() - 1, 0))
+    table = torch.where(valid, indices.to(torch.int64)[idx] if indices.numel() else torch.zeros_like(idx),
+                        torch.zeros_like(idx))
+    lens = torch.where(counts > 0, (counts - 1) * page_size + last, torch.zeros_like(counts))
+    if ((counts > 0) & ((last < 1) | (last > page_size))).any():
+        raise ValueError("last_page_len must be in [1, page_size] for a request with pages")
+    return table.to(torch.int32).contiguous(), lens.to(torch.int32).contiguous()
+
+
+class BatchDecodeWithPagedKVCacheWrapper:
+    """FlashInfer's paged decode wrapper, for MTP decode on this library's kernels.
+
+    >>> w = BatchDecodeWithPagedKVCacheWrapper(workspace, "NHD", use_tensor_cores=True)
+    >>> w.plan(indptr, indices, last_page_len, 32, 8, 128, 16, q_data_type=torch.float16,
+    ...        q_len_per_req=4)
+    >>> out = w.run(q, kv_cache)        # q [batch * 4, 32, 128]; kv_cache [pages, 2, 16, 8, 128]
+    """
+
+    def __init__(self, float_workspace_buffer, kv_layout: str = "NHD", use_cuda_graph: bool = False,
+                 use_tensor_cores: bool = False, paged_kv_indptr_buffer=None, paged_kv_indices_buffer=None,
+                 paged_kv_last_page_len_buffer=None, backend: str = "auto", jit_args=None):
+        if kv_layout not in ("NHD", "HND"):
+            raise ValueError(f"unknown kv_layout {kv_layout!r}")
+        if jit_args is not None:
+            _unsupported("jit_args")
+        ws = float_workspace_buffer
+        self._workspace = ws.view(torch.uint8) if ws is not None and ws.is_contiguous() else None
+        self._kv_layout = kv_layout
+        self._plan = None
+
+    def plan(self, indptr, indices, last_page_len, num_qo_heads: int, num_kv_heads: int, head_dim: int,
+             page_size: int, pos_encoding_mode: str = "NONE", window_left: int = -1, logits_soft_cap=None,
+             q_data_type="float16", kv_data_type=None, data_type=None, sm_scale=None, rope_scale=None,
+             rope_theta=None, non_blocking: bool = True, block_tables=None, seq_lens=None,
+             fixed_split_size=None, disable_split_kv: bool = False, q_len_per_req: int = 1, **unused):
+        """Fix the batch: page layout, heads, types, scale and draft tokens per request."""
+        if pos_encoding_mode != "NONE":
+            _unsupported(f"pos_encoding_mode={pos_encoding_mode!r}")
+        if window_left != -1:
+            _unsupported("a sliding window")
+        if logits_soft_cap not in (None, 0, 0.0):
+            _unsupported("a logits soft cap")
+        if rope_scale is not None or rope_theta is not None:
+            _unsupported("rope")
+        if head_dim != 128 or page_size != 16 or num_qo_heads != 4 * num_kv_heads:
+            _unsupported(f"head_dim {head_dim}, page_size {page_size}, heads {num_qo_heads}/{num_kv_heads}")
+        q_len = int(q_len_per_req or 1)
+        if not 1 <= q_len <= 16:
+            _unsupported(f"q_len_per_req={q_len}")
+        q_dt = getattr(torch, q_data_type) if isinstance(q_data_type, str) else q_data_type
+        if data_type is not None:  # older name of the query/KV type
+            q_dt = getattr(torch, data_type) if isinstance(data_type, str) else data_type
+        kv_dt = kv_data_type if kv_data_type is not None else q_dt
+        kv_dt = getattr(torch, kv_dt) if isinstance(kv_dt, str) else kv_dt
+        if q_dt not in (torch.float16, torch.bfloat16):
+            _unsupported(f"query type {q_dt}")
+        if kv_dt not in (q_dt, getattr(torch, "float8_e4m3fn", None)):
+            _unsupported(f"KV type {kv_dt}")
+        if block_tables is not None and seq_lens is not None:
+            table, lens = block_tables.to(torch.int32).contiguous(), seq_lens.to(torch.int32).contiguous()
+        else:
+            table, lens = csr_to_block_table(indptr, indices, last_page_len, page_size)
+        self._plan = dict(table=table, lens=lens, q_len=q_len, hq=num_qo_heads, hkv=num_kv_heads,
+                          q_dtype=q_dt, kv_dtype=kv_dt, max_seq_len=int(lens.max()) if lens.numel() else 0,
+                          sm_scale=float(sm_scale) if sm_scale is not None else 128 ** -0.5)
+
+    begin_forward = plan
+
+    def run(self, q, paged_kv_cache, *args, q_scale=None, k_scale=None, v_scale=None, out=None, lse=None,
+            return_lse: bool = False, window_left=None, enable_pdl=None):
+        """Attention of ``q`` ``[batch * q_len_per_req, num_qo_heads, 128]`` over the planned pages;
+        ``paged_kv_cache`` is ``(k_cache, v_cache)`` or one ``[pages, 2, ...]`` tensor."""
+        p = self._plan
+        if p is None:
+            raise RuntimeError("plan() has not been called")
+        if return_lse or lse is not None:
+            _unsupported("return_lse")
+        if window_left not in (None, -1):
+            _unsupported("a sliding window")
+        if q.dim() != 3 or q.shape[0] != p["table"].shape[0] * p["q_len"] or q.shape[1] != p["hq"]:
+            raise ValueError("q must be [batch * q_len_per_req, num_qo_heads, head_dim] as planned")
+        if q.dtype != p["q_dtype"]:
+            raise ValueError(f"q is {q.dtype}, planned {p['q_dtype']}")
+        if isinstance(paged_kv_cache, (tuple, list)):
+            k_cache, v_cache = paged_kv_cache
+        else:
+            if paged_kv_cache.dim() != 5 or paged_kv_cache.shape[1] != 2:
+                _unsupported("a paged_kv_cache tensor that is not [pages, 2, ...]")
+            k_cache, v_cache = paged_kv_cache[:, 0], paged_kv_cache[:, 1]
+        scale = p["sm_scale"] * (float(q_scale) if q_scale is not None else 1.0) * (
+            float(k_scale) if k_scale is not None else 1.0)
+        out_scale = float(v_scale) if v_scale is not None else 1.0
+        batch = p["table"].shape[0]
+        q4 = q.view(batch, p["q_len"], q.shape[1], q.shape[2])
+        out4 = None
+        if out is not None:
+            if out.shape != q.shape or out.dtype != q.dtype:
+                raise ValueError("out must be shaped and typed like q")
+            out4 = out.view(q4.shape)
+        res = small_q_attention(q4, k_cache, v_cache, p["table"], p["lens"], 16, p["max_seq_len"], out=out4,
+                                workspace=self._workspace, kv_layout=self._kv_layout, sm_scale=scale,
+                                out_scale=out_scale)
+        return res.view(q.shape)
+
+    forward = run

@@ -119,3 +119,32 @@ def test_flashinfer_compatible_entry_rejects_what_it_does_not_do(sqa):
                {"bmm1_scale": torch.tensor(0.1)}, {"uses_shared_paged_kv_idx": False}, {"q_len_per_req": 3}):
         with pytest.raises(ValueError):
             trtllm_batch_decode_with_kv_cache(*args, q_len_per_req=kw.pop("q_len_per_req", 2), **kw)
+
+
+@pytest.mark.parametrize("q_len,kv_form", [(2, "pool"), (4, "tuple"), (8, "pool"), (16, "tuple")])
+def test_flashinfer_decode_wrapper_with_q_len_per_req(sqa, q_len, kv_form):
+    """FlashInfer's decode wrapper as the upstream drives it for MTP
+    (scripts/compare_flashinfer_paths.py:104-121): CSR pages, plan(..., q_len_per_req),
+    run(q, kv) with the NHD [pages, 2, 16, Hkv, 128] pool or a (k, v) tuple."""
+    from small_q_attention_b200.flashinfer_compat import BatchDecodeWithPagedKVCacheWrapper
+
+    lens = [q_len, 700, 4096, 33]
+    c = case(q_len, lens, seed=60 + q_len)
+    pages = [(n + 15) // 16 for n in lens]
+    indices = torch.cat([c["block_tables"][b, :p] for b, p in enumerate(pages)])
+    indptr = torch.tensor([0] + list(np.cumsum(pages)), dtype=torch.int32, device="cuda")
+    last = torch.tensor([n - (p - 1) * 16 for n, p in zip(lens, pages)], dtype=torch.int32, device="cuda")
+    kv = (c["key_cache"], c["value_cache"]) if kv_form == "tuple" else interleaved(c["key_cache"], c["value_cache"])
+    w = BatchDecodeWithPagedKVCacheWrapper(torch.zeros(64 << 20, dtype=torch.int8, device="cuda"), "NHD",
+                                           use_tensor_cores=True)
+    w.plan(indptr=indptr, indices=indices, last_page_len=last, num_qo_heads=32, num_kv_heads=8, head_dim=128,
+           page_size=16, pos_encoding_mode="NONE", q_data_type=torch.float16, kv_data_type=torch.float16,
+           q_len_per_req=q_len)
+    b = len(lens)
+    out = w.run(c["query"].reshape(b * q_len, 32, 128), kv)
+    assert out.shape == (b * q_len, 32, 128)
+    assert_close(out.view(c["query"].shape), oracle(c))
+    with pytest.raises(ValueError):
+        w.run(c["query"].reshape(b * q_len, 32, 128), kv, return_lse=True)
+    with pytest.raises(ValueError):
+        w.plan(indptr, indices, last, 32, 8, 128, 16, pos_encoding_mode="ROPE_LLAMA", q_len_per_req=q_len)

@@ -228,6 +228,26 @@ def test_forward_v3_compat(sqa):
         forward_v3(*args, 0)
 
 
+@pytest.mark.parametrize("q_len", [2, 4, 8])
+def test_forward_v0_v1_v2_aliases(sqa, q_len):
+    """The upstream entry points of the earlier kernel revisions
+    (src/small_q_attention/cuda.py:61-153) compute the same operator here."""
+    from small_q_attention_b200.cuda import forward_v0, forward_v1, forward_v2, load_v0, load_v2
+
+    c = case(q_len, [q_len, 300, 2048], seed=70 + q_len)
+    ref = oracle(c)
+    args = (c["query"], c["key_cache"], c["value_cache"], c["block_tables"], c["seq_lens"], 16)
+    assert load_v0() is load_v2()  # one library behind every revision
+    assert_close(forward_v0(*args), ref)
+    assert_close(forward_v1(*args), ref)
+    assert_close(forward_v2(*args, 128), ref)
+    assert_close(forward_v2(*args, chunk_keys=4096), ref)
+    with pytest.raises(ValueError):
+        forward_v2(*args, chunk_keys=0)
+    with pytest.raises(ValueError):
+        forward_v0(c["query"].bfloat16(), *args[1:])
+
+
 def test_device_status_errors(sqa):
     c = case(4, [40, 20], hkv=2, seed=17)
     bad = c["block_tables"].clone()

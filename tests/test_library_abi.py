@@ -169,3 +169,21 @@ def test_torch_extension_registers_the_operators():
     with pytest.raises(ValueError, match="CUDA tensors"):
         ext.forward(cpu[0], cpu[1], cpu[1], torch.zeros(2, 32, dtype=torch.int32),
                     torch.zeros(2, dtype=torch.int32), 16, 0, None, None, 0, 0, 0, False, 0, 0.0, 1.0)
+
+
+def test_torch_extension_shares_the_process_cpp_runtime():
+    """The extension must link the shared libstdc++ that torch uses, not carry a
+    private static copy: its C++ exceptions are caught and rethrown by torch's
+    error translation, which is undefined behaviour across two runtimes."""
+    import shutil
+    import subprocess
+
+    from small_q_attention_b200 import build
+
+    if not (shutil.which("readelf") and shutil.which("nm")):
+        pytest.skip("binutils not available")
+    path = build.build_torch_ext()
+    needed = subprocess.run(["readelf", "-d", str(path)], capture_output=True, text=True).stdout
+    assert "libstdc++.so.6" in needed
+    exported = subprocess.run(["nm", "-D", "--defined-only", str(path)], capture_output=True, text=True).stdout
+    assert "__cxa_allocate_exception" not in exported and "__cxa_throw" not in exported
