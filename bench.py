@@ -235,7 +235,8 @@ WORKLOADS = {
     "cfg2": "cfg2 batch-sharded, weak: B=4 per GPU, q_len=4, kv_len=8192, random pages, pool 1.5x",
     "cfg3": "cfg3 KV-head-sharded, strong: B=16, q_len=8, kv_len=32768, 8/N KV heads per GPU",
     "cfg4": "cfg4 batch-sharded (LPT by tokens), strong: B=64, q_len=4, kv_len U[512,32768], K x4 on 1%",
-    "cfg5": "cfg5 long-context, strong: B=1, q_len=16, kv_len=262144 split over N GPUs, (O, LSE) all-gather + merge",
+    "cfg5": "cfg5 long-context, strong: B=1, q_len=16, kv_len=262144 split over N GPUs, (O, LSE) to rank 0 by "
+            "NVLink peer stores + merge",
 }
 
 
@@ -318,19 +319,30 @@ class DeviceArm:
         self.ws_bytes = ws_bytes
         self.ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=device)
         self.merged = torch.empty(self.reps[0]["query"].shape, dtype=torch.float16, device=device)
+        # long-context exchange across ranks: peer stores into rank 0 + its merge (NVLink)
+        self.lc = None
+        if self.longctx and dist is not None:
+            from small_q_attention_b200.sharding import LongContextGroup
+
+            q0 = self.reps[0]["query"]
+            self.lc = LongContextGroup(rows=q0.shape[0] * q0.shape[1] * q0.shape[2], device=device)
         self.kernel_id = lib.sqa_selected_kernel(ctypes.byref(self.cargs[0]), device.index)
         if self.kernel_id < 0:
             _native.check(-self.kernel_id, "sqa_selected_kernel")
-        # our kernels per step: split-KV + per-call merge (+ the cross-rank merge in long-context mode)
-        self.launches_per_step = 3 if self.longctx else 2
+        # our kernels per step on rank 0: split-KV + per-call merge, in long-context mode also the
+        # cross-rank merge (one GPU) or the send + merge of the NVLink exchange (several)
+        self.launches_per_step = (4 if self.lc is not None else 3) if self.longctx else 2
+
+    def close(self):
+        if self.lc is not None:
+            self.lc.close()
+            self.lc = None
 
     def call(self, i, stream, ev0=None, ev1=None):
         import ctypes
 
         import small_q_attention_b200 as sqa
         from small_q_attention_b200 import _native
-        from small_q_attention_b200.sharding import gather_partials
-
         lib, a = self.lib, self.cargs[i % REPLICAS]
         if ev0 is None:
             code = lib.sqa_forward(ctypes.byref(a), ctypes.c_void_p(self.ws.data_ptr()),
@@ -340,13 +352,12 @@ class DeviceArm:
                                          ctypes.c_size_t(self.ws_bytes), ctypes.c_void_p(stream),
                                          ctypes.c_void_p(ev0), ctypes.c_void_p(ev1))
         _native.check(code, "sqa_forward")
-        if self.longctx:  # the exchange step: gather every rank's (O, LSE), merge
+        if self.longctx:  # the exchange step: every rank's (O, LSE) merged on rank 0
             j = i % REPLICAS
-            if self.dist is not None:
-                parts_o, parts_lse = gather_partials(self.outs[j], self.lses[j])
+            if self.lc is not None:
+                self.lc.exchange(self.outs[j], self.lses[j], out=self.merged)
             else:
-                parts_o, parts_lse = self.outs[j][None], self.lses[j][None]
-            sqa.merge_partials(parts_o, parts_lse, out=self.merged)
+                sqa.merge_partials(self.outs[j][None], self.lses[j][None], out=self.merged)
 
 
 def measure_device(arm, args, device, with_clocks=True):
@@ -367,13 +378,15 @@ def measure_device(arm, args, device, with_clocks=True):
         for i in range(K):
             arm.call(i, torch.cuda.current_stream().cuda_stream)
     torch.cuda.synchronize()
-    # warm replays (untimed) so that the timed replay starts at the clock of a busy GPU
+    # warm replays (untimed) so that the timed replay starts at the clock of a busy GPU; the
+    # count is the same on every rank (a replay holds cross-rank exchanges)
     t_warm = time.perf_counter()
-    while True:
+    graph.replay()
+    torch.cuda.synchronize()
+    n_warm = int(_max_over_ranks(float(math.ceil(0.05 / max(time.perf_counter() - t_warm, 1e-4))), dist, device))
+    for _ in range(min(n_warm, 200)):
         graph.replay()
-        torch.cuda.synchronize()
-        if time.perf_counter() - t_warm > 0.05:
-            break
+    torch.cuda.synchronize()
 
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clocks = ClockSampler(device.index) if with_clocks else None
@@ -479,9 +492,10 @@ def measure_e2e(arm, args, device):
     def attend(j):
         d = dev_in[j][1]
         if longctx:
-            return long_context_attention(d["query"], reps[j]["key_cache"], reps[j]["value_cache"],
-                                          d["block_tables"], d["seq_lens"], d["mask_lens"], 16, out=e2e_out[j],
-                                          workspace=arm.ws)
+            o = long_context_attention(d["query"], reps[j]["key_cache"], reps[j]["value_cache"],
+                                       d["block_tables"], d["seq_lens"], d["mask_lens"], 16, out=e2e_out[j],
+                                       workspace=arm.ws, exchange=arm.lc)
+            return e2e_out[j] if o is None else o  # ranks > 0 hold no merged output: read back their buffer
         return sqa.small_q_attention(d["query"], reps[j]["key_cache"], reps[j]["value_cache"], d["block_tables"],
                                      d["seq_lens"], 16, arm.max_len, out=e2e_out[j], workspace=arm.ws,
                                      kernel=args.kernel)
@@ -563,6 +577,7 @@ def run_ours(args):
     eager_gbs = kern_bytes / (res["kern_eager_ms"] * 1e-3) / 1e9
     e2e = measure_e2e(arm, args, device)
     e2e_tbs = K * arm.bytes_job / (e2e["e2e_ms"] * 1e-3) / 1e12
+    arm.close()
     launches = arm.launches_per_step * K
     main_desc = dict(kernel_id=arm.kernel_id, max_len=arm.max_len, q=arm.reps[0]["query"],
                      cache_mb=REPLICAS * arm.reps[0]["key_cache"].numel() * 4 / 1e6, bytes_job=arm.bytes_job)
@@ -578,6 +593,7 @@ def run_ours(args):
             sarm = DeviceArm(sub, args, world, rank, device, dist, lib)
             sres = measure_device(sarm, args, device, with_clocks=False)
             sharded[sub] = _sharded_line(sarm, sres, args, peak_gbs)
+            sarm.close()
             del sarm
             torch.cuda.empty_cache()
 
@@ -613,7 +629,7 @@ def run_ours(args):
                        "seq_len": main_desc["max_len"] if name != "cfg5" else 262144, "q_len": int(q.shape[1]),
                        "parallelism": {"cfg2": f"batch-shard x{world}", "cfg3": f"kv-head-shard x{world}",
                                        "cfg4": f"batch-shard (LPT) x{world}",
-                                       "cfg5": f"kv-range split x{world} + NCCL all-gather"}[name],
+                                       "cfg5": f"kv-range split x{world} + NVLink exchange to rank 0"}[name],
                        "l2": f"inputs rotated over {REPLICAS} replicas per GPU "
                              f"({main_desc['cache_mb']:.0f} MB > 126 MB L2)",
                        "us_per_call": round(t_ms / K * 1e3, 3),

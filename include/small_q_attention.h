@@ -264,6 +264,44 @@ typedef struct sqa_append_args {
 
 SQA_API int sqa_cache_append(const sqa_append_args* args, void* stream);
 
+/* ---- Long-context split across the GPUs of one node ----
+ * One sequence's pages are cut into contiguous ranges, one per rank (one
+ * process per GPU); every rank computes the shard form of the operator over
+ * its range (sqa_forward in partial mode, mask_lens in whole-sequence
+ * coordinates) and these calls merge the partial (O, LSE) on rank 0: every rank
+ * stores its partial into its slot in rank 0's memory with peer stores over
+ * NVLink and sets a flag; rank 0 waits for the flags (bounded waits), merges
+ * with the arithmetic of sqa_merge_partials and acknowledges every rank.  No
+ * collective library is involved; the steady state allocates nothing, does not
+ * synchronise the host and can be captured in a CUDA graph (the step counter
+ * lives in device memory).  The upstream has no multi-GPU code; this replaces
+ * an all-gather of the partials to every rank plus a merge on every rank.
+ *
+ * Set-up, on every rank with its device current:
+ *   sqa_lc_create(rank, world, rows, &group, handle)   allocates this rank's
+ *     exchange block (cudaMalloc) and writes its IPC handle (sqa_lc_handle_bytes()
+ *     bytes) to `handle`; rows = batch * q_len * num_q_heads of the merged output;
+ *   exchange the handles between the ranks (any host channel), then
+ *   sqa_lc_connect(group, handles)   maps the other ranks' blocks; `handles` holds
+ *     world handles back to back in rank order.
+ * Every step, in the same order on every rank, on the stream of the partial:
+ *   sqa_lc_exchange(group, o, lse, out, out_bf16, stream)   o fp32 [rows, 128] and
+ *     lse fp32 [rows] (natural log, -inf for a row without keys) of this rank;
+ *     on rank 0 `out` receives the merged [rows, 128] fp16 (bf16 with out_bf16),
+ *     elsewhere it is ignored (may be NULL).
+ * A wait that gives up (about a second: a rank that stopped) sets
+ * SQA_DEV_TIMEOUT in the group's status word, read with sqa_lc_read_status
+ * (synchronises the stream).  sqa_lc_destroy unmaps and frees; call it on every
+ * rank after a barrier, with no exchange in flight.  world <= 8. */
+typedef struct sqa_lc_group sqa_lc_group;
+SQA_API size_t sqa_lc_handle_bytes(void);
+SQA_API int sqa_lc_create(int32_t rank, int32_t world, int64_t rows, sqa_lc_group** group, void* handle_out);
+SQA_API int sqa_lc_connect(sqa_lc_group* group, const void* handles);
+SQA_API int sqa_lc_exchange(sqa_lc_group* group, const float* o, const float* lse, void* out, int32_t out_bf16,
+                            void* stream);
+SQA_API int sqa_lc_read_status(sqa_lc_group* group, uint32_t* device_bits, int clear, void* stream);
+SQA_API int sqa_lc_destroy(sqa_lc_group* group);
+
 /* Static description of a status code. */
 SQA_API const char* sqa_status_string(int status);
 

@@ -55,6 +55,12 @@ EXPORTED_SYMBOLS = (
     "sqa_abi_version",
     "sqa_selected_kernel",
     "sqa_cache_append",
+    "sqa_lc_handle_bytes",
+    "sqa_lc_create",
+    "sqa_lc_connect",
+    "sqa_lc_exchange",
+    "sqa_lc_read_status",
+    "sqa_lc_destroy",
 )
 
 
@@ -159,6 +165,18 @@ def library(path: Path | None = None):
         lib.sqa_selected_kernel.restype = ctypes.c_int
         lib.sqa_cache_append.argtypes = [ctypes.POINTER(SqaAppendArgs), vp]
         lib.sqa_cache_append.restype = ctypes.c_int
+        lib.sqa_lc_handle_bytes.argtypes = []
+        lib.sqa_lc_handle_bytes.restype = sz
+        lib.sqa_lc_create.argtypes = [i32, i32, i64, ctypes.POINTER(vp), vp]
+        lib.sqa_lc_create.restype = ctypes.c_int
+        lib.sqa_lc_connect.argtypes = [vp, vp]
+        lib.sqa_lc_connect.restype = ctypes.c_int
+        lib.sqa_lc_exchange.argtypes = [vp, vp, vp, vp, i32, vp]
+        lib.sqa_lc_exchange.restype = ctypes.c_int
+        lib.sqa_lc_read_status.argtypes = [vp, ctypes.POINTER(ctypes.c_uint32), ctypes.c_int, vp]
+        lib.sqa_lc_read_status.restype = ctypes.c_int
+        lib.sqa_lc_destroy.argtypes = [vp]
+        lib.sqa_lc_destroy.restype = ctypes.c_int
         if path is None:
             _lib = lib
         return lib

@@ -27,7 +27,7 @@ CSRC = PKG / "csrc"
 LIB_DIR = PKG / "_lib"
 LIB_PATH = LIB_DIR / "libsqa_b200.so"
 SOURCES = ["sqa_split_kv.cu", "sqa_split_kv_tc.cu", "sqa_merge.cu", "sqa_api.cu", "sqa_noalloc.cu",
-           "sqa_append.cu"]
+           "sqa_append.cu", "sqa_exchange.cu"]
 HEADERS = ["sqa_internal.h", "sqa_ptx.cuh", "sqa_schedule.cuh", "sqa_merge_row.cuh"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [

@@ -14,7 +14,7 @@
 namespace sqa {
 namespace {
 
-constexpr int kAbiVersion = 108;
+constexpr int kAbiVersion = 109;
 constexpr size_t kAlign = 256;
 constexpr int kMaxDevices = 64;
 constexpr int kCtasPerSm = 2;

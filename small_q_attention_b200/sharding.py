@@ -13,12 +13,18 @@ these are the three ways its operator shards:
 * long-context split — one sequence's pages are cut into contiguous ranges, one
   per rank (each rank holds its range in its own HBM); every rank computes the
   shard form of the operator (normalised O and LSE over the tokens it holds,
-  with the causal rule in whole-sequence coordinates), the partials are
-  all-gathered over NCCL and merged with the log-sum-exp merge kernel.
-  :func:`page_split`, :func:`shard_lengths`, :func:`long_context_attention`.
+  with the causal rule in whole-sequence coordinates) and the partials are
+  merged.  :class:`LongContextGroup` does the exchange in the library's own
+  kernels: each rank stores its partial into rank 0's memory with peer stores
+  over NVLink and sets a flag, rank 0 waits for the flags (bounded) and merges
+  (result on rank 0).  :func:`long_context_attention` without a group
+  all-gathers the partials over ``torch.distributed`` and merges on every rank
+  (any backend; the CPU tests use gloo).  :func:`page_split`,
+  :func:`shard_lengths`.
 
-Every collective here goes through ``torch.distributed`` (NCCL on GPUs, gloo in
-the CPU tests); every bulk load in the kernels reads this GPU's own memory.
+Set-up collectives (handle exchange, barriers) go through ``torch.distributed``;
+every bulk load in the kernels reads this GPU's own memory, and the exchange
+uses plain peer stores (no multicast).
 """
 
 from __future__ import annotations
@@ -88,20 +94,116 @@ def gather_partials(o: torch.Tensor, lse: torch.Tensor, group=None):
     return parts_o.view(world, *o.shape), parts_lse.view(world, *lse.shape)
 
 
+class LongContextGroup:
+    """The exchange step of the long-context split, over NVLink peer memory.
+
+    Collective construction (every rank of the process group, each with its own
+    GPU current): each rank allocates its exchange block (``sqa_lc_create``), the
+    IPC handles are all-gathered over ``torch.distributed`` and every rank maps
+    the others' blocks (``sqa_lc_connect``).  ``rows`` is ``batch * q_len * Hq``
+    of the merged output.  Then :meth:`exchange` once per step on every rank, in
+    the same order: rank r's fp32 (O, LSE) goes into its slot on rank 0 with peer
+    stores, rank 0 merges into ``out`` (fp16 or bf16).  No allocation, no host
+    synchronisation and no collective library on the step; capturable in a CUDA
+    graph.  Waits are bounded (about a second): a rank that stops shows up as
+    ``SQA_DEV_TIMEOUT`` in :meth:`device_status`.  :meth:`close` (collective)
+    unmaps and frees.
+    """
+
+    def __init__(self, rows: int, group=None, device=None):
+        import ctypes
+
+        from . import _native
+
+        self._lib = _native.library()
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rows = int(rows)
+        self._group = group
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        n = int(self._lib.sqa_lc_handle_bytes())
+        handle = (ctypes.c_uint8 * n)()
+        ptr = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            code = self._lib.sqa_lc_create(self.rank, self.world, self.rows, ctypes.byref(ptr), handle)
+            _native.check(code, "sqa_lc_create")
+            self._ptr = ptr
+            handles = [bytes(handle)]
+            if self.world > 1:
+                handles = [None] * self.world
+                dist.all_gather_object(handles, bytes(handle), group=group)
+            joined = (ctypes.c_uint8 * (n * self.world)).from_buffer_copy(b"".join(handles))
+            _native.check(self._lib.sqa_lc_connect(self._ptr, joined), "sqa_lc_connect")
+            if self.world > 1:
+                dist.barrier(group=group)  # every block is mapped before the first exchange
+
+    def exchange(self, o: torch.Tensor, lse: torch.Tensor, out: torch.Tensor | None = None):
+        """Send this rank's partial; on rank 0 return the merged output (``out`` or a
+        new fp16 tensor shaped like ``o``), on the other ranks None."""
+        import ctypes
+
+        from . import _native
+        from .attention import _stream_handle
+
+        if o.dtype != torch.float32 or lse.dtype != torch.float32 or not (o.is_contiguous() and lse.is_contiguous()):
+            raise ValueError("o and lse must be contiguous fp32 tensors")
+        if o.numel() != self.rows * 128 or lse.numel() != self.rows or o.device != self.device:
+            raise ValueError(f"o must hold {self.rows} rows of 128 and lse {self.rows} entries on {self.device}")
+        if self.rank == 0:
+            if out is None:
+                out = torch.empty(o.shape, dtype=torch.float16, device=o.device)
+            if out.dtype not in (torch.float16, torch.bfloat16) or out.numel() != o.numel() or not out.is_contiguous():
+                raise ValueError("out must be a contiguous fp16 or bf16 tensor shaped like o")
+        code = self._lib.sqa_lc_exchange(self._ptr, ctypes.c_void_p(o.data_ptr()), ctypes.c_void_p(lse.data_ptr()),
+                                         ctypes.c_void_p(out.data_ptr() if self.rank == 0 else None),
+                                         int(self.rank == 0 and out.dtype == torch.bfloat16),
+                                         ctypes.c_void_p(_stream_handle(self.device)))
+        _native.check(code, "sqa_lc_exchange")
+        return out if self.rank == 0 else None
+
+    def device_status(self, clear: bool = True) -> int:
+        """Synchronise and return the SQA_DEV_* bits of this rank's exchange block."""
+        import ctypes
+
+        from .attention import _stream_handle
+
+        bits = ctypes.c_uint32(0)
+        self._lib.sqa_lc_read_status(self._ptr, ctypes.byref(bits), int(clear),
+                                     ctypes.c_void_p(_stream_handle(self.device)))
+        return int(bits.value)
+
+    def close(self):
+        """Collective: unmap and free once no rank has an exchange in flight."""
+        from . import _native
+
+        if self._ptr is None:
+            return
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self._group)
+        _native.check(self._lib.sqa_lc_destroy(self._ptr), "sqa_lc_destroy")
+        self._ptr = None
+
+
 def long_context_attention(query, key_cache, value_cache, block_tables, held_lens, mask_lens,
-                           page_size: int = PAGE, group=None, *, out=None, workspace=None):
+                           page_size: int = PAGE, group=None, *, out=None, workspace=None,
+                           exchange: LongContextGroup | None = None):
     """Attention over sequences whose pages are split across the ranks of ``group``.
 
     Each rank passes the full ``query`` and its own shard: ``key_cache`` /
     ``value_cache`` pool on this GPU, ``block_tables`` of the pages it holds,
     ``held_lens`` (tokens held per sequence) and ``mask_lens`` (whole length
     minus this shard's token offset), as given by :func:`shard_lengths`.
-    Returns the merged fp16 output on every rank.
+    With ``exchange`` (a :class:`LongContextGroup` of the same ranks) the merged
+    fp16 output is returned on rank 0 and None elsewhere; without it the
+    partials are all-gathered and the merged output is returned on every rank.
     """
     from .attention import merge_partials, small_q_attention_partial
 
     o, lse = small_q_attention_partial(query, key_cache, value_cache, block_tables, held_lens, page_size,
                                        mask_lens=mask_lens, workspace=workspace)
+    if exchange is not None:
+        return exchange.exchange(o, lse, out=out)
     parts_o, parts_lse = gather_partials(o, lse, group)
     return merge_partials(parts_o, parts_lse, out=out)
 

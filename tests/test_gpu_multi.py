@@ -1,8 +1,13 @@
-"""Sharded operator on 2 GPUs (NCCL): long-context split, batch and KV-head shards.
+"""Sharded operator on 2 GPUs: long-context split, batch and KV-head shards.
 
 Each rank holds the same seeded pool (generated on the host) and runs its
 shard through the C ABI; the reassembled output must match the single-GPU
-operator and the oracle.  Skipped on hosts with fewer than 2 GPUs.
+operator and the oracle.  The long-context split is checked with both
+exchanges: the NCCL all-gather and the library's NVLink peer-store exchange
+(three steps in a row, then a captured CUDA graph replayed twice, then a step
+that rank 1 skips, which rank 0's bounded wait must report as a timeout).
+NVLS is off (NCCL_NVLS_ENABLE=0); the exchange uses plain peer stores.
+Skipped on hosts with fewer than 2 GPUs.
 """
 
 import os
@@ -29,7 +34,7 @@ def _rank(rank, port, result):
     import torch.distributed as dist
 
     from oracle import paged_mtp_attention_reference
-    from small_q_attention_b200 import small_q_attention
+    from small_q_attention_b200 import small_q_attention, small_q_attention_partial
     from small_q_attention_b200.sharding import (kv_head_range, long_context_attention, lpt_batch_shards,
                                                  shard_sequence_pages)
     from small_q_attention_b200.workloads import make_case
@@ -63,6 +68,43 @@ def _rank(rank, port, result):
                                             c["seq_lens"], 16, 8)
         errs["long_vs_whole"] = float((out.float() - whole.float()).abs().max())
         errs["long_vs_oracle"] = float(np.abs(out.float().cpu().numpy() - ref).max())
+
+        # the same split through the NVLink exchange: the merged output lands on rank 0
+        from small_q_attention_b200.sharding import LongContextGroup
+
+        held_t = torch.tensor(held, dtype=torch.int32, device=dev)
+        mlen_t = torch.tensor(mlen, dtype=torch.int32, device=dev)
+        grp = LongContextGroup(rows=2 * 16 * 32)
+        for _ in range(3):
+            p2p = long_context_attention(c["query"], c["key_cache"], c["value_cache"], table, held_t, mlen_t,
+                                         exchange=grp)
+        torch.cuda.synchronize()
+        if rank == 0:
+            errs["p2p_vs_whole"] = float((p2p.float() - whole.float()).abs().max())
+        else:
+            errs["p2p_vs_whole"] = 0.0 if p2p is None else 1.0
+        o, lse = small_q_attention_partial(c["query"], c["key_cache"], c["value_cache"], table, held_t, 16,
+                                           mask_lens=mlen_t)
+        gout = torch.empty(c["query"].shape, dtype=torch.float16, device=dev)
+        s_ = torch.cuda.Stream(dev)
+        s_.wait_stream(torch.cuda.current_stream(dev))
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s_):
+            grp.exchange(o, lse, out=gout)
+        for _ in range(2):
+            gout.zero_()
+            g.replay()
+        torch.cuda.synchronize()
+        del g
+        if rank == 0:
+            errs["graph_vs_whole"] = float((gout.float() - whole.float()).abs().max())
+        errs["p2p_status"] = grp.device_status()
+        dist.barrier()
+        if rank == 0:  # rank 1 skips this step: the bounded wait gives up and says so
+            grp.exchange(o, lse, out=gout)
+            errs["skip_status"] = grp.device_status()
+        dist.barrier()
+        grp.close()
 
         # batch shards (LPT), gathered for checking only
         lens = [3000, 40, 900, 5000, 17]
@@ -111,5 +153,9 @@ def test_two_gpu_sharding():
         for r in range(WORLD):
             errs = result[r]
             assert errs["long_vs_whole"] < 2e-3, errs
+            assert errs["p2p_vs_whole"] < 2e-3 and errs["p2p_status"] == 0, errs
+            if r == 0:
+                assert errs["graph_vs_whole"] < 2e-3, errs
+                assert errs["skip_status"] & 1, errs  # SQA_DEV_TIMEOUT
             for k in ("long_vs_oracle", "batch_vs_oracle", "heads_vs_oracle"):
                 assert errs[k] < 2e-2, (k, errs)

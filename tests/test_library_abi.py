@@ -42,7 +42,7 @@ def test_every_declared_symbol_is_exported(lib):
 
 
 def test_abi_version_and_status_strings(lib):
-    assert lib.sqa_abi_version() == 108
+    assert lib.sqa_abi_version() == 109
     for code in range(6):
         assert lib.sqa_status_string(code).decode()
     assert lib.sqa_status_string(99).decode() == "unknown status"
@@ -156,7 +156,7 @@ def test_torch_extension_registers_the_operators():
 
     build.build_torch_ext()  # no-op when up to date
     ext = _native.torch_ext()
-    assert ext.abi_version() == 108
+    assert ext.abi_version() == 109
     q = torch.empty(2, 4, 32, 128, dtype=torch.float16, device="meta")
     k = torch.empty(64, 16, 8, 128, dtype=torch.float16, device="meta")
     bt = torch.empty(2, 32, dtype=torch.int32, device="meta")
