@@ -383,8 +383,13 @@ def measure_device(arm, args, device, with_clocks=True):
     t_warm = time.perf_counter()
     graph.replay()
     torch.cuda.synchronize()
-    n_warm = int(_max_over_ranks(float(math.ceil(0.05 / max(time.perf_counter() - t_warm, 1e-4))), dist, device))
-    for _ in range(min(n_warm, 200)):
+    t_first = time.perf_counter() - t_warm
+    if arm.lc is not None:  # a cross-rank exchange that timed out anywhere: stop, do not replay it again
+        bits = arm.lc.device_status()
+        if _max_over_ranks(float(bits), dist, device) != 0:
+            raise RuntimeError(f"long-context exchange reported device status bits {bits:#x}")
+    n_warm = int(_max_over_ranks(float(math.ceil(0.05 / max(t_first, 1e-4))), dist, device))
+    for _ in range(min(n_warm, 50)):
         graph.replay()
     torch.cuda.synchronize()
 

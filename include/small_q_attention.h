@@ -291,8 +291,9 @@ SQA_API int sqa_cache_append(const sqa_append_args* args, void* stream);
  *     elsewhere it is ignored (may be NULL).
  * A wait that gives up (about a second: a rank that stopped) sets
  * SQA_DEV_TIMEOUT in the group's status word, read with sqa_lc_read_status
- * (synchronises the stream).  sqa_lc_destroy unmaps and frees; call it on every
- * rank after a barrier, with no exchange in flight.  world <= 8. */
+ * (synchronises the stream).  Tear-down, with no exchange in flight: every rank
+ * calls sqa_lc_disconnect (unmaps the other ranks' blocks), then after a
+ * barrier sqa_lc_destroy (frees its own block).  world <= 8. */
 typedef struct sqa_lc_group sqa_lc_group;
 SQA_API size_t sqa_lc_handle_bytes(void);
 SQA_API int sqa_lc_create(int32_t rank, int32_t world, int64_t rows, sqa_lc_group** group, void* handle_out);
@@ -300,6 +301,7 @@ SQA_API int sqa_lc_connect(sqa_lc_group* group, const void* handles);
 SQA_API int sqa_lc_exchange(sqa_lc_group* group, const float* o, const float* lse, void* out, int32_t out_bf16,
                             void* stream);
 SQA_API int sqa_lc_read_status(sqa_lc_group* group, uint32_t* device_bits, int clear, void* stream);
+SQA_API int sqa_lc_disconnect(sqa_lc_group* group);
 SQA_API int sqa_lc_destroy(sqa_lc_group* group);
 
 /* Static description of a status code. */

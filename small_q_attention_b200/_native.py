@@ -60,6 +60,7 @@ EXPORTED_SYMBOLS = (
     "sqa_lc_connect",
     "sqa_lc_exchange",
     "sqa_lc_read_status",
+    "sqa_lc_disconnect",
     "sqa_lc_destroy",
 )
 
@@ -175,6 +176,8 @@ def library(path: Path | None = None):
         lib.sqa_lc_exchange.restype = ctypes.c_int
         lib.sqa_lc_read_status.argtypes = [vp, ctypes.POINTER(ctypes.c_uint32), ctypes.c_int, vp]
         lib.sqa_lc_read_status.restype = ctypes.c_int
+        lib.sqa_lc_disconnect.argtypes = [vp]
+        lib.sqa_lc_disconnect.restype = ctypes.c_int
         lib.sqa_lc_destroy.argtypes = [vp]
         lib.sqa_lc_destroy.restype = ctypes.c_int
         if path is None:

@@ -273,11 +273,20 @@ int sqa_lc_read_status(sqa_lc_group* g, uint32_t* device_bits, int clear, void* 
   return sqa_read_device_status(g->local, device_bits, clear, stream);
 }
 
-int sqa_lc_destroy(sqa_lc_group* g) {
+int sqa_lc_disconnect(sqa_lc_group* g) {
   if (!g) return SQA_OK;
   int st = SQA_OK;
-  for (int r = 0; r < g->world; ++r)
+  for (int r = 0; r < g->world; ++r) {
     if (g->opened[r] && cudaIpcCloseMemHandle(g->blocks[r]) != cudaSuccess) st = SQA_ERR_CUDA;
+    if (r != g->rank) g->blocks[r] = nullptr;
+    g->opened[r] = false;
+  }
+  return st;
+}
+
+int sqa_lc_destroy(sqa_lc_group* g) {
+  if (!g) return SQA_OK;
+  int st = sqa_lc_disconnect(g);
   if (g->local && cudaFree(g->local) != cudaSuccess) st = SQA_ERR_CUDA;
   delete g;
   return st;

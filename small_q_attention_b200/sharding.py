@@ -180,7 +180,10 @@ class LongContextGroup:
             return
         torch.cuda.synchronize(self.device)
         if self.world > 1:
-            dist.barrier(group=self._group)
+            dist.barrier(group=self._group)  # no rank has an exchange in flight
+        _native.check(self._lib.sqa_lc_disconnect(self._ptr), "sqa_lc_disconnect")
+        if self.world > 1:
+            dist.barrier(group=self._group)  # no rank maps another's block any more
         _native.check(self._lib.sqa_lc_destroy(self._ptr), "sqa_lc_destroy")
         self._ptr = None
 
