@@ -929,6 +929,55 @@ def run_matrix(args):
         Path(args.matrix).write_text("".join(json.dumps(r) + "\n" for r in rows))
 
 
+def run_kernel_case(args):
+    """A few launches of one kernel of the path on a small case (for profiling with ncu
+    -k / -c: the same command runs without the profiler first)."""
+    import torch
+
+    import small_q_attention_b200 as sqa
+    from small_q_attention_b200.workloads import make_case, make_config
+
+    torch.cuda.set_device(0)
+    name = args.kernel_case
+    if name == "append":  # 64 sequences of 2048 tokens, q_len 4: 2 MB of new K/V per call, 0.5 GB pool
+        from small_q_attention_b200.cache import cache_append
+
+        c = make_case(64, 4, [2048] * 64, pool_factor=1.0, seed=0)
+        newk = torch.randn(64, 4, 8, 128, dtype=torch.float16, device="cuda")
+        newv = torch.randn_like(newk)
+        for _ in range(5):
+            cache_append(newk, newv, c["key_cache"], c["value_cache"], c["block_tables"], c["seq_lens"])
+    elif name == "merge":  # 8 per-GPU partials of cfg5's rows (q16 x 32 heads)
+        parts_o = torch.randn(8, 1, 16, 32, 128, device="cuda")
+        parts_lse = torch.randn(8, 1, 16, 32, device="cuda")
+        out = torch.empty(1, 16, 32, 128, dtype=torch.float16, device="cuda")
+        for _ in range(5):
+            sqa.merge_partials(parts_o, parts_lse, out=out)
+    elif name == "exchange":  # the NVLink exchange's kernels at world 1 (own slot, own merge)
+        from small_q_attention_b200.sharding import LongContextGroup
+
+        grp = LongContextGroup(rows=16 * 32)
+        o = torch.randn(1, 16, 32, 128, device="cuda")
+        lse = torch.randn(1, 16, 32, device="cuda")
+        for _ in range(5):
+            grp.exchange(o, lse)
+        torch.cuda.synchronize()
+        if grp.device_status():
+            raise RuntimeError("exchange reported a device error")
+        grp.close()
+    else:  # a split-KV case: cfg2 or a matrix label, through the public API
+        if name.startswith("cfg"):
+            c = make_config(name, seed=0)
+        else:
+            q, kv, b = (int(x) for x in name.replace("q", "").replace("kv", "").replace("b", "").split("_"))
+            c = make_case(b, q, [kv] * b, pool_factor=1.0, seed=0)
+        for _ in range(5):
+            sqa.small_q_attention(c["query"], c["key_cache"], c["value_cache"], c["block_tables"], c["seq_lens"],
+                                  16, max(c["lens"]), kernel=args.kernel)
+    torch.cuda.synchronize()
+    print(json.dumps({"kernel_case": name, "ok": True}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -960,12 +1009,17 @@ def main():
                     help="--impl reference: leave out the upstream GPU kernel beside the CPU reference")
     ap.add_argument("--ref-gpu-matrix", type=str, default=None,
                     help="--impl reference: also time the upstream GPU kernel on every matrix case, JSONL here")
+    ap.add_argument("--kernel-case", type=str, default=None,
+                    help="run one kernel a few times on a small case (append, merge, exchange, cfg2, q4_kv8192_b4, "
+                         "...) for an ncu capture")
     ap.add_argument("--matrix-replica-mb", type=float, default=400.0,
                     help="matrix: MB of distinct K/V replicas rotated per case (>= 126 MB L2)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
-    if args.impl == "reference":
+    if args.kernel_case:
+        run_kernel_case(args)
+    elif args.impl == "reference":
         run_reference(args)
     elif args.matrix_only or args.matrix:
         run_matrix(args)
