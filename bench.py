@@ -66,7 +66,14 @@ def _peaks():
     return FALLBACK_HBM_GBS, "fallback"
 
 
-KERNEL_NAMES = {1: "sqa_split_kv_kernel", 2: "sqa_split_kv_tc_kernel"}
+class _KernelNames(dict):
+    """Kernel id (sqa_selected_kernel) -> name; 2 + 100 * C is the tcgen05 kernel in clusters of C."""
+
+    def __missing__(self, k):
+        return f"sqa_split_kv_tc_kernel (clusters of {(k - 2) // 100})" if k > 100 else f"kernel {k}"
+
+
+KERNEL_NAMES = _KernelNames({1: "sqa_split_kv_kernel", 2: "sqa_split_kv_tc_kernel"})
 def _as_dtype(c, name):
     """A workload dict with its Q/K/V cast to ``name`` ("f16" leaves it as generated)."""
     if name == "f16":
@@ -85,7 +92,7 @@ def _traffic(workload: str, kernel_id: int):
     p = ROOT / "profiles" / "traffic.json"
     if not p.exists():
         return None
-    return json.loads(p.read_text()).get(f"{workload}/{KERNEL_NAMES[kernel_id]}")
+    return json.loads(p.read_text()).get(f"{workload}/{KERNEL_NAMES[kernel_id]}")  # measured per build
 
 
 # ------------------------------------------------------------------ clocks
@@ -298,11 +305,15 @@ class DeviceArm:
         self.longctx = name == "cfg5"
         self.reps, self.bytes_rank, self.bytes_job = _rank_cases(name, world, rank, device, REPLICAS)
         self.max_len = max(max(r["lens"]) for r in self.reps)
+        self.min_len = 0 if args.no_length_hints else min(min(r["lens"]) for r in self.reps)
         self.cargs, self.outs, self.lses = [], [], []
         ws_bytes = 0
         for r in self.reps:
             a = _fill_args(r["query"], r["key_cache"], r["value_cache"], r["block_tables"], r["seq_lens"],
                            r.get("mask_lens"), self.max_len, 0, 0, args.kernel)
+            # the serving loop knows its lengths: both bounds steer the launch (cluster mode
+            # for near-uniform batches), as a planned step would
+            a.min_seq_len = min(r["lens"]) if not args.no_length_hints else 0
             if self.longctx:
                 o = torch.empty(r["query"].shape, dtype=torch.float32, device=device)
                 l = torch.empty(r["query"].shape[:3], dtype=torch.float32, device=device)
@@ -329,9 +340,10 @@ class DeviceArm:
         self.kernel_id = lib.sqa_selected_kernel(ctypes.byref(self.cargs[0]), device.index)
         if self.kernel_id < 0:
             _native.check(-self.kernel_id, "sqa_selected_kernel")
-        # our kernels per step on rank 0: split-KV + per-call merge, in long-context mode also the
-        # cross-rank merge (one GPU) or the send + merge of the NVLink exchange (several)
-        self.launches_per_step = (4 if self.lc is not None else 3) if self.longctx else 2
+        # our kernels per step on rank 0: split-KV + per-call merge (none in cluster mode), in
+        # long-context mode also the cross-rank merge (one GPU) or the exchange's send + merge
+        self.launches_per_step = (1 if self.kernel_id > 100 else 2) + (
+            (2 if self.lc is not None else 1) if self.longctx else 0)
 
     def close(self):
         if self.lc is not None:
@@ -503,7 +515,7 @@ def measure_e2e(arm, args, device):
             return e2e_out[j] if o is None else o  # ranks > 0 hold no merged output: read back their buffer
         return sqa.small_q_attention(d["query"], reps[j]["key_cache"], reps[j]["value_cache"], d["block_tables"],
                                      d["seq_lens"], 16, arm.max_len, out=e2e_out[j], workspace=arm.ws,
-                                     kernel=args.kernel)
+                                     kernel=args.kernel, min_seq_len=arm.min_len)
 
     def step(i):
         j = i % REPLICAS
@@ -853,12 +865,14 @@ def matrix_rows(args, settle: float = 1.0, replica_mb: float = 400.0, verbose: b
         n_rep = max(2, min(64, math.ceil(replica_mb * 1e6 / max(1, cache_bytes))))
         inst = [first] + [make(label, c, s_) for s_ in range(1, n_rep)]
         outs = [torch.empty_like(x["query"]) for x in inst]
+        min_len = 0 if args.no_length_hints else min(inst[0]["lens"])
         fn = lambda i: sqa.small_q_attention(  # noqa: E731
             inst[i]["query"], inst[i]["key_cache"], inst[i]["value_cache"], inst[i]["block_tables"],
-            inst[i]["seq_lens"], 16, max(inst[i]["lens"]), out=outs[i], workspace=ws, kernel=args.kernel)
+            inst[i]["seq_lens"], 16, max(inst[i]["lens"]), out=outs[i], workspace=ws, kernel=args.kernel,
+            min_seq_len=min_len)
         kernel_id = sqa.selected_kernel(inst[0]["query"], inst[0]["key_cache"], inst[0]["value_cache"],
                                         inst[0]["block_tables"], inst[0]["seq_lens"], 16, max(inst[0]["lens"]),
-                                        kernel=args.kernel)
+                                        kernel=args.kernel, min_seq_len=min_len)
         for i in range(5):
             fn(i % len(inst))
         torch.cuda.synchronize()
@@ -1009,6 +1023,8 @@ def main():
                     help="--impl reference: leave out the upstream GPU kernel beside the CPU reference")
     ap.add_argument("--ref-gpu-matrix", type=str, default=None,
                     help="--impl reference: also time the upstream GPU kernel on every matrix case, JSONL here")
+    ap.add_argument("--no-length-hints", action="store_true",
+                    help="do not pass min_seq_len (no cluster mode): the cost-balanced schedule for every call")
     ap.add_argument("--kernel-case", type=str, default=None,
                     help="run one kernel a few times on a small case (append, merge, exchange, cfg2, q4_kv8192_b4, "
                          "...) for an ncu capture")

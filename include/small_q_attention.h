@@ -137,6 +137,18 @@ typedef struct sqa_args {
    * fp16 tolerance).  Fold the caches' dequantisation scales into sm_scale (K)
    * and out_scale (V). */
   int32_t kv_dtype;
+  /* Lower bound of seq_lens (0 = unknown).  Like max_seq_len, only steers the
+   * launch: with both bounds within 15% of each other (near-uniform lengths)
+   * and few enough (sequence, KV head) segments for two or more CTAs each, the
+   * tcgen05 kernel splits every segment evenly over a thread-block cluster and
+   * reduces the parts through distributed shared memory (no merge launch).  A
+   * wrong hint still gives the right result, only a slower launch. */
+  int32_t min_seq_len;
+  /* Cluster mode: 0 = auto (above), 1 = off (segments cut into cost-balanced
+   * CTA ranges, merged by a second kernel), 2 / 4 / 8 / 16 = that many CTAs per
+   * segment (tcgen05 kernel; 16-CTA clusters where the device allows them).
+   * No upstream counterpart (the upstream splits with chunk_keys, ext.cu:1178). */
+  int32_t cluster;
 } sqa_args;
 
 #define SQA_DTYPE_F16 0
@@ -185,7 +197,8 @@ SQA_API int sqa_merge_partials(const float* parts_o, const float* parts_lse, int
 SQA_API int sqa_read_device_status(void* workspace, uint32_t* device_bits, int clear, void* stream);
 
 /* The kernel sqa_forward would launch for these arguments on `device` (-1 =
- * the current device): 1 = warp-level mma.sync kernel, 2 = tcgen05 kernel;
+ * the current device): 1 = warp-level mma.sync kernel, 2 = tcgen05 kernel,
+ * 2 + 100 * C = tcgen05 kernel in clusters of C CTAs per segment;
  * minus the SQA_ERR_* code on invalid arguments.  Resolves kernel = 0 (auto).
  * No upstream counterpart (introspection for measurement and tests). */
 SQA_API int sqa_selected_kernel(const sqa_args* args, int device);

@@ -120,6 +120,8 @@ class SqaArgs(ctypes.Structure):
         ("out_scale", ctypes.c_float),
         ("page_stride", ctypes.c_int64),
         ("kv_dtype", ctypes.c_int32),
+        ("min_seq_len", ctypes.c_int32),
+        ("cluster", ctypes.c_int32),
     ]
 
 

@@ -180,12 +180,14 @@ def _fill_args(query, key_cache, value_cache, block_tables, seq_lens, mask_lens,
 
 def selected_kernel(query, key_cache, value_cache, block_tables, seq_lens, page_size,
                     max_seq_len: int = 0, *, num_ctas: int = 0, min_pages_per_cta: int = 0,
-                    kernel: int = 0, kv_layout: str = "NHD") -> int:
+                    kernel: int = 0, kv_layout: str = "NHD", min_seq_len: int = 0, cluster: int = 0) -> int:
     """The kernel a call with these shapes launches: 1 = warp-level mma.sync,
-    2 = tcgen05 (``kernel=0`` resolved the way ``small_q_attention`` resolves it)."""
+    2 = tcgen05, 2 + 100 * C = tcgen05 in clusters of C CTAs (``kernel=0`` and
+    ``cluster=0`` resolved the way ``small_q_attention`` resolves them)."""
     _check_inputs(query, key_cache, value_cache, block_tables, seq_lens, page_size, kv_layout=kv_layout)
     args = _fill_args(query, key_cache, value_cache, block_tables, seq_lens, None, max_seq_len,
                       num_ctas, min_pages_per_cta, kernel, kv_layout)
+    args.min_seq_len, args.cluster = int(min_seq_len), int(cluster)
     code = _native.library().sqa_selected_kernel(ctypes.byref(args), query.device.index)
     if code < 0:
         _native.check(-code, "sqa_selected_kernel")
@@ -230,7 +232,8 @@ def _raise_device_bits(bits: int) -> None:
 def small_q_attention(query, key_cache, value_cache, block_tables, seq_lens, page_size: int,
                       max_seq_len: int = 0, *, out=None, workspace=None, num_ctas: int = 0,
                       min_pages_per_cta: int = 0, kernel: int = 0, check: bool = False,
-                      kv_layout: str = "NHD", sm_scale: float | None = None, out_scale: float = 1.0):
+                      kv_layout: str = "NHD", sm_scale: float | None = None, out_scale: float = 1.0,
+                      min_seq_len: int = 0, cluster: int = 0):
     """Causal paged MTP attention; returns ``[batch, q_len, Hq, 128]`` in the input type.
 
     Q/K/V are FP16 (the upstream contract) or BF16 (all three of one type;
@@ -251,6 +254,10 @@ def small_q_attention(query, key_cache, value_cache, block_tables, seq_lens, pag
     tensor memory (same operator).  ``kv_layout`` "HND" takes caches as
     ``[pages, Hkv, 16, 128]``; ``sm_scale`` (default ``128**-0.5``) scales q.k and
     ``out_scale`` every output row (FlashInfer's ``bmm1_scale`` / ``bmm2_scale``).
+    ``min_seq_len`` (a lower bound of ``seq_lens``, 0 = unknown) lets the launch
+    split each (sequence, KV head) over a thread-block cluster when lengths are
+    near-uniform; ``cluster`` forces that mode (2/4/8/16 CTAs) or turns it off (1).
+    Both only steer the launch: the result is the same operator.
     """
     if not _cuda_available():
         raise RuntimeError("CUDA is required for the small-q attention kernel")
@@ -258,7 +265,7 @@ def small_q_attention(query, key_cache, value_cache, block_tables, seq_lens, pag
         return _native.torch_ext().forward(
             query, key_cache, value_cache, block_tables, seq_lens, page_size, max_seq_len, out, workspace,
             num_ctas, min_pages_per_cta, kernel, check, _layout_code(kv_layout),
-            0.0 if sm_scale is None else sm_scale, out_scale)
+            0.0 if sm_scale is None else sm_scale, out_scale, min_seq_len, cluster)
     except TypeError as e:  # a non-tensor where a tensor belongs (pybind11's argument check)
         raise ValueError(f"all inputs must be CUDA tensors ({e})") from None
 
@@ -267,7 +274,8 @@ def small_q_attention_partial(query, key_cache, value_cache, block_tables, seq_l
                               mask_lens=None, max_seq_len: int = 0, *, out=None, out_lse=None,
                               workspace=None, num_ctas: int = 0, min_pages_per_cta: int = 0,
                               kernel: int = 0, check: bool = False, kv_layout: str = "NHD",
-                              sm_scale: float | None = None, out_scale: float = 1.0):
+                              sm_scale: float | None = None, out_scale: float = 1.0, min_seq_len: int = 0,
+                              cluster: int = 0):
     """Attention over the tokens this call holds; returns ``(O fp32, LSE fp32)``.
 
     The shard form of the operator for splitting one sequence's KV range:
@@ -283,7 +291,7 @@ def small_q_attention_partial(query, key_cache, value_cache, block_tables, seq_l
         return _native.torch_ext().forward_partial(
             query, key_cache, value_cache, block_tables, seq_lens, page_size, mask_lens, max_seq_len, out, out_lse,
             workspace, num_ctas, min_pages_per_cta, kernel, check, _layout_code(kv_layout),
-            0.0 if sm_scale is None else sm_scale, out_scale)
+            0.0 if sm_scale is None else sm_scale, out_scale, min_seq_len, cluster)
     except TypeError as e:
         raise ValueError(f"all inputs must be CUDA tensors ({e})") from None
 

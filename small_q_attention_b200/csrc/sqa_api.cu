@@ -14,7 +14,7 @@
 namespace sqa {
 namespace {
 
-constexpr int kAbiVersion = 109;
+constexpr int kAbiVersion = 110;
 constexpr size_t kAlign = 256;
 constexpr int kMaxDevices = 64;
 constexpr int kCtasPerSm = 2;
@@ -169,6 +169,7 @@ struct Plan {
   int stages;
   int smem;
   int kv_fp8 = 0;  // fp8 caches: 2 = 4-page blocks, 3 = 8-page blocks
+  int cluster = 0;  // tcgen05 cluster mode: CTAs per segment (0 = cost-balanced ranges + merge kernel)
   int segments;
   int pieces;
   size_t off_lse, off_o, off_timeline = 0, bytes;
@@ -201,6 +202,11 @@ int validate(const sqa_args* a) {
     return SQA_ERR_INVALID_ARGUMENT;
   if (!(a->sm_scale >= 0.f) || !std::isfinite(a->sm_scale) || !std::isfinite(a->out_scale))
     return SQA_ERR_INVALID_ARGUMENT;
+  if (a->min_seq_len < 0) return SQA_ERR_INVALID_ARGUMENT;
+  if (a->cluster != 0 && a->cluster != 1 && a->cluster != 2 && a->cluster != 4 && a->cluster != 8 &&
+      a->cluster != 16)
+    return SQA_ERR_INVALID_ARGUMENT;
+  if (a->cluster >= 2 && a->kernel == 1) return SQA_ERR_UNSUPPORTED;  // clusters are a tcgen05-kernel mode
   // unit indices are 32-bit on the device
   if ((long long)a->batch * a->num_kv_heads * a->max_pages >= (1ll << 31)) return SQA_ERR_UNSUPPORTED;
   if ((long long)a->num_pages * kPageSize >= (1ll << 31)) return SQA_ERR_UNSUPPORTED;
@@ -246,6 +252,7 @@ int make_plan(const sqa_args* a, int device, Plan* plan) {
   } else {
     pl.tc = a->kernel == 2;
   }
+  if (a->cluster >= 2) pl.tc = true;  // a requested cluster size runs the tcgen05 kernel
   const int ctas_per_sm = pl.tc ? 1 : kCtasPerSm;  // tcgen05: one CTA per SM (all of TMEM)
   const int min_pages = a->min_pages_per_cta > 0 ? a->min_pages_per_cta : kDefaultMinPagesPerCta;
   long long grid = a->num_ctas > 0 ? a->num_ctas : (long long)sms * ctas_per_sm;
@@ -255,6 +262,26 @@ int make_plan(const sqa_args* a, int device, Plan* plan) {
   }
   if (grid < 1) grid = 1;
   pl.grid = (int)grid;
+  const int grid_default = pl.grid;
+  if (pl.tc && a->num_ctas == 0 && a->cluster != 1) {
+    // Cluster mode: every (sequence, KV head) segment split evenly over C CTAs of one
+    // thread-block cluster, parts reduced through distributed shared memory.  Auto
+    // only for near-uniform lengths (both hints within 15%), two or more CTAs per
+    // segment on the SMs and at least 16 pages per CTA; every cluster resident at once.
+    const long long segs = pl.segments;
+    if (a->cluster >= 2) {
+      pl.cluster = a->cluster;
+    } else if (a->max_seq_len > 0 && a->min_seq_len > 0 && 100LL * a->min_seq_len >= 85LL * a->max_seq_len) {
+      const int cands[4] = {16, 8, 4, 2};
+      for (int c : cands) {
+        if (segs * c <= sms && pages_upper / c >= 16) {
+          pl.cluster = c;
+          break;
+        }
+      }
+    }
+    if (pl.cluster) pl.grid = (int)(segs * pl.cluster);
+  }
   if (pl.tc) {
     // a ring of blocks in up to 227 KB of shared memory: 32 KB (16-bit caches, 4
     // pages), fp8 caches 16 KB (4 pages) or, for long per-CTA ranges, 32 KB (8 pages)
@@ -264,6 +291,18 @@ int make_plan(const sqa_args* a, int device, Plan* plan) {
     pl.stages = (kMaxSmemPerCta - fixed) / (split_kv_tc_block_bytes(pl.kv_fp8) + 16);
     if (pl.stages > kMaxStages) pl.stages = kMaxStages;
     pl.smem = split_kv_tc_smem_bytes(pl.stages, pl.kv_fp8);
+    if (pl.cluster) {
+      // every cluster must be resident at once for the auto choice; a requested size
+      // only needs the device to launch it (more clusters run in waves)
+      const int fit = split_kv_tc_max_clusters(pl.cluster, pl.smem);
+      if (fit < 1) {
+        if (a->cluster >= 2) return SQA_ERR_UNSUPPORTED;
+        pl.cluster = 0;
+      } else if (a->cluster == 0 && fit < pl.segments) {
+        pl.cluster = 0;
+      }
+      if (!pl.cluster) pl.grid = grid_default;
+    }
   } else {
     const int fixed = split_kv_smem_bytes(pl.shape, 0);
     pl.stages = (kSmemPerCta - fixed) / (kStageBytes + 24);
@@ -331,7 +370,7 @@ int sqa_selected_kernel(const sqa_args* args, int device) {
   Plan pl;
   st = make_plan(args, dev, &pl);
   if (st != SQA_OK) return -st;
-  return pl.tc ? 2 : 1;
+  return pl.tc ? 2 + 100 * pl.cluster : 1;
 }
 
 int sqa_workspace_init(void* workspace, size_t workspace_bytes, void* stream) {
@@ -393,6 +432,7 @@ int forward_impl(const sqa_args* a, void* workspace, size_t workspace_bytes, voi
   p.out_scale = a->out_scale != 0.f ? a->out_scale : 1.f;
   p.kv_fp8 = pl.kv_fp8;
   p.seg_cost = pl.tc ? kSegmentCostTc : kSegmentCostMma;
+  p.cluster = pl.cluster;
 
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_ptr);
   // Timing events: under stream capture they become event-record nodes of the
@@ -432,6 +472,7 @@ int forward_impl(const sqa_args* a, void* workspace, size_t workspace_bytes, voi
   m.bf16 = p.bf16;
   m.split_grid = pl.grid;
   m.seg_cost = p.seg_cost;
+  if (pl.cluster) return SQA_OK;  // the clusters reduced every segment themselves
   if (launch_segment_merge(m, pl.shape.rows_pad, stream) != cudaSuccess) return SQA_ERR_CUDA;
   if (!debug_sync(stream, "merge kernel", pl.segments, 0, a)) return SQA_ERR_CUDA;
   return SQA_OK;

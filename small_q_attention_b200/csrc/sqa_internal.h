@@ -58,6 +58,8 @@ struct SplitKvParams {
   int kv_fp8;                   // caches hold fp8 e4m3, read as fp8 by the tensor core (tcgen05 kernel):
                                 // 2 in blocks of 4 pages, 3 in blocks of 8 pages
   int seg_cost;                 // schedule: units a segment start costs a CTA (one more epilogue)
+  int cluster;                  // tcgen05 kernel: 0, or C >= 2 = segment blockIdx.x / C split evenly over
+                                // a thread-block cluster of C CTAs, partials reduced through DSMEM
 };
 
 struct MergeParams {
@@ -91,5 +93,8 @@ cudaError_t launch_split_kv_tc(const SplitKvParams& p, const CUtensorMap& tm_k, 
                                int grid, int smem_bytes, cudaStream_t stream);
 int split_kv_tc_smem_bytes(int num_blocks, int kv_fp8 = 0);
 int split_kv_tc_block_bytes(int kv_fp8 = 0);
+// Clusters of `cluster` tcgen05 CTAs (with `smem_bytes` each) that can be resident at once on
+// the current device (0 when that cluster size cannot be launched).
+int split_kv_tc_max_clusters(int cluster, int smem_bytes);
 
 }  // namespace sqa

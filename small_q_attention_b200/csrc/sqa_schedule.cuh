@@ -199,9 +199,57 @@ __device__ __forceinline__ Schedule compute_schedule(const SplitKvParams& p) {
   return s;
 }
 
+// Cluster mode (p.cluster = C >= 2, tcgen05 kernel): CTA blockIdx.x works on segment
+// s = blockIdx.x / C, the (blockIdx.x % C)-th of C equal page ranges (whole 4-page
+// blocks; a range may be empty).  Whole warp; every lane gets the result.  Lengths
+// are read once; block 0 raises the same status bits as compute_schedule.
+template <bool kSpec>
+__device__ __forceinline__ Schedule cluster_schedule(const SplitKvParams& p) {
+  const int lane = threadIdx.x & 31;
+  const int C = p.cluster;
+  const int seg = (int)blockIdx.x / C;
+  const int k = (int)blockIdx.x - seg * C;
+  const int b = seg / p.hkv;
+  const int h = seg - b * p.hkv;
+  unsigned int flags = 0;
+  int before = 0, pages_b = 0;
+  for (int base = 0; base < p.batch; base += 32) {
+    const int i = base + lane;
+    int pg = 0;
+    if (i < p.batch) {
+      const int len = load_len<kSpec>(p, i);
+      pg = min((max(len, 0) + kPageSize - 1) / kPageSize, p.max_pages);
+      if (len > p.max_pages * kPageSize) flags |= 2u;      // SQA_DEV_SEQ_TOO_LONG
+      if (p.out != nullptr && len < p.q_len) flags |= 4u;  // SQA_DEV_SEQ_TOO_SHORT
+    }
+    int pre = (i < b) ? pg : 0;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) pre += __shfl_xor_sync(0xffffffffu, pre, off);
+    before += pre;
+    if (b >= base && b < base + 32) pages_b = __shfl_sync(0xffffffffu, pg, b - base);
+  }
+  if (!kSpec) {
+    flags = __reduce_or_sync(0xffffffffu, flags);
+    if (blockIdx.x == 0 && lane == 0 && flags) atomicOr(p.status, flags);
+  }
+  const int per = ((pages_b + C - 1) / C + 3) / 4 * 4;  // pages per CTA, whole 4-page blocks
+  const int lo = min(pages_b, k * per);
+  const int hi = min(pages_b, lo + per);
+  Schedule sch;
+  sch.b0 = b < p.batch ? b : p.batch;
+  sch.u_b0 = before * p.hkv;  // units of the sequences before b
+  sch.pages_b0 = pages_b;
+  const int seg_start = sch.u_b0 + h * pages_b;
+  sch.start = seg_start + lo;
+  sch.end = seg_start + hi;
+  sch.per_cta = per;
+  sch.abort = 0;
+  return sch;
+}
+
 // Warp 0: the schedule into shared memory, before the CTA-wide barrier.
 __device__ __forceinline__ void build_schedule(const SplitKvParams& p, Schedule* sch) {
-  const Schedule s = compute_schedule<false>(p);
+  const Schedule s = p.cluster ? cluster_schedule<false>(p) : compute_schedule<false>(p);
   if ((threadIdx.x & 31) == 0) *sch = s;
 }
 
@@ -280,7 +328,7 @@ template <bool F8>
 __device__ __forceinline__ void prefetch_start(const SplitKvParams& p, const CUtensorMap* tm_k,
                                                const CUtensorMap* tm_v, int budget) {
   const int lane = threadIdx.x & 31;
-  const Schedule s = compute_schedule<true>(p);
+  const Schedule s = p.cluster ? cluster_schedule<true>(p) : compute_schedule<true>(p);
   if (s.start >= s.end) return;
   int b = s.b0;
   int pages = s.pages_b0;

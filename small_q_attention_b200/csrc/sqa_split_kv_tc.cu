@@ -39,6 +39,8 @@
 // The QK issuer runs up to four blocks ahead of the softmax (one per S slot).
 #include <cuda_fp8.h>
 
+#include <mutex>
+
 #include "sqa_internal.h"
 #include "sqa_ptx.cuh"
 #include "sqa_schedule.cuh"
@@ -86,6 +88,10 @@ constexpr int kMergeStride = kMergeCols + 1;    // floats per merge row (conflic
 constexpr int kMergeBytes = 128 * kMergeStride * 4;  // one row per TMEM lane
 constexpr int kMlBytes = 128 * 8;               // (max, sum) per lane
 constexpr float kRescaleLog2 = 8.f;
+// Cluster mode: a CTA's normalised part [rows <= 64, 128] fp32 and its LSEs sit at
+// the start of the operand ring (idle once the CTA's one piece is done).
+constexpr int kClusterRows = 64;
+constexpr int kMaxCluster = 16;
 constexpr float kLn2 = 0.6931471805599453f;
 
 struct TcSmem {
@@ -684,7 +690,11 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
         }
         const size_t out_row = (size_t)(w.b * p.q_len + (r >> 2)) * p.hq + w.h * kGroup + (r & 3);
         const int col = c0 + ch * 8;
-        if (whole && p.out != nullptr) {
+        if (p.cluster) {  // cluster mode: this CTA's part, for the reduction across the cluster
+          float* dst = reinterpret_cast<float*>(sm.ring) + r * kHeadDim + col;
+          *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+          *reinterpret_cast<float4*>(dst + 4) = make_float4(v[4], v[5], v[6], v[7]);
+        } else if (whole && p.out != nullptr) {
           uint4 h;
           h.x = pack2<BF>(v[0], v[1]);
           h.y = pack2<BF>(v[2], v[3]);
@@ -705,8 +715,9 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
     (void)t_ep;
     if (rep == 0 && active) {
       const size_t out_row = (size_t)(w.b * p.q_len + (lrow >> 2)) * p.hq + w.h * kGroup + (lrow & 3);
-      if (whole && p.out == nullptr) p.out_lse[out_row] = lse;
-      if (!whole) p.ws_lse[(size_t)piece * p.rows_pad + lrow] = lse;
+      if (p.cluster) reinterpret_cast<float*>(sm.ring)[kClusterRows * kHeadDim + lrow] = lse;
+      else if (whole && p.out == nullptr) p.out_lse[out_row] = lse;
+      else if (!whole) p.ws_lse[(size_t)piece * p.rows_pad + lrow] = lse;
     }
 
     gb0 += nblk;
@@ -718,6 +729,92 @@ __device__ void tc_softmax(const SplitKvParams& p, const Schedule& sch, const Tc
 #ifdef SQA_DEBUG_TIMELINE
   if (tid == 0 && p.timeline) p.timeline[(size_t)blockIdx.x * 32 + 15] = (unsigned long long)gb0 * 100 + pc;
 #endif
+}
+
+// ------------------------------------------------------------------ cluster reduction (all threads)
+// Cluster mode: each CTA of the cluster left its part of the segment (normalised
+// rows and natural-log LSEs, -inf for a part without keys) in its shared memory;
+// after a cluster barrier, the cluster's rank-0 CTA reads every part through
+// distributed shared memory and writes the segment's rows with the arithmetic of
+// the split-KV merge (max, weights exp(lse - max), sum, divide; 0 for a row that
+// sees no key).  A second barrier keeps every CTA's shared memory alive until
+// rank 0 has read it.  Every thread of every CTA reaches both barriers.
+template <bool BF>
+__device__ void tc_cluster_reduce(const SplitKvParams& p, const TcSmem& sm, const Schedule& s) {
+  float* cl = reinterpret_cast<float*>(sm.ring);
+  float* cl_lse = cl + kClusterRows * kHeadDim;
+  const int rows = kGroup * p.q_len;
+  if (s.start >= s.end)  // no page here: this part carries no weight
+    for (int r = threadIdx.x; r < rows; r += blockDim.x) cl_lse[r] = -INFINITY;
+  cluster_sync_all();
+  const int C = p.cluster;
+  if ((int)blockIdx.x % C == 0) {
+    const int seg = (int)blockIdx.x / C;
+    const int b = seg / p.hkv;
+    const int h = seg - b * p.hkv;
+    const uint32_t o_base = smem_u32(cl), l_base = smem_u32(cl_lse);
+    for (int idx = threadIdx.x; idx < rows * (kHeadDim / 4); idx += blockDim.x) {
+      const int r = idx / (kHeadDim / 4);
+      const int c4 = idx - r * (kHeadDim / 4);
+      // parts 8 at a time, every load of a batch in flight at once; a running max
+      // rescales what earlier batches summed (one round trip for C <= 8)
+      constexpr int kBatch = 8;
+      float mx = -INFINITY, total = 0.f;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int j0 = 0; j0 < C; j0 += kBatch) {
+        float l[kBatch];
+        float4 v[kBatch];
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+          if (j0 + j < C) {
+            l[j] = ld_cluster_f32(cluster_map(l_base + r * 4, j0 + j));
+            v[j] = ld_cluster_v4(cluster_map(o_base + (r * kHeadDim + c4 * 4) * 4, j0 + j));
+          } else {
+            l[j] = -INFINITY;
+            v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+        }
+        float bmx = mx;
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) bmx = fmaxf(bmx, l[j]);
+        if (bmx == -INFINITY) continue;  // nothing visible so far
+        if (bmx > mx && mx != -INFINITY) {
+          const float scale = ex2((mx - bmx) * 1.4426950408889634f);
+          total *= scale;
+          acc.x *= scale;
+          acc.y *= scale;
+          acc.z *= scale;
+          acc.w *= scale;
+        }
+        mx = bmx;
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+          const float wgt = ex2((l[j] - mx) * 1.4426950408889634f);  // -inf -> 0
+          total += wgt;
+          acc.x += wgt * v[j].x;
+          acc.y += wgt * v[j].y;
+          acc.z += wgt * v[j].z;
+          acc.w += wgt * v[j].w;
+        }
+      }
+      const float inv = total > 0.f ? 1.f / total : 0.f;
+      acc.x *= inv;
+      acc.y *= inv;
+      acc.z *= inv;
+      acc.w *= inv;
+      const size_t out_row = (size_t)(b * p.q_len + (r >> 2)) * p.hq + h * kGroup + (r & 3);
+      if (p.out != nullptr) {
+        uint2 o;
+        o.x = pack2<BF>(acc.x, acc.y);
+        o.y = pack2<BF>(acc.z, acc.w);
+        *reinterpret_cast<uint2*>(p.out + out_row * kHeadDim + c4 * 4) = o;
+      } else {
+        *reinterpret_cast<float4*>(p.out_o + out_row * kHeadDim + c4 * 4) = acc;
+        if (c4 == 0) p.out_lse[out_row] = total > 0.f ? (mx + __log2f(total) * kLn2) : -INFINITY;
+      }
+    }
+  }
+  cluster_sync_all();
 }
 
 template <int R, bool BF, int KV>
@@ -811,6 +908,7 @@ __global__ void __launch_bounds__(kThreadsTc, 1)
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
+  if (p.cluster) tc_cluster_reduce<BF>(p, sm, s);
 #ifdef SQA_DEBUG_TIMELINE
   if (tl && threadIdx.x == 0) {
     tl[4] = global_timer_ns();
@@ -836,16 +934,24 @@ cudaError_t launch_tc(const SplitKvParams& p, const CUtensorMap& tm_k, const CUt
     if (err != cudaSuccess) return err;
     if (dev >= 0 && dev < 64) configured[dev] = smem_bytes;
   }
+  if (p.cluster > 8) {  // 16-CTA clusters are outside the portable size
+    err = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (err != cudaSuccess) return err;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreadsTc);
   cfg.dynamicSmemBytes = smem_bytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = p.cluster > 1 ? p.cluster : 1;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = p.cluster > 1 ? 2 : 1;
   err = cudaLaunchKernelEx(&cfg, kernel, p, tm_k, tm_v);
   if (err != cudaSuccess) return err;
   return cudaGetLastError();
@@ -854,6 +960,42 @@ cudaError_t launch_tc(const SplitKvParams& p, const CUtensorMap& tm_k, const CUt
 }  // namespace
 
 int split_kv_tc_block_bytes(int kv_fp8) { return kv_fp8 == 3 ? 8 * 4096 : kv_fp8 ? 4 * 4096 : kBlockBytes; }
+
+int split_kv_tc_max_clusters(int cluster, int smem_bytes) {
+  if (cluster < 2 || cluster > kMaxCluster) return 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  static std::mutex mu;
+  static int cache[64][kMaxCluster + 1] = {};
+  static int cache_smem[64][kMaxCluster + 1] = {};
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache_smem[dev][cluster] == smem_bytes) return cache[dev][cluster];
+  auto kernel = sqa_split_kv_tc_kernel<4, false, 0>;  // every instantiation: same threads, 1 CTA per SM
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes) != cudaSuccess ||
+      (cluster > 8 && cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)) {
+    (void)cudaGetLastError();
+    return 0;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(cluster);
+  cfg.blockDim = dim3(kThreadsTc);
+  cfg.dynamicSmemBytes = smem_bytes;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess) {
+    (void)cudaGetLastError();
+    n = 0;
+  }
+  cache[dev][cluster] = n;
+  cache_smem[dev][cluster] = smem_bytes;
+  return n;
+}
 
 int split_kv_tc_smem_bytes(int num_blocks, int kv_fp8) {
   return 1024 + num_blocks * split_kv_tc_block_bytes(kv_fp8) + kMergeBytes + kMlBytes +

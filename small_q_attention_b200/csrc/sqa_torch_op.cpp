@@ -94,7 +94,7 @@ void check_inputs(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
 sqa_args fill_args(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& bt,
                    const at::Tensor& sl, const c10::optional<at::Tensor>& mask_lens, int64_t max_seq_len,
                    int64_t num_ctas, int64_t min_pages_per_cta, int64_t kernel, int64_t kv_layout, double sm_scale,
-                   double out_scale) {
+                   double out_scale, int64_t min_seq_len = 0, int64_t cluster = 0) {
   sqa_args a = {};
   const bool hnd = kv_layout == SQA_KV_HND;
   a.query = q.data_ptr();
@@ -121,6 +121,8 @@ sqa_args fill_args(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v
   a.out_scale = (float)out_scale;
   a.page_stride = cache_page_stride(k, v);
   a.kv_dtype = k.scalar_type() == at::kFloat8_e4m3fn ? SQA_KV_FP8_E4M3 : SQA_KV_SAME;
+  a.min_seq_len = (int32_t)min_seq_len;
+  a.cluster = (int32_t)cluster;
   return a;
 }
 
@@ -196,7 +198,7 @@ at::Tensor forward(const at::Tensor& query, const at::Tensor& key_cache, const a
                    const at::Tensor& block_tables, const at::Tensor& seq_lens, int64_t page_size, int64_t max_seq_len,
                    const c10::optional<at::Tensor>& out, const c10::optional<at::Tensor>& workspace, int64_t num_ctas,
                    int64_t min_pages_per_cta, int64_t kernel, bool check, int64_t kv_layout, double sm_scale,
-                   double out_scale) {
+                   double out_scale, int64_t min_seq_len, int64_t cluster) {
   check_inputs(query, key_cache, value_cache, block_tables, seq_lens, page_size, c10::nullopt, kv_layout);
   at::Tensor o;
   if (out.has_value()) {
@@ -208,7 +210,7 @@ at::Tensor forward(const at::Tensor& query, const at::Tensor& key_cache, const a
     o = at::empty_like(query);
   }
   sqa_args a = fill_args(query, key_cache, value_cache, block_tables, seq_lens, c10::nullopt, max_seq_len, num_ctas,
-                         min_pages_per_cta, kernel, kv_layout, sm_scale, out_scale);
+                         min_pages_per_cta, kernel, kv_layout, sm_scale, out_scale, min_seq_len, cluster);
   a.out = o.data_ptr();
   launch(a, query, workspace, check);
   return o;
@@ -219,7 +221,8 @@ std::tuple<at::Tensor, at::Tensor> forward_partial(
     const at::Tensor& block_tables, const at::Tensor& seq_lens, int64_t page_size,
     const c10::optional<at::Tensor>& mask_lens, int64_t max_seq_len, const c10::optional<at::Tensor>& out,
     const c10::optional<at::Tensor>& out_lse, const c10::optional<at::Tensor>& workspace, int64_t num_ctas,
-    int64_t min_pages_per_cta, int64_t kernel, bool check, int64_t kv_layout, double sm_scale, double out_scale) {
+    int64_t min_pages_per_cta, int64_t kernel, bool check, int64_t kv_layout, double sm_scale, double out_scale,
+    int64_t min_seq_len, int64_t cluster) {
   check_inputs(query, key_cache, value_cache, block_tables, seq_lens, page_size, mask_lens, kv_layout);
   const auto f32 = query.options().dtype(at::kFloat);
   at::Tensor o = out.has_value() ? *out : at::empty(query.sizes(), f32);
@@ -231,7 +234,7 @@ std::tuple<at::Tensor, at::Tensor> forward_partial(
                         l.device() == query.device(),
                     "out_lse must be a contiguous fp32 tensor [batch, q_len, Hq]");
   sqa_args a = fill_args(query, key_cache, value_cache, block_tables, seq_lens, mask_lens, max_seq_len, num_ctas,
-                         min_pages_per_cta, kernel, kv_layout, sm_scale, out_scale);
+                         min_pages_per_cta, kernel, kv_layout, sm_scale, out_scale, min_seq_len, cluster);
   a.out_partial = o.data_ptr<float>();
   a.out_lse = l.data_ptr<float>();
   launch(a, query, workspace, check);
@@ -243,7 +246,7 @@ at::Tensor op_forward(const at::Tensor& query, const at::Tensor& key_cache, cons
                       const at::Tensor& block_tables, const at::Tensor& seq_lens, int64_t page_size,
                       int64_t max_seq_len, int64_t kernel, int64_t kv_layout, double sm_scale, double out_scale) {
   return forward(query, key_cache, value_cache, block_tables, seq_lens, page_size, max_seq_len, c10::nullopt,
-                 c10::nullopt, 0, 0, kernel, false, kv_layout, sm_scale, out_scale);
+                 c10::nullopt, 0, 0, kernel, false, kv_layout, sm_scale, out_scale, 0, 0);
 }
 
 std::tuple<at::Tensor, at::Tensor> op_forward_partial(const at::Tensor& query, const at::Tensor& key_cache,
@@ -254,7 +257,7 @@ std::tuple<at::Tensor, at::Tensor> op_forward_partial(const at::Tensor& query, c
                                                       double sm_scale, double out_scale) {
   return forward_partial(query, key_cache, value_cache, block_tables, seq_lens, page_size, mask_lens, max_seq_len,
                          c10::nullopt, c10::nullopt, c10::nullopt, 0, 0, kernel, false, kv_layout, sm_scale,
-                         out_scale);
+                         out_scale, 0, 0);
 }
 
 at::Tensor meta_forward(const at::Tensor& query, const at::Tensor&, const at::Tensor&, const at::Tensor&,

@@ -42,7 +42,7 @@ def test_every_declared_symbol_is_exported(lib):
 
 
 def test_abi_version_and_status_strings(lib):
-    assert lib.sqa_abi_version() == 109
+    assert lib.sqa_abi_version() == 110
     for code in range(6):
         assert lib.sqa_status_string(code).decode()
     assert lib.sqa_status_string(99).decode() == "unknown status"
@@ -156,7 +156,7 @@ def test_torch_extension_registers_the_operators():
 
     build.build_torch_ext()  # no-op when up to date
     ext = _native.torch_ext()
-    assert ext.abi_version() == 109
+    assert ext.abi_version() == 110
     q = torch.empty(2, 4, 32, 128, dtype=torch.float16, device="meta")
     k = torch.empty(64, 16, 8, 128, dtype=torch.float16, device="meta")
     bt = torch.empty(2, 32, dtype=torch.int32, device="meta")
@@ -168,7 +168,7 @@ def test_torch_extension_registers_the_operators():
     cpu = [torch.zeros(2, 4, 32, 128, dtype=torch.float16), torch.zeros(64, 16, 8, 128, dtype=torch.float16)]
     with pytest.raises(ValueError, match="CUDA tensors"):
         ext.forward(cpu[0], cpu[1], cpu[1], torch.zeros(2, 32, dtype=torch.int32),
-                    torch.zeros(2, dtype=torch.int32), 16, 0, None, None, 0, 0, 0, False, 0, 0.0, 1.0)
+                    torch.zeros(2, dtype=torch.int32), 16, 0, None, None, 0, 0, 0, False, 0, 0.0, 1.0, 0, 0)
 
 
 def test_torch_extension_shares_the_process_cpp_runtime():
