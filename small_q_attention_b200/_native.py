@@ -126,7 +126,8 @@ class SqaArgs(ctypes.Structure):
 
 
 _lib = None
-_lock = threading.Lock()
+# Reentrant: torch_ext() holds it while it loads the C library through library().
+_lock = threading.RLock()
 
 
 def library(path: Path | None = None):

@@ -187,3 +187,18 @@ def test_torch_extension_shares_the_process_cpp_runtime():
     assert "libstdc++.so.6" in needed
     exported = subprocess.run(["nm", "-D", "--defined-only", str(path)], capture_output=True, text=True).stdout
     assert "__cxa_allocate_exception" not in exported and "__cxa_throw" not in exported
+
+
+def test_extension_loads_first_in_a_fresh_process():
+    """A process whose first call is the operator loads the torch extension before
+    the C library: that must not deadlock (a fresh interpreter, bounded)."""
+    import subprocess
+    import sys
+
+    code = ("import sys; sys.path.insert(0, %r)\n"
+            "from small_q_attention_b200 import _native\n"
+            "ext = _native.torch_ext()\n"
+            "assert ext.abi_version() == _native.library().sqa_abi_version()\n"
+            "print('ok')\n") % str(ROOT)
+    res = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=120)
+    assert res.returncode == 0 and res.stdout.strip().endswith("ok"), res.stderr[-2000:]
