@@ -9,9 +9,11 @@ weak scaling: global batch 4N, no collective on the hot path).
 Reported:
 * ``value``      effective HBM TB/s of the whole job = algorithmic bytes of all
                  ranks' calls / max-over-ranks device time of K steps, inputs
-                 resident in HBM, the K calls replayed from one CUDA graph, each
-                 step on the next of 4 input replicas (805 MB > the 126 MB L2,
-                 so K/V always come from HBM);
+                 resident in HBM, the K calls replayed from one CUDA graph whose
+                 first and last nodes are the timing events (the device time of
+                 the K steps, not the host's graph launch), each step on the next
+                 of 4 input replicas (805 MB > the 126 MB L2, so K/V always come
+                 from HBM);
 * ``e2e``        the same metric through the public Python API with the step's
                  query, page table and lengths copied from pinned host memory
                  and the output copied back every step (the KV cache is the
@@ -385,11 +387,20 @@ def measure_device(arm, args, device, with_clocks=True):
         for i in range(W):
             arm.call(i, sh)
     stream.synchronize()
+    # the timing events are nodes of the graph, first and last: the timed region is the K
+    # steps on the device, not the host's graph launch before them
+    start, end = torch.cuda.Event(enable_timing=True, external=True), torch.cuda.Event(enable_timing=True,
+                                                                                        external=True)
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
+        start.record()
         for i in range(K):
             arm.call(i, torch.cuda.current_stream().cuda_stream)
+        end.record()
     torch.cuda.synchronize()
+    clocks = ClockSampler(device.index) if with_clocks else None
+    if clocks:  # sampling from before the warm replays: the sampler's start-up stays out of the timed replay
+        clocks.__enter__()
     # warm replays (untimed) so that the timed replay starts at the clock of a busy GPU; the
     # count is the same on every rank (a replay holds cross-rank exchanges)
     t_warm = time.perf_counter()
@@ -405,18 +416,12 @@ def measure_device(arm, args, device, with_clocks=True):
         graph.replay()
     torch.cuda.synchronize()
 
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    clocks = ClockSampler(device.index) if with_clocks else None
-    if clocks:
-        clocks.__enter__()
     try:
         if dist is not None:
             dist.barrier()
         torch.cuda.synchronize()
-        start.record(stream)
         with torch.cuda.stream(stream):
             graph.replay()
-        end.record(stream)
         torch.cuda.synchronize()
         if dist is not None:
             dist.barrier()
@@ -671,7 +676,8 @@ def run_ours(args):
                     "d2h_bytes_per_step": e2e["d2h"], "us_per_step": round(e2e["e2e_ms"] / K * 1e3, 3),
                     "mode": args.e2e_mode,
                     "api": "small_q_attention_b200.small_q_attention (torch extension over the C ABI)"},
-            "clocks": res["clocks"],
+            "clocks": dict(res["clocks"], window="NVML every 2 ms from the warm replays through the timed replay")
+            if res["clocks"] else None,
             "gpu_launches": launches,
         }
         if sharded:
@@ -879,9 +885,13 @@ def matrix_rows(args, settle: float = 1.0, replica_mb: float = 400.0, verbose: b
         s = torch.cuda.Stream()
         g = torch.cuda.CUDAGraph()
         reps = max(20, n_rep)  # every replica once per replay
-        with torch.cuda.graph(g, stream=s):
+        e0, e1 = torch.cuda.Event(enable_timing=True, external=True), torch.cuda.Event(enable_timing=True,
+                                                                                      external=True)
+        with torch.cuda.graph(g, stream=s):  # the timing events are the graph's first and last nodes
+            e0.record()
             for i in range(reps):
                 fn(i % len(inst))
+            e1.record()
         g.replay()
         torch.cuda.synchronize()
         # A burst of heavy cases leaves the SM clock low for up to ~2 s afterwards
@@ -893,10 +903,7 @@ def matrix_rows(args, settle: float = 1.0, replica_mb: float = 400.0, verbose: b
         samples = []
         with ClockSampler(torch.cuda.current_device()) as clocks:
             for _ in range(5):
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record()
                 g.replay()
-                e1.record()
                 torch.cuda.synchronize()
                 samples.append(e0.elapsed_time(e1) * 1e3 / reps)
             # the upstream's per-call protocol on replica 0
@@ -904,13 +911,13 @@ def matrix_rows(args, settle: float = 1.0, replica_mb: float = 400.0, verbose: b
                 fn(0)
             torch.cuda.synchronize()
             eager = []
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             for _ in range(15):
-                e0.record()
+                f0.record()
                 fn(0)
-                e1.record()
-                e1.synchronize()
-                eager.append(e0.elapsed_time(e1) * 1e3)
+                f1.record()
+                f1.synchronize()
+                eager.append(f0.elapsed_time(f1) * 1e3)
         us = statistics.median(samples)
         eager_us = statistics.median(eager)
         bits = sqa.read_device_status(ws.data_ptr(), clear=True)
@@ -927,7 +934,8 @@ def matrix_rows(args, settle: float = 1.0, replica_mb: float = 400.0, verbose: b
                "peak_gbs": peak_gbs, "peak_source": peak_src, "replicas": n_rep, "sm_mhz": cs["sm_mhz"],
                "clock_reasons": cs["reasons"], "dtype": args.dtype}
         if verbose:
-            row["timing"] = (f"p50: CUDA graph of {reps} back-to-back calls over rotating replicas, median of 5; "
+            row["timing"] = (f"p50: CUDA graph of {reps} back-to-back calls over rotating replicas, timed by "
+                             "events that are the graph's first and last nodes, median of 5 replays; "
                              "eager: upstream per-call protocol, median of 15")
             print(json.dumps(row), flush=True)
         rows.append(row)

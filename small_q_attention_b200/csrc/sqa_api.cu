@@ -265,16 +265,21 @@ int make_plan(const sqa_args* a, int device, Plan* plan) {
   const int grid_default = pl.grid;
   if (pl.tc && a->num_ctas == 0 && a->cluster != 1) {
     // Cluster mode: every (sequence, KV head) segment split evenly over C CTAs of one
-    // thread-block cluster, parts reduced through distributed shared memory.  Auto
-    // only for near-uniform lengths (both hints within 15%), two or more CTAs per
-    // segment on the SMs and at least 16 pages per CTA; every cluster resident at once.
+    // thread-block cluster, parts reduced through distributed shared memory.  Measured
+    // on B200: it removes the merge launch but runs on segments x C <= SMs CTAs, and
+    // one CTA streams at most ~55 GB/s, so long segments need all the SMs of the
+    // cost-balanced schedule (cfg2: 27.0 us in 4-CTA clusters against 26.4 us); it wins
+    // on short near-uniform segments (q4 x 1K x 4: 11.4 against 13.2 us).  Auto: both
+    // length hints within 15%, q_len <= 8, 16..32 pages per CTA, clusters of 4 or 2,
+    // every cluster resident at once.
     const long long segs = pl.segments;
     if (a->cluster >= 2) {
       pl.cluster = a->cluster;
-    } else if (a->max_seq_len > 0 && a->min_seq_len > 0 && 100LL * a->min_seq_len >= 85LL * a->max_seq_len) {
-      const int cands[4] = {16, 8, 4, 2};
+    } else if (a->max_seq_len > 0 && a->min_seq_len > 0 && 100LL * a->min_seq_len >= 85LL * a->max_seq_len &&
+               a->q_len <= 8) {
+      const int cands[2] = {4, 2};
       for (int c : cands) {
-        if (segs * c <= sms && pages_upper / c >= 16) {
+        if (segs * c <= sms && pages_upper / c >= 16 && pages_upper / c <= 32) {
           pl.cluster = c;
           break;
         }
