@@ -112,9 +112,12 @@ __global__ void __launch_bounds__(256) sqa_lc_send_kernel(const LcSendParams p) 
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < p.rows; i += stride)
       p.slot_lse[i] = __ldg(p.lse + i);
   }
-  __threadfence_system();  // this thread's peer stores, before the arrival below
+  // The CTA's peer stores precede the barrier; one system-scope fence by thread 0
+  // after it orders all of them before the arrival (and, through the last CTA's
+  // fence, before the flag).  A fence in every thread cost ~16 us per launch.
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence_system();
     const bool last = atomicAdd(arrive, 1u) == gridDim.x - 1;
     if (last) {
       __threadfence_system();
@@ -140,9 +143,9 @@ __global__ void __launch_bounds__(256) sqa_lc_merge_kernel(const LcMergeParams p
   if (row < p.rows)  // the slots were written by other GPUs: read through L2
     merge_row<true>(p.slots_o + row * kHeadDim, (size_t)p.rows * kHeadDim, p.slots_lse + row, (size_t)p.rows,
                     p.world, p.out + row * kHeadDim, nullptr, nullptr, p.bf16 != 0);
-  __threadfence_system();  // every read of the slots is done before the acks below
-  __syncthreads();
+  __syncthreads();  // every read of the slots in this CTA is done before the acks below
   if (threadIdx.x == 0) {
+    __threadfence_system();
     const bool last = atomicAdd(arrive, 1u) == gridDim.x - 1;
     if (last) {
       __threadfence_system();
