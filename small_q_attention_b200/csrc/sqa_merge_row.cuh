@@ -16,15 +16,15 @@ constexpr float kMergeLog2e = 1.4426950408889634f;
 // Merge `cnt` parts of one row; part i's row is at o + i * o_stride and
 // lse + i * lse_stride.  Writes to whichever of out (fp16, or bf16 with
 // out_bf16) / out_o / out_lse is set.
-// Parts are taken 8 at a time with all loads of a batch issued before use: one
-// memory round trip per 8 parts.
+// Parts are taken kBatch at a time with all loads of a batch issued before use: one
+// memory round trip per batch (8 for the usual few parts; 24 when a row has more, as
+// when one sequence is split over every CTA of the GPU).
 // kCoherent reads through L2 (ld.global.cg): required when the parts were
 // written by other CTAs of the same kernel; otherwise the read-only path.
-template <bool kCoherent>
-__device__ __forceinline__ void merge_row(const float* o, size_t o_stride, const float* lse,
-                                          size_t lse_stride, int cnt, __half* out, float* out_o,
-                                          float* out_lse, bool out_bf16 = false) {
-  constexpr int kBatch = 8;
+template <bool kCoherent, int kBatch = 8>
+__device__ __forceinline__ void merge_row_batched(const float* o, size_t o_stride, const float* lse,
+                                                  size_t lse_stride, int cnt, __half* out, float* out_o,
+                                                  float* out_lse, bool out_bf16) {
   const int lane = threadIdx.x & 31;
   auto load_f = [](const float* ptr) { return kCoherent ? __ldcg(ptr) : __ldg(ptr); };
   auto load_f4 = [](const float4* ptr) { return kCoherent ? __ldcg(ptr) : __ldg(ptr); };
@@ -79,6 +79,16 @@ __device__ __forceinline__ void merge_row(const float* o, size_t o_stride, const
   }
   if (out_o != nullptr) reinterpret_cast<float4*>(out_o)[lane] = acc;
   if (out_lse != nullptr && lane == 0) *out_lse = (total > 0.f) ? base + __logf(total) : -INFINITY;
+}
+
+template <bool kCoherent>
+__device__ __forceinline__ void merge_row(const float* o, size_t o_stride, const float* lse,
+                                          size_t lse_stride, int cnt, __half* out, float* out_o,
+                                          float* out_lse, bool out_bf16 = false) {
+  if (cnt <= 8)
+    merge_row_batched<kCoherent, 8>(o, o_stride, lse, lse_stride, cnt, out, out_o, out_lse, out_bf16);
+  else
+    merge_row_batched<kCoherent, 24>(o, o_stride, lse, lse_stride, cnt, out, out_o, out_lse, out_bf16);
 }
 
 }  // namespace sqa
