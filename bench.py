@@ -612,12 +612,22 @@ def run_ours(args):
         for sub in ("cfg3", "cfg4", "cfg5"):
             if sub == name:
                 continue
-            sarm = DeviceArm(sub, args, world, rank, device, dist, lib)
-            sres = measure_device(sarm, args, device, with_clocks=False)
-            sharded[sub] = _sharded_line(sarm, sres, args, peak_gbs)
-            sarm.close()
-            del sarm
-            torch.cuda.empty_cache()
+            sarm = None
+            try:  # a failed sub-measurement is reported in its entry; the line above stands
+                sarm = DeviceArm(sub, args, world, rank, device, dist, lib)
+                sres = measure_device(sarm, args, device, with_clocks=False)
+                sharded[sub] = _sharded_line(sarm, sres, args, peak_gbs)
+            except Exception as e:  # noqa: BLE001
+                print(f"bench: {sub} failed: {e}", file=sys.stderr)
+                sharded[sub] = {"workload": WORKLOADS[sub], "error": f"{type(e).__name__}: {e}"[:300]}
+            finally:
+                if sarm is not None:
+                    try:
+                        sarm.close()
+                    except Exception as e:  # noqa: BLE001
+                        print(f"bench: {sub} close failed: {e}", file=sys.stderr)
+                del sarm
+                torch.cuda.empty_cache()
 
     # --- the 36-case matrix and the named configs (N=1 only: it would hold every GPU)
     matrix = None
