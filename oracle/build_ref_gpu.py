@@ -12,7 +12,8 @@ beside the CPU reference.
 
     python oracle/build_ref_gpu.py --reference <upstream checkout>
 
-or ``SQA_REFERENCE_ROOT=<upstream checkout> python oracle/build_ref_gpu.py``.
+or ``SQA_REFERENCE_ROOT=<upstream checkout> python oracle/build_ref_gpu.py`` (default:
+a ``reference`` checkout beside this repository).
 The build needs only nvcc and torch's headers (no GPU); without the upstream
 tree it does nothing.
 """
@@ -28,7 +29,7 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 OUT_DIR = HERE / "_ref"
 NAME = "small_q_attention_ext_ref"
-DEFAULT_REFERENCE = "/root/reference"
+DEFAULT_REFERENCE = HERE.parent.parent / "reference"  # an upstream checkout beside this repository
 
 
 def reference_root(path: str | None = None) -> Path:
