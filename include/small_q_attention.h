@@ -175,9 +175,13 @@ SQA_API int sqa_forward(const sqa_args* args, void* workspace, size_t workspace_
 /* sqa_forward that also records the caller's CUDA events (cudaEvent_t, may be
  * NULL) on `stream` immediately before and after the split-KV kernel launch,
  * so the dominant kernel can be timed with events on its own stream.  Under
- * stream capture the records become event-record nodes of the graph
- * (cudaEventRecordExternal), timing the kernel inside each replay.  Does the
- * same work as sqa_forward.  No upstream counterpart (measurement hook). */
+ * stream capture the records become event-record nodes on side branches of the
+ * graph: each depends on the work captured before it, and nothing captured later
+ * depends on it, so consecutive launches keep their programmatic (early-launch)
+ * overlap; event_before then fires when the previous call's last kernel ends and
+ * event_after when the split-KV kernel ends (its duration inside a replay of
+ * back-to-back calls).  Does the same work as sqa_forward.  No upstream
+ * counterpart (measurement hook). */
 SQA_API int sqa_forward_timed(const sqa_args* args, void* workspace, size_t workspace_bytes, void* stream,
                               void* event_before, void* event_after);
 

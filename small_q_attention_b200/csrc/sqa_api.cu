@@ -386,6 +386,25 @@ int sqa_workspace_init(void* workspace, size_t workspace_bytes, void* stream) {
 }
 
 namespace {
+// Under stream capture: an event-record node that depends on the stream's current
+// capture dependencies without joining them, so the next captured kernel keeps its
+// programmatic (early-launch) edge to the previous one.  The event then fires when
+// the work captured so far has completed: before a split-KV launch, when the previous
+// call's merge ends (the moment the split kernel's dependency wait returns); after
+// it, when the split kernel ends.  The graph keeps such unjoined nodes.
+cudaError_t record_side_branch(cudaEvent_t ev, cudaStream_t stream) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  cudaGraph_t graph = nullptr;
+  const cudaGraphNode_t* deps = nullptr;
+  const cudaGraphEdgeData* edges = nullptr;
+  size_t n = 0;
+  cudaError_t e = cudaStreamGetCaptureInfo_v3(stream, &cs, nullptr, &graph, &deps, &edges, &n);
+  if (e != cudaSuccess) return e;
+  if (cs != cudaStreamCaptureStatusActive || graph == nullptr) return cudaErrorStreamCaptureInvalidated;
+  cudaGraphNode_t node = nullptr;
+  return cudaGraphAddEventRecordNode(&node, graph, deps, n, ev);
+}
+
 int forward_impl(const sqa_args* a, void* workspace, size_t workspace_bytes, void* stream_ptr,
                  void* ev_before, void* ev_after) {
   int st = validate(a);
@@ -440,22 +459,26 @@ int forward_impl(const sqa_args* a, void* workspace, size_t workspace_bytes, voi
   p.cluster = pl.cluster;
 
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_ptr);
-  // Timing events: under stream capture they become event-record nodes of the
-  // graph (cudaEventRecordExternal), so the kernel is timed inside a replay.
-  unsigned int ev_flags = cudaEventRecordDefault;
+  // Timing events.  Eagerly: records on the stream before and after the split-KV
+  // launch.  Under stream capture: event-record nodes on side branches of the graph
+  // (record_side_branch), so the launches keep their programmatic edges.
+  bool capturing = false;
   if (ev_before || ev_after) {
     cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
     if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess) return SQA_ERR_CUDA;
-    if (cs == cudaStreamCaptureStatusActive) ev_flags = cudaEventRecordExternal;
+    capturing = cs == cudaStreamCaptureStatusActive;
   }
-  if (ev_before && cudaEventRecordWithFlags(reinterpret_cast<cudaEvent_t>(ev_before), stream, ev_flags) != cudaSuccess)
-    return SQA_ERR_CUDA;
+  auto record = [&](void* ev) {
+    if (!ev) return true;
+    const cudaEvent_t e = reinterpret_cast<cudaEvent_t>(ev);
+    return (capturing ? record_side_branch(e, stream) : cudaEventRecord(e, stream)) == cudaSuccess;
+  };
+  if (!record(ev_before)) return SQA_ERR_CUDA;
   const cudaError_t launched = pl.tc ? launch_split_kv_tc(p, tm_k, tm_v, pl.grid, pl.smem, stream)
                                     : launch_split_kv(p, tm_k, tm_v, pl.grid, pl.smem, stream);
   if (launched != cudaSuccess) return SQA_ERR_CUDA;
   if (!debug_sync(stream, "split-KV kernel", pl.grid, pl.smem, a)) return SQA_ERR_CUDA;
-  if (ev_after && cudaEventRecordWithFlags(reinterpret_cast<cudaEvent_t>(ev_after), stream, ev_flags) != cudaSuccess)
-    return SQA_ERR_CUDA;
+  if (!record(ev_after)) return SQA_ERR_CUDA;
 
   MergeParams m;
   m.parts_o = p.ws_o;
