@@ -71,10 +71,18 @@ def _peaks():
 
 
 class _KernelNames(dict):
-    """Kernel id (sqa_selected_kernel) -> name; 2 + 100 * C is the tcgen05 kernel in clusters of C."""
+    """Kernel id (sqa_selected_kernel) -> name; 2 + 100 * C is the tcgen05 kernel in clusters of C,
+    2 + 10000 * k the tcgen05 kernel with every segment split evenly over k CTAs."""
 
     def __missing__(self, k):
+        if k >= 10000:
+            return f"sqa_split_kv_tc_kernel (segments split over {(k - 2) // 10000} CTAs each)"
         return f"sqa_split_kv_tc_kernel (clusters of {(k - 2) // 100})" if k > 100 else f"kernel {k}"
+
+
+def _cluster_mode(kernel_id: int) -> bool:
+    """The launch reduces every segment inside its clusters: no merge kernel."""
+    return kernel_id > 100 and (kernel_id // 100) % 100 > 0
 
 
 KERNEL_NAMES = _KernelNames({1: "sqa_split_kv_kernel", 2: "sqa_split_kv_tc_kernel"})
@@ -346,7 +354,7 @@ class DeviceArm:
             _native.check(-self.kernel_id, "sqa_selected_kernel")
         # our kernels per step on rank 0: split-KV + per-call merge (none in cluster mode), in
         # long-context mode also the cross-rank merge (one GPU) or the exchange's send + merge
-        self.launches_per_step = (1 if self.kernel_id > 100 else 2) + (
+        self.launches_per_step = (1 if _cluster_mode(self.kernel_id) else 2) + (
             (2 if self.lc is not None else 1) if self.longctx else 0)
 
     def close(self):
@@ -1060,7 +1068,8 @@ def main():
     ap.add_argument("--ref-gpu-matrix", type=str, default=None,
                     help="--impl reference: also time the upstream GPU kernel on every matrix case, JSONL here")
     ap.add_argument("--no-length-hints", action="store_true",
-                    help="do not pass min_seq_len (no cluster mode): the cost-balanced schedule for every call")
+                    help="do not pass min_seq_len (no cluster mode or segment-aligned split): the cost-balanced "
+                         "schedule for every call")
     ap.add_argument("--kernel-case", type=str, default=None,
                     help="run one kernel a few times on a small case (append, merge, exchange, cfg2, q4_kv8192_b4, "
                          "...) for an ncu capture")

@@ -141,8 +141,10 @@ typedef struct sqa_args {
    * launch: with both bounds within 15% of each other (near-uniform lengths)
    * and few enough (sequence, KV head) segments for two or more CTAs each, the
    * tcgen05 kernel splits every segment evenly over a thread-block cluster and
-   * reduces the parts through distributed shared memory (no merge launch).  A
-   * wrong hint still gives the right result, only a slower launch. */
+   * reduces the parts through distributed shared memory (no merge launch) on
+   * short segments, or evenly over k CTAs without a cluster (merged by the merge
+   * kernel; no CTA crosses a segment boundary) on long ones.  A wrong hint still
+   * gives the right result, only a slower launch. */
   int32_t min_seq_len;
   /* Cluster mode: 0 = auto (above), 1 = off (segments cut into cost-balanced
    * CTA ranges, merged by a second kernel), 2 / 4 / 8 / 16 = that many CTAs per
@@ -202,7 +204,8 @@ SQA_API int sqa_read_device_status(void* workspace, uint32_t* device_bits, int c
 
 /* The kernel sqa_forward would launch for these arguments on `device` (-1 =
  * the current device): 1 = warp-level mma.sync kernel, 2 = tcgen05 kernel,
- * 2 + 100 * C = tcgen05 kernel in clusters of C CTAs per segment;
+ * 2 + 100 * C = tcgen05 kernel in clusters of C CTAs per segment,
+ * 2 + 10000 * k = tcgen05 kernel with every segment split evenly over k CTAs;
  * minus the SQA_ERR_* code on invalid arguments.  Resolves kernel = 0 (auto).
  * No upstream counterpart (introspection for measurement and tests). */
 SQA_API int sqa_selected_kernel(const sqa_args* args, int device);

@@ -170,6 +170,7 @@ struct Plan {
   int smem;
   int kv_fp8 = 0;  // fp8 caches: 2 = 4-page blocks, 3 = 8-page blocks
   int cluster = 0;  // tcgen05 cluster mode: CTAs per segment (0 = cost-balanced ranges + merge kernel)
+  int seg_split = 0;  // tcgen05 segment-aligned split: CTAs per segment (partials merged by the merge kernel)
   int segments;
   int pieces;
   size_t off_lse, off_o, off_timeline = 0, bytes;
@@ -287,6 +288,22 @@ int make_plan(const sqa_args* a, int device, Plan* plan) {
     }
     if (pl.cluster) pl.grid = (int)(segs * pl.cluster);
   }
+  // Segment-aligned split: with near-uniform length hints and fewer segments than
+  // CTAs, every segment split evenly over k = grid / segments CTAs, so that no CTA
+  // crosses a segment boundary.  In the cost-balanced schedule a CTA that does (a
+  // batch-1 call has 8 segments over 148 CTAs) ends ~2 us after the others: a second
+  // piece epilogue and pipeline refill on the same page count.  Only where the split
+  // keeps >= 90% of the CTAs busy and gives each >= 16 pages; a wrong hint costs
+  // time, not correctness.
+  if (pl.tc && a->num_ctas == 0 && !pl.cluster && a->max_seq_len > 0 && a->min_seq_len > 0 &&
+      100LL * a->min_seq_len >= 85LL * a->max_seq_len) {
+    const long long segs = pl.segments;
+    const long long k = segs > 0 ? grid_default / segs : 0;
+    if (k >= 2 && 10 * segs * k >= 9LL * grid_default && pages_upper >= 16 * k) {
+      pl.seg_split = (int)k;
+      pl.grid = (int)(segs * k);
+    }
+  }
   if (pl.tc) {
     // a ring of blocks in up to 227 KB of shared memory: 32 KB (16-bit caches, 4
     // pages), fp8 caches 16 KB (4 pages) or, for long per-CTA ranges, 32 KB (8 pages)
@@ -306,7 +323,7 @@ int make_plan(const sqa_args* a, int device, Plan* plan) {
       } else if (a->cluster == 0 && fit < pl.segments) {
         pl.cluster = 0;
       }
-      if (!pl.cluster) pl.grid = grid_default;
+      if (!pl.cluster && !pl.seg_split) pl.grid = grid_default;
     }
   } else {
     const int fixed = split_kv_smem_bytes(pl.shape, 0);
@@ -375,7 +392,7 @@ int sqa_selected_kernel(const sqa_args* args, int device) {
   Plan pl;
   st = make_plan(args, dev, &pl);
   if (st != SQA_OK) return -st;
-  return pl.tc ? 2 + 100 * pl.cluster : 1;
+  return pl.tc ? 2 + 100 * pl.cluster + 10000 * pl.seg_split : 1;
 }
 
 int sqa_workspace_init(void* workspace, size_t workspace_bytes, void* stream) {
@@ -429,7 +446,7 @@ int forward_impl(const sqa_args* a, void* workspace, size_t workspace_bytes, voi
     return SQA_ERR_CUDA;
 
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  SplitKvParams p;
+  SplitKvParams p = {};
   p.q = static_cast<const __half*>(a->query);
   p.block_tables = a->block_tables;
   p.seq_lens = a->seq_lens;
@@ -457,6 +474,7 @@ int forward_impl(const sqa_args* a, void* workspace, size_t workspace_bytes, voi
   p.kv_fp8 = pl.kv_fp8;
   p.seg_cost = pl.tc ? kSegmentCostTc : kSegmentCostMma;
   p.cluster = pl.cluster;
+  p.seg_split = pl.seg_split;
 
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_ptr);
   // Timing events.  Eagerly: records on the stream before and after the split-KV
@@ -480,7 +498,7 @@ int forward_impl(const sqa_args* a, void* workspace, size_t workspace_bytes, voi
   if (!debug_sync(stream, "split-KV kernel", pl.grid, pl.smem, a)) return SQA_ERR_CUDA;
   if (!record(ev_after)) return SQA_ERR_CUDA;
 
-  MergeParams m;
+  MergeParams m = {};
   m.parts_o = p.ws_o;
   m.parts_lse = p.ws_lse;
   m.seq_lens = a->seq_lens;
@@ -500,6 +518,7 @@ int forward_impl(const sqa_args* a, void* workspace, size_t workspace_bytes, voi
   m.bf16 = p.bf16;
   m.split_grid = pl.grid;
   m.seg_cost = p.seg_cost;
+  m.seg_split = pl.seg_split;
   if (pl.cluster) return SQA_OK;  // the clusters reduced every segment themselves
   if (launch_segment_merge(m, pl.shape.rows_pad, stream) != cudaSuccess) return SQA_ERR_CUDA;
   if (!debug_sync(stream, "merge kernel", pl.segments, 0, a)) return SQA_ERR_CUDA;

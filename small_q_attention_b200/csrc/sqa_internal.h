@@ -60,6 +60,8 @@ struct SplitKvParams {
   int seg_cost;                 // schedule: units a segment start costs a CTA (one more epilogue)
   int cluster;                  // tcgen05 kernel: 0, or C >= 2 = segment blockIdx.x / C split evenly over
                                 // a thread-block cluster of C CTAs, partials reduced through DSMEM
+  int seg_split;                // tcgen05 kernel: 0, or k >= 2 = segment blockIdx.x / k split evenly over
+                                // k CTAs (no cluster), partials merged by the merge kernel
 };
 
 struct MergeParams {
@@ -77,6 +79,8 @@ struct MergeParams {
   int batch, q_len, hq, hkv, max_pages;
   int bf16;                     // out holds bf16 (else fp16)
   int split_grid, seg_cost;     // per-call merge: the split-KV launch's schedule (pieces of a segment)
+  int seg_split;                // per-call merge: k >= 2 when the split-KV launch split every segment
+                                // evenly over k CTAs (SplitKvParams::seg_split)
 };
 
 // Launchers (stream-ordered, no allocation).  Return cudaGetLastError().

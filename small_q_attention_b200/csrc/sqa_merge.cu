@@ -31,7 +31,9 @@ __global__ void __launch_bounds__(128) sqa_segment_merge_kernel(const MergeParam
   const int s = blockIdx.x;
   const int b = s / p.hkv;
   const int h = s - b * p.hkv;
-  const int2 info = segment_pieces(p.seq_lens, p.batch, p.max_pages, p.hkv, p.seg_cost, p.split_grid, b, h);
+  const int2 info = p.seg_split
+                        ? aligned_segment_pieces(p.seq_lens, p.max_pages, p.hkv, p.seg_split, b, h)
+                        : segment_pieces(p.seq_lens, p.batch, p.max_pages, p.hkv, p.seg_cost, p.split_grid, b, h);
   grid_dependency_wait();    // the split-KV grid has finished writing the partials
   if (threadIdx.x == 0) SQA_STAMP(tl, 1);
   const int rows = kGroup * p.q_len;

@@ -199,14 +199,26 @@ __device__ __forceinline__ Schedule compute_schedule(const SplitKvParams& p) {
   return s;
 }
 
-// Cluster mode (p.cluster = C >= 2, tcgen05 kernel): CTA blockIdx.x works on segment
-// s = blockIdx.x / C, the (blockIdx.x % C)-th of C equal page ranges (whole 4-page
-// blocks; a range may be empty).  Whole warp; every lane gets the result.  Lengths
-// are read once; block 0 raises the same status bits as compute_schedule.
+// Pages per CTA when a segment of `pages` pages is split evenly over `parts` CTAs:
+// in whole 4-page blocks in cluster mode, to the page in the segment-aligned split.
+// CTA j of the segment takes [min(pages, j * per), min(pages, (j + 1) * per)), so
+// the CTAs with pages are j < ceil(pages / per).
+__device__ __forceinline__ int even_split_pages(int pages, int parts, bool whole_blocks) {
+  const int per = (pages + parts - 1) / parts;
+  return whole_blocks ? (per + 3) / 4 * 4 : per;
+}
+
+// Even split of every segment over C CTAs (tcgen05 kernel): cluster mode
+// (p.cluster = C >= 2, whole 4-page blocks) or the segment-aligned split
+// (p.seg_split = C >= 2, to the page).  CTA blockIdx.x works on segment
+// s = blockIdx.x / C, the (blockIdx.x % C)-th of C page ranges (a range may be
+// empty), so no CTA crosses a segment boundary.  Whole warp; every lane gets the
+// result.  Lengths are read once; block 0 raises the same status bits as
+// compute_schedule.
 template <bool kSpec>
 __device__ __forceinline__ Schedule cluster_schedule(const SplitKvParams& p) {
   const int lane = threadIdx.x & 31;
-  const int C = p.cluster;
+  const int C = p.cluster > 1 ? p.cluster : p.seg_split;
   const int seg = (int)blockIdx.x / C;
   const int k = (int)blockIdx.x - seg * C;
   const int b = seg / p.hkv;
@@ -232,7 +244,7 @@ __device__ __forceinline__ Schedule cluster_schedule(const SplitKvParams& p) {
     flags = __reduce_or_sync(0xffffffffu, flags);
     if (blockIdx.x == 0 && lane == 0 && flags) atomicOr(p.status, flags);
   }
-  const int per = ((pages_b + C - 1) / C + 3) / 4 * 4;  // pages per CTA, whole 4-page blocks
+  const int per = even_split_pages(pages_b, C, p.cluster > 1);
   const int lo = min(pages_b, k * per);
   const int hi = min(pages_b, lo + per);
   Schedule sch;
@@ -249,7 +261,7 @@ __device__ __forceinline__ Schedule cluster_schedule(const SplitKvParams& p) {
 
 // Warp 0: the schedule into shared memory, before the CTA-wide barrier.
 __device__ __forceinline__ void build_schedule(const SplitKvParams& p, Schedule* sch) {
-  const Schedule s = p.cluster ? cluster_schedule<false>(p) : compute_schedule<false>(p);
+  const Schedule s = (p.cluster || p.seg_split) ? cluster_schedule<false>(p) : compute_schedule<false>(p);
   if ((threadIdx.x & 31) == 0) *sch = s;
 }
 
@@ -317,6 +329,19 @@ __device__ __forceinline__ int2 segment_pieces(const int32_t* seq_lens, int batc
   return make_int2(first_cta + b * hkv + h, last_cta - first_cta + 1);
 }
 
+// The pieces of segment s = b * Hkv + h under the segment-aligned split of k CTAs per
+// segment: CTA s * k + j writes piece slot (CTA + segment) = s * (k + 1) + j, and the
+// CTAs with pages are j < ceil(pages / per) (even_split_pages).  Whole warp (every
+// lane reads the one length).
+__device__ __forceinline__ int2 aligned_segment_pieces(const int32_t* seq_lens, int max_pages, int hkv, int k,
+                                                       int b, int h) {
+  const int len = max(__ldcg(seq_lens + b), 0);
+  const int pages = min((len + kPageSize - 1) / kPageSize, max_pages);
+  if (pages == 0) return make_int2(0, 0);
+  const int per = even_split_pages(pages, k, false);
+  return make_int2((b * hkv + h) * (k + 1), (pages + per - 1) / per);
+}
+
 // Producer warp, before the dependency wait: L2 prefetches of the first
 // `budget` pages (at most 32 per segment, two segments at most) and the first
 // Q rows this CTA will load, from a schedule and page ids read through L2
@@ -328,7 +353,7 @@ template <bool F8>
 __device__ __forceinline__ void prefetch_start(const SplitKvParams& p, const CUtensorMap* tm_k,
                                                const CUtensorMap* tm_v, int budget) {
   const int lane = threadIdx.x & 31;
-  const Schedule s = p.cluster ? cluster_schedule<true>(p) : compute_schedule<true>(p);
+  const Schedule s = (p.cluster || p.seg_split) ? cluster_schedule<true>(p) : compute_schedule<true>(p);
   if (s.start >= s.end) return;
   int b = s.b0;
   int pages = s.pages_b0;

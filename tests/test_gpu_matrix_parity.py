@@ -50,7 +50,9 @@ def _cases():
 
 
 CASES = _cases()
-PARAMS = [(name, k) for name in CASES for k in ((0, 2) if name.endswith("fp8") else (0, 1, 2))]
+# kernel "h": the automatic choice given both length hints (min and max of seq_lens), as the
+# benchmark passes them: cluster mode or the segment-aligned split where they apply
+PARAMS = [(name, k) for name in CASES for k in ((0, 2, "h") if name.endswith("fp8") else (0, 1, 2, "h"))]
 
 
 def _make(name):
@@ -123,8 +125,9 @@ def case_and_ref(name):
 @pytest.mark.parametrize("name,kernel", PARAMS, ids=[f"{n}-k{k}" for n, k in PARAMS])
 def test_matrix_case_vs_oracle(sqa, name, kernel):
     c, idx, ref = case_and_ref(name)
+    hints = dict(kernel=0, min_seq_len=min(c["lens"])) if kernel == "h" else dict(kernel=kernel)
     out = sqa.small_q_attention(c["query"], c["key_cache"], c["value_cache"], c["block_tables"], c["seq_lens"], 16,
-                                max(c["lens"]), kernel=kernel, check=True)
+                                max(c["lens"]), check=True, **hints)
     assert out.dtype == torch.float16
     assert_close(out[idx], ref)
 
