@@ -140,7 +140,10 @@ SHARDED = [(cfg, w) for cfg in ("cfg3", "cfg4", "cfg5") for w in (2, 4, 8)]
 def test_sharded_config_vs_oracle(sqa, cfg, world):
     """What every rank of ``bench.py --gpus N --workload cfgX`` computes, run rank by
     rank on this GPU, then combined the way the ranks combine it (cfg3 / cfg4: each
-    rank's output is its slice of the whole; cfg5: the (O, LSE) partials are merged)."""
+    rank's output is its slice of the whole; cfg5: the (O, LSE) partials are merged).
+    Each rank passes the bounds of its own lengths, as the bench does, so the launch
+    shapes are the bench's (the segment-aligned split for cfg5's shards and for cfg3 at
+    8 ranks)."""
     from small_q_attention_b200.sharding import kv_head_range, lpt_batch_shards, page_split, shard_lengths
 
     c, idx, ref = case_and_ref(cfg)
@@ -151,14 +154,15 @@ def test_sharded_config_vs_oracle(sqa, cfg, world):
             lo, hi = kv_head_range(8, world, r)
             out[:, :, 4 * lo:4 * hi] = sqa.small_q_attention(
                 q[:, :, 4 * lo:4 * hi].contiguous(), kc[:, :, lo:hi].contiguous(), vc[:, :, lo:hi].contiguous(),
-                bt, sl, 16, check=True)
+                bt, sl, 16, max(c["lens"]), min_seq_len=min(c["lens"]), check=True)
         assert_close(out[idx], ref)
     elif cfg == "cfg4":  # rank r owns the sequences LPT gives it (same pool)
         out = torch.empty_like(q)
         for mine in lpt_batch_shards(c["lens"], world):
             sel = torch.tensor(mine, dtype=torch.long, device="cuda")
+            my_lens = [c["lens"][i] for i in mine]
             out[sel] = sqa.small_q_attention(q[sel].contiguous(), kc, vc, bt[sel].contiguous(), sl[sel].contiguous(),
-                                             16, check=True)
+                                             16, max(my_lens), min_seq_len=min(my_lens), check=True)
         assert_close(out[idx], ref)
     else:  # cfg5: rank r holds pages [lo, hi) of the one sequence; partials merged
         total = c["lens"][0]
@@ -168,7 +172,8 @@ def test_sharded_config_vs_oracle(sqa, cfg, world):
             held, mlen = shard_lengths(total, lo, hi)
             o, lse = sqa.small_q_attention_partial(
                 q, kc, vc, bt[:, lo:hi].contiguous(), torch.tensor([held], dtype=torch.int32, device="cuda"), 16,
-                mask_lens=torch.tensor([mlen], dtype=torch.int32, device="cuda"), check=True)
+                mask_lens=torch.tensor([mlen], dtype=torch.int32, device="cuda"), max_seq_len=held, min_seq_len=held,
+                check=True)
             parts_o.append(o)
             parts_lse.append(lse)
         merged = sqa.merge_partials(torch.stack(parts_o), torch.stack(parts_lse))
