@@ -1029,9 +1029,10 @@ def run_kernel_case(args):
         else:
             q, kv, b = (int(x) for x in name.replace("q", "").replace("kv", "").replace("b", "").split("_"))
             c = make_case(b, q, [kv] * b, pool_factor=1.0, seed=0)
+        hint = 0 if args.no_length_hints else min(c["lens"])  # both bounds, as the bench line passes them
         for _ in range(5):
             sqa.small_q_attention(c["query"], c["key_cache"], c["value_cache"], c["block_tables"], c["seq_lens"],
-                                  16, max(c["lens"]), kernel=args.kernel)
+                                  16, max(c["lens"]), kernel=args.kernel, min_seq_len=hint)
     torch.cuda.synchronize()
     print(json.dumps({"kernel_case": name, "ok": True}), flush=True)
 
