@@ -216,7 +216,7 @@ __device__ __forceinline__ int even_split_pages(int pages, int parts, bool whole
 // result.  Lengths are read once; block 0 raises the same status bits as
 // compute_schedule.
 template <bool kSpec>
-__device__ __forceinline__ Schedule cluster_schedule(const SplitKvParams& p) {
+__device__ __forceinline__ Schedule even_schedule(const SplitKvParams& p) {
   const int lane = threadIdx.x & 31;
   const int C = p.cluster > 1 ? p.cluster : p.seg_split;
   const int seg = (int)blockIdx.x / C;
@@ -261,7 +261,7 @@ __device__ __forceinline__ Schedule cluster_schedule(const SplitKvParams& p) {
 
 // Warp 0: the schedule into shared memory, before the CTA-wide barrier.
 __device__ __forceinline__ void build_schedule(const SplitKvParams& p, Schedule* sch) {
-  const Schedule s = (p.cluster || p.seg_split) ? cluster_schedule<false>(p) : compute_schedule<false>(p);
+  const Schedule s = (p.cluster || p.seg_split) ? even_schedule<false>(p) : compute_schedule<false>(p);
   if ((threadIdx.x & 31) == 0) *sch = s;
 }
 
@@ -353,7 +353,7 @@ template <bool F8>
 __device__ __forceinline__ void prefetch_start(const SplitKvParams& p, const CUtensorMap* tm_k,
                                                const CUtensorMap* tm_v, int budget) {
   const int lane = threadIdx.x & 31;
-  const Schedule s = (p.cluster || p.seg_split) ? cluster_schedule<true>(p) : compute_schedule<true>(p);
+  const Schedule s = (p.cluster || p.seg_split) ? even_schedule<true>(p) : compute_schedule<true>(p);
   if (s.start >= s.end) return;
   int b = s.b0;
   int pages = s.pages_b0;
