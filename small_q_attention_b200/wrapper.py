@@ -55,12 +55,19 @@ class PagedMTPAttention:
              max_seq_len: int = 0, *, page_size: int = PAGE_SIZE, head_dim: int = HEAD_DIM,
              num_ctas: int = 0, min_pages_per_cta: int = 0, kv_layout: str = "NHD",
              sm_scale: float | None = None, out_scale: float = 1.0,
-             cache_dtype: torch.dtype | None = None) -> "PagedMTPAttention":
+             cache_dtype: torch.dtype | None = None, min_seq_len: int = 0,
+             cluster: int = 0) -> "PagedMTPAttention":
         """Fix the shapes of the following ``run`` calls and size the workspace.
 
         ``max_seq_len`` bounds ``seq_lens`` for the launch size (0: the page-table
         width); a ``run`` with longer sequences than planned is clamped to the
-        table like ``small_q_attention``.
+        table like ``small_q_attention``.  ``min_seq_len`` (a lower bound of the
+        runs' ``seq_lens``, 0 = unknown) and ``cluster`` steer the launch as in
+        ``small_q_attention``: with both bounds within 15% of each other, batches
+        of few sequences run the tcgen05 kernel in thread-block clusters or with
+        every segment split evenly over several CTAs (``selected_kernel`` reports
+        ``2 + 100 * C`` or ``2 + 10000 * k``); a run whose lengths fall outside the
+        bounds still gives the right result.
         """
         if not (1 <= q_len <= MAX_Q_LEN):
             raise ValueError(f"q_len must be in [1, {MAX_Q_LEN}]")
@@ -68,11 +75,14 @@ class PagedMTPAttention:
             raise ValueError("the kernel supports head_dim 128 and page_size 16")
         if batch < 0 or num_kv_heads <= 0 or num_pages <= 0 or max_pages <= 0 or max_seq_len < 0:
             raise ValueError("invalid plan shape")
+        if min_seq_len < 0 or cluster not in (0, 1, 2, 4, 8, 16):
+            raise ValueError("min_seq_len must be >= 0 and cluster one of 0, 1, 2, 4, 8, 16")
         a = _native.SqaArgs()
         a.batch, a.q_len, a.num_q_heads, a.head_dim = batch, q_len, GQA_GROUP * num_kv_heads, head_dim
         a.num_kv_heads, a.page_size, a.num_pages, a.max_pages = num_kv_heads, page_size, num_pages, max_pages
         a.max_seq_len, a.num_ctas, a.min_pages_per_cta, a.kernel = max_seq_len, num_ctas, min_pages_per_cta, self._kernel
         a.kv_layout = _layout_code(kv_layout)
+        a.min_seq_len, a.cluster = min_seq_len, cluster
         if cache_dtype is not None and cache_dtype == getattr(torch, "float8_e4m3fn", None):
             a.kv_dtype = _native.KV_FP8_E4M3  # fp8 caches run on the tcgen05 kernel
         lib = _native.library()
@@ -87,6 +97,7 @@ class PagedMTPAttention:
         self._shape = (batch, q_len, num_kv_heads, num_pages, max_pages)
         self._max_seq_len, self._num_ctas, self._min_pages = max_seq_len, num_ctas, min_pages_per_cta
         self._kv_layout, self._sm_scale, self._out_scale = kv_layout, sm_scale, out_scale
+        self._min_seq_len, self._cluster = min_seq_len, cluster
         self.selected_kernel = int(picked)
         return self
 
@@ -125,6 +136,7 @@ class PagedMTPAttention:
         a = _fill_args(query, key_cache, value_cache, block_tables, seq_lens, None, self._max_seq_len,
                        self._num_ctas, self._min_pages, self._kernel, self._kv_layout, self._sm_scale,
                        self._out_scale)
+        a.min_seq_len, a.cluster = self._min_seq_len, self._cluster
         a.out = out.data_ptr()
         ws = self._workspace
         with _on_device(self.device):

@@ -87,3 +87,34 @@ def test_shape_checks(sqa):
         attn.run(c["query"], c["key_cache"], c["value_cache"], c["block_tables"], c["seq_lens"])
     with pytest.raises(ValueError):
         attn.plan(2, 17, 8, 10, 10)
+
+
+@pytest.mark.parametrize("q_len,lens,expect", [(4, [8192], "split"), (4, [1024] * 4, "cluster")],
+                         ids=["aligned-split", "cluster"])
+def test_plan_with_length_bounds(sqa, q_len, lens, expect):
+    """Both bounds given to plan(): the batch-1 call gets the segment-aligned split and
+    the short near-uniform batch the cluster mode, as small_q_attention gives them; run
+    matches the oracle eagerly and replayed from a CUDA graph."""
+    c = case(q_len, lens, seed=21)
+    q = c["query"]
+    attn = sqa.PagedMTPAttention(q.device).plan(
+        q.shape[0], q.shape[1], c["key_cache"].shape[2], c["key_cache"].shape[0], c["block_tables"].shape[1],
+        max(lens), min_seq_len=min(lens))
+    sel = attn.selected_kernel
+    assert sel >= 10000 if expect == "split" else 100 < sel < 10000, sel
+    assert sel == sqa.selected_kernel(q, c["key_cache"], c["value_cache"], c["block_tables"], c["seq_lens"], 16,
+                                      max(lens), min_seq_len=min(lens))
+    ref = oracle(c)
+    out = torch.empty_like(q)
+    attn.run(q, c["key_cache"], c["value_cache"], c["block_tables"], c["seq_lens"], out=out, check=True)
+    assert_close(out, ref)
+    out.zero_()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=torch.cuda.Stream()):
+        attn.run(q, c["key_cache"], c["value_cache"], c["block_tables"], c["seq_lens"], out=out)
+    g.replay()
+    torch.cuda.synchronize()
+    assert_close(out, ref)
+    with pytest.raises(ValueError):
+        attn.plan(1, 4, 8, 64, 8, 128, min_seq_len=-1)
