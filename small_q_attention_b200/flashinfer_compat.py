@@ -208,8 +208,12 @@ class BatchDecodeWithPagedKVCacheWrapper:
             table, lens = block_tables.to(torch.int32).contiguous(), seq_lens.to(torch.int32).contiguous()
         else:
             table, lens = csr_to_block_table(indptr, indices, last_page_len, page_size)
+        # both length bounds, read once here as FlashInfer's plan reads its host-side layout:
+        # they steer the launch (cluster mode or the segment-aligned split for near-uniform
+        # batches of few requests), never the result
         self._plan = dict(table=table, lens=lens, q_len=q_len, hq=num_qo_heads, hkv=num_kv_heads,
                           q_dtype=q_dt, kv_dtype=kv_dt, max_seq_len=int(lens.max()) if lens.numel() else 0,
+                          min_seq_len=int(lens.min()) if lens.numel() else 0,
                           sm_scale=float(sm_scale) if sm_scale is not None else 128 ** -0.5)
 
     begin_forward = plan
@@ -247,7 +251,7 @@ class BatchDecodeWithPagedKVCacheWrapper:
             out4 = out.view(q4.shape)
         res = small_q_attention(q4, k_cache, v_cache, p["table"], p["lens"], 16, p["max_seq_len"], out=out4,
                                 workspace=self._workspace, kv_layout=self._kv_layout, sm_scale=scale,
-                                out_scale=out_scale)
+                                out_scale=out_scale, min_seq_len=p["min_seq_len"])
         return res.view(q.shape)
 
     forward = run
