@@ -147,8 +147,9 @@ typedef struct sqa_args {
    * gives the right result, only a slower launch. */
   int32_t min_seq_len;
   /* Cluster mode: 0 = auto (above), 1 = off (segments cut into cost-balanced
-   * CTA ranges, merged by a second kernel), 2 / 4 / 8 / 16 = that many CTAs per
-   * segment (tcgen05 kernel; 16-CTA clusters where the device allows them).
+   * CTA ranges, or with both length hints split evenly over k CTAs, merged by a
+   * second kernel), 2 / 4 / 8 / 16 = that many CTAs per segment in one cluster
+   * (tcgen05 kernel; 16-CTA clusters where the device allows them).
    * No upstream counterpart (the upstream splits with chunk_keys, ext.cu:1178). */
   int32_t cluster;
 } sqa_args;
